@@ -1,0 +1,446 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 decode hot path.
+
+Workload: long-context split-KV decode attention over a Qwen3-32B-shaped layer
+stack -- 64 layers, 64 query / 8 KV heads, head_dim 128, bf16, batch 4,
+131072 cached tokens per sequence in 64-token pages, KV sharded by sequence
+over the N GPUs (one process per GPU).  One step = one decode step of the
+stack: for every layer, append the new token's K/V (on the rank holding the
+sequence tail), run paged decode attention over the rank's shard, and --
+for N > 1 -- all-gather the per-head (m, l, o) records over NCCL and merge
+them.  Synthetic data (seeded normal K/V, random page placement); the KV
+working set (137 GB / N) is far larger than L2, so no flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl helm|reference]
+
+Rank 0 prints one JSON line.  `--impl reference` times the reference's own
+CPU attention algorithm (oracle/cpu_baseline.py) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+METRIC = "paged decode-attn HBM GB/s (% of peak); decode tok/s at 1/2/4/8 B200"
+CFG = dict(layers=64, batch=4, q_heads=64, kv_heads=8, head_dim=128, page=64, ctx=131072)
+WORKLOAD = ("config5: Qwen3-32B-shaped attention stack, 64 layers, 64q/8kv heads, d128, bf16, "
+            "batch 4, 131072-token paged KV (64-token pages), KV sequence-sharded")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------
+# nvidia-smi clock sampler (runs during the timed region)
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_selector(dev, local):
+    """nvidia-smi -i argument for this process's GPU (its UUID when torch exposes it)."""
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        return vis.split(",")[local] if vis else str(local)
+
+
+# ----------------------------------------------------------------------------
+# distributed helpers
+# ----------------------------------------------------------------------------
+def dist_setup(n):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}: launch with torchrun --nproc-per-node {n}")
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, local, world
+
+
+def init_pg(world, local, backend="nccl"):
+    import datetime
+    import torch.distributed as dist
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local) if backend == "nccl" else None)
+    return dist
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------------
+# reference arm: the reference's CPU algorithm on the host cores
+# ----------------------------------------------------------------------------
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import time_decode_attention
+    c = CFG
+    warm = min(args.warmup, 1)
+    calls = max(1, min(args.steps, 3))
+    t, n, threads = time_decode_attention(c["q_heads"], c["kv_heads"], c["head_dim"], c["page"], c["ctx"],
+                                          torch.bfloat16, path=2, min_seconds=0.0 if warm == 0 else 5.0,
+                                          max_calls=calls)
+    step_s = t * c["layers"] * c["batch"]
+    tok_s = c["batch"] / step_s
+    sample = (f"reference all-CPU path (kv_cache.py:376-380, ported op-for-op) on 1 of {c['layers']} layers x "
+              f"1 of {c['batch']} sequences at {c['ctx']} tokens, median of {n} calls, x{c['layers'] * c['batch']}")
+    line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": n, "warmup": warm, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "parallelism": "host cores", "global_batch": c["batch"],
+                       "seq_len": c["ctx"]},
+            "cpu_baseline": {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tok_s, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# helm arm
+# ----------------------------------------------------------------------------
+class Stack:
+    """Device state of the sharded attention stack on one rank."""
+
+    def __init__(self, rank, world, dev, spare_pages):
+        from helm_b200 import ops
+        self.ops = ops
+        c = CFG
+        self.rank, self.world, self.dev = rank, world, dev
+        self.L, self.B, self.Hq, self.Hkv, self.D, self.P = (c["layers"], c["batch"], c["q_heads"], c["kv_heads"],
+                                                             c["head_dim"], c["page"])
+        assert c["ctx"] % (world * self.P) == 0
+        self.local_ctx = c["ctx"] // world
+        self.npg = self.local_ctx // self.P
+        self.tail = rank == world - 1
+        self.spare = spare_pages if self.tail else 0
+        width = self.npg + self.spare
+        n_pool = self.L * self.B * width
+        self.n_pool = n_pool
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        # pool [pages, K/V, Hkv, P, D]
+        self.pool = torch.empty((n_pool, 2, self.Hkv, self.P, self.D), dtype=torch.bfloat16, device=dev)
+        chunk = 2048
+        for i in range(0, n_pool, chunk):
+            self.pool[i:i + chunk].normal_(generator=g)
+        perm = torch.randperm(n_pool, device=dev, generator=g).to(torch.int32).reshape(self.L, self.B, width)
+        self.page_table = perm[:, :, :].clone()
+        self.spare_ids = perm[:, :, self.npg:].contiguous()
+        self.page_used = torch.full((self.L, self.B, width), self.P, dtype=torch.int32, device=dev)
+        self.page_used[:, :, self.npg:] = 0
+        self.num_pages = torch.full((self.L, self.B), self.npg, dtype=torch.int32, device=dev)
+        self.spare_next = torch.zeros((self.L, self.B), dtype=torch.int32, device=dev)
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.q = torch.randn((self.L, self.B, self.Hq, self.D), generator=g, device=dev).to(torch.bfloat16)
+        self.k_new = torch.randn((self.L, self.B, self.Hkv, self.D), generator=g, device=dev).to(torch.bfloat16)
+        self.v_new = torch.randn((self.L, self.B, self.Hkv, self.D), generator=g, device=dev).to(torch.bfloat16)
+        self.out = torch.empty((self.L, self.B, self.Hq, self.D), dtype=torch.bfloat16, device=dev)
+        rows = self.B * self.Hq
+        self.rec = torch.empty((self.L, rows, self.D + 2), dtype=torch.float32, device=dev)
+        self.gathered = torch.empty((self.L, world, rows, self.D + 2), dtype=torch.float32, device=dev)
+        self.k_base = self.pool[:, 0]
+        self.v_base = self.pool[:, 1]
+        self.page_stride = 2 * self.Hkv * self.P * self.D
+        self.head_stride = self.P * self.D
+        self._build_params()
+
+    def _build_params(self):
+        ops = self.ops
+        from helm_b200 import _native as N
+        self.lib = N.lib()
+        self.attn_params, self.append_params = [], []
+        ws_need = 0
+        for l in range(self.L):
+            p = ops.make_attn_params(
+                self.q[l], self.k_base, self.v_base, self.page_table[l], self.page_used[l], self.num_pages[l],
+                num_kv_heads=self.Hkv, page_size=self.P, page_stride=self.page_stride,
+                head_stride=self.head_stride, num_pool_pages=self.n_pool,
+                max_pages=self.page_table.shape[-1], out=self.out[l] if self.world == 1 else None,
+                out_record=self.rec[l] if self.world > 1 else None, error_flag=self.error_flag)
+            S = ctypes.c_int32(0)
+            need = self.lib.helm_paged_attn_workspace_bytes(ctypes.byref(p), ctypes.byref(S))
+            p.num_splits = S.value
+            ws_need = max(ws_need, need)
+            self.attn_params.append(p)
+            if self.tail:
+                a = ops.make_append_params(
+                    self.k_new[l], self.v_new[l], self.k_base, self.v_base, page_stride=self.page_stride,
+                    head_stride=self.head_stride, num_pool_pages=self.n_pool, page_size=self.P,
+                    page_table=self.page_table[l], page_used=self.page_used[l], num_pages=self.num_pages[l],
+                    spare_pages=self.spare_ids[l], spare_next=self.spare_next[l], error_flag=self.error_flag)
+                self.append_params.append(a)
+        self.splits = self.attn_params[0].num_splits
+        self.ws = torch.empty(max(ws_need // 4, 1), dtype=torch.float32, device=self.dev)
+        for p in self.attn_params:
+            p.workspace = self.ws.data_ptr()
+            p.workspace_bytes = self.ws.numel() * 4
+        # launches per step of our own kernels
+        per_layer = (1 if self.tail else 0) + 1 + (1 if self.splits > 1 else 0) + (1 if self.world > 1 else 0)
+        self.launches_per_step = self.L * per_layer
+
+    def attn_bytes(self, tokens_per_seq):
+        """Algorithmic bytes of one attention launch: K+V of every cached token read once per
+        (sequence, kv head) plus q in and the output out."""
+        kv = 2 * self.Hkv * self.D * 2 * tokens_per_seq * self.B
+        qo = self.B * self.Hq * self.D * (2 + (2 if self.world == 1 else 4))
+        return kv + qo
+
+    def step(self, stream, ev_pairs=None):
+        import torch.distributed as dist
+        from helm_b200 import _native as N
+        sp = stream.cuda_stream
+        for l in range(self.L):
+            if self.tail:
+                N.check("helm_kv_append", self.lib.helm_kv_append(ctypes.byref(self.append_params[l]), sp))
+            if ev_pairs is not None:
+                ev_pairs[l][0].record(stream)
+            N.check("helm_paged_attn_decode", self.lib.helm_paged_attn_decode(ctypes.byref(self.attn_params[l]), sp))
+            if ev_pairs is not None:
+                ev_pairs[l][1].record(stream)
+            if self.world > 1:
+                dist.all_gather_into_tensor(self.gathered[l], self.rec[l])
+                self.ops.lse_merge(self.gathered[l], out=self.out[l].view(self.B * self.Hq, self.D))
+
+
+def run_helm(args, rank, local, world):
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = init_pg(world, local)
+    c = CFG
+    total_steps = args.warmup + args.steps + (args.e2e_steps if args.e2e_steps is not None else args.steps) + 4
+    spare = (total_steps + c["page"] - 1) // c["page"] + 1
+    st = Stack(rank, world, dev, spare)
+    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        st.step(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+
+    # ---------------- device-timed region ----------------
+    ev_pairs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+                 for _ in range(st.L)] for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(gpu_selector(dev, local))
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    t0.record(stream)
+    for s in range(args.steps):
+        st.step(stream, ev_pairs[s])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    barrier(world)
+    ms = t0.elapsed_time(t1)
+    ms_max = max_over_ranks(ms, world, dev)
+    ms_step = ms_max / args.steps
+    attn_ms = [p[0].elapsed_time(p[1]) for step in ev_pairs for p in step]
+    attn_avg_ms = sum(attn_ms) / len(attn_ms)
+    err = int(st.error_flag.item())
+
+    # ---------------- end-to-end through the public op API ----------------
+    e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
+    e2e = run_e2e(st, stream, e2e_steps, world, dev)
+
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        tokens_per_seq = st.local_ctx + args.warmup + args.steps // 2
+        bytes_launch = st.attn_bytes(tokens_per_seq)
+        achieved = bytes_launch / (attn_avg_ms * 1e-3) / 1e9
+        step_bytes_all = bytes_launch * st.L * world
+        tok_s = c["batch"] / (ms_step * 1e-3)
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline()
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": c["batch"], "seq_len": c["ctx"],
+                       "layers": c["layers"], "parallelism": f"kv-seq-shard{world}",
+                       "l2": "inputs larger than L2 (KV %.1f GB per GPU)" % (st.pool.numel() * 2 / 1e9),
+                       "num_splits": st.splits},
+            "hbm_gbs": step_bytes_all / (ms_step * 1e-3) / 1e9 / world,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "attn_tc_kernel + lse_merge_kernel (one helm_paged_attn_decode call)",
+                         "bytes_per_launch": bytes_launch, "avg_launch_ms": attn_avg_ms},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": st.launches_per_step * args.steps,
+            "clocks": clk,
+            "device_error_flag": err,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(st, stream, steps, world, dev):
+    """The same decode steps through the public op API with the step's inputs (q, new K/V of
+    every layer) copied from pinned host memory and the outputs read back every step."""
+    from helm_b200 import ops
+    import torch.distributed as dist
+    L, B = st.L, st.B
+    q_h = st.q.cpu().pin_memory()
+    k_h = st.k_new.cpu().pin_memory()
+    v_h = st.v_new.cpu().pin_memory()
+    out_h = torch.empty(st.out.shape, dtype=st.out.dtype).pin_memory()
+    q_d = torch.empty_like(st.q)
+    k_d = torch.empty_like(st.k_new)
+    v_d = torch.empty_like(st.v_new)
+    h2d = q_h.numel() * 2 + (k_h.numel() * 2 * 2 if st.tail else 0)
+    d2h = out_h.numel() * 2
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        q_d.copy_(q_h, non_blocking=True)
+        if st.tail:
+            k_d.copy_(k_h, non_blocking=True)
+            v_d.copy_(v_h, non_blocking=True)
+        for l in range(L):
+            if st.tail:
+                ops.kv_append(k_d[l], v_d[l], st.k_base, st.v_base, page_stride=st.page_stride,
+                              head_stride=st.head_stride, num_pool_pages=st.n_pool, page_size=st.P,
+                              page_table=st.page_table[l], page_used=st.page_used[l], num_pages=st.num_pages[l],
+                              spare_pages=st.spare_ids[l], spare_next=st.spare_next[l], error_flag=st.error_flag)
+            if world == 1:
+                ops.paged_decode_attention(q_d[l], st.k_base, st.v_base, st.page_table[l], st.page_used[l],
+                                           st.num_pages[l], num_kv_heads=st.Hkv, page_size=st.P,
+                                           page_stride=st.page_stride, head_stride=st.head_stride,
+                                           num_pool_pages=st.n_pool, out=st.out[l], workspace=st.ws)
+            else:
+                ops.paged_decode_attention(q_d[l], st.k_base, st.v_base, st.page_table[l], st.page_used[l],
+                                           st.num_pages[l], num_kv_heads=st.Hkv, page_size=st.P,
+                                           page_stride=st.page_stride, head_stride=st.head_stride,
+                                           num_pool_pages=st.n_pool, out_record=st.rec[l], workspace=st.ws)
+                dist.all_gather_into_tensor(st.gathered[l], st.rec[l])
+                ops.lse_merge(st.gathered[l], out=st.out[l].view(B * st.Hq, st.D))
+        out_h.copy_(st.out, non_blocking=True)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(t0.elapsed_time(t1), world, dev) / steps
+    return {"value": CFG["batch"] / (ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "api": "helm_b200.ops (C ABI per layer)"}
+
+
+def cpu_baseline():
+    from oracle.cpu_baseline import time_decode_attention
+    c = CFG
+    t, n, threads = time_decode_attention(c["q_heads"], c["kv_heads"], c["head_dim"], c["page"], c["ctx"],
+                                          torch.bfloat16, path=2, min_seconds=8.0, max_calls=3)
+    step_s = t * c["layers"] * c["batch"]
+    return {"value": c["batch"] / step_s, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": (f"reference all-CPU attention path (kv_cache.py:376-380, torch CPU, ported) on 1 layer x "
+                       f"1 sequence at {c['ctx']} tokens, median of {n} calls ({t * 1e3:.0f} ms), "
+                       f"extrapolated x{c['layers'] * c['batch']} to one decode step")}
+
+
+def main():
+    args = parse()
+    rank, local, world = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_helm(args, rank, local, world)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,877 @@
+// Paged decode attention with split-KV partials and a log-sum-exp merge.
+//
+// Semantics follow HELM's perform_streaming_attention
+// (helm/runtime/kv_cache.py:318-442): one query token per sequence, K/V read
+// page by page, online softmax with fp32 running max / sum / output, pages
+// with zero used tokens skipped, GQA by q head -> kv head hq / (Hq/Hkv),
+// output o / clamp(l, 1e-12) cast to the output dtype.
+//
+// Two kernels compute the same partial records:
+//   * attn_generic_kernel: CUDA cores, any page size / head dim <= 256 /
+//     dtype (fp32, fp16, bf16).  Used for fp32 pages and odd shapes.
+//   * attn_tc_kernel: bf16/fp16 pages of 64 tokens x 128 dims.  A producer
+//     warp streams each page's K and V tiles with TMA (cp.async.bulk.tensor,
+//     128B swizzle) into a 3-stage shared-memory ring guarded by mbarriers;
+//     four consumer warps each own 16 tokens of a page and compute
+//     S^T = K Q^T and O^T += V^T P^T with m16n8k16 tensor-core MMAs (the GQA
+//     group is the N=8 dimension), keeping the online softmax in registers
+//     with warp-shuffle max/sum reductions.  P is fed to the PV product as a
+//     hi+lo pair of 16-bit values so the weights keep ~16 mantissa bits.
+#include "common.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace helm {
+
+struct AttnArgs {
+  const void *q;
+  const void *k_base;
+  const void *v_base;
+  int64_t page_stride;
+  int64_t head_stride;
+  int32_t num_pool_pages;
+  const int32_t *page_table;
+  const int32_t *page_used;
+  const int32_t *num_pages;
+  int32_t pt_stride;
+  int32_t B, Hq, Hkv, D, P, gq;
+  int32_t q_dtype, out_dtype;
+  float scale_log2;      // softmax scale * log2(e)
+  int32_t num_splits;
+  float *rec;            // split records [S][B*Hq][D+2] (null: none)
+  float *out_record;     // merged record when S == 1 (null: none)
+  void *out;             // normalised output when S == 1 (null: none)
+  int32_t *error_flag;
+};
+
+// Page range [lo, hi) of split s for a sequence of n pages: balanced integer
+// division, so every split gets floor(n/S) or ceil(n/S) pages.
+__device__ __forceinline__ void split_range(int n, int s, int S, int &lo, int &hi) {
+  lo = (int)(((int64_t)n * s) / S);
+  hi = (int)(((int64_t)n * (s + 1)) / S);
+}
+
+__device__ __forceinline__ int read_num_pages(const AttnArgs &a, int b) {
+  int n = a.num_pages[b];
+  if (n < 0 || n > a.pt_stride) {
+    flag_error(a.error_flag, HELM_DEVERR_NUM_PAGES);
+    n = n < 0 ? 0 : a.pt_stride;
+  }
+  return n;
+}
+
+// Writes the CTA's result for query head hq, dim d: the unnormalised record
+// (split or merged) and/or the normalised output.
+__device__ __forceinline__ void emit(const AttnArgs &a, int split, int b, int hq, int d,
+                                     float m, float l, float o) {
+  const int rows = a.B * a.Hq;
+  const int row = b * a.Hq + hq;
+  const int rl = a.D + 2;
+  if (a.rec) {
+    float *r = a.rec + ((int64_t)split * rows + row) * rl;
+    r[d] = o;
+    if (d == 0) { r[a.D] = m; r[a.D + 1] = l; }
+  }
+  if (a.out_record) {
+    float *r = a.out_record + (int64_t)row * rl;
+    r[d] = o;
+    if (d == 0) { r[a.D] = m; r[a.D + 1] = l; }
+  }
+  if (a.out) {
+    float v = l > 0.f ? o / l : 0.f;
+    store_f(a.out, a.out_dtype, (int64_t)row * a.D + d, v);
+  }
+}
+
+// ===========================================================================
+// Generic CUDA-core kernel.
+// grid (S, Hkv, B), 128 threads.  Warp w handles pages lo+w, lo+w+4, ...;
+// inside a page, lane t owns token t0+t for the scores and dim lane+32i for
+// the P.V accumulation.  Per-warp (m, l, o) live in shared memory and are
+// merged across warps at the end.
+// ===========================================================================
+constexpr int kGenWarps = 4;
+constexpr int kGenHeadChunk = 8;
+constexpr int kGenMaxDPL = 8;  // dims per lane: D <= 256
+
+template <typename KT>
+__global__ void __launch_bounds__(128) attn_generic_kernel(AttnArgs a) {
+  extern __shared__ float smem_g[];
+  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = a.gq, D = a.D;
+
+  float *q_s = smem_g;                                  // [gq][D]
+  float *o_s = q_s + gq * D;                            // [4][gq][D]
+  float *p_s = o_s + kGenWarps * gq * D;                // [4][32][gq]
+  float *m_s = p_s + kGenWarps * 32 * gq;               // [4][gq]
+  float *l_s = m_s + kGenWarps * gq;                    // [4][gq]
+  float *al_s = l_s + kGenWarps * gq;                   // [4][gq]
+
+  for (int i = threadIdx.x; i < gq * D; i += blockDim.x) {
+    int h = i / D, d = i - h * D;
+    q_s[i] = load_f(a.q, a.q_dtype, ((int64_t)(b * a.Hq + g * gq + h)) * D + d);
+  }
+  for (int i = threadIdx.x; i < kGenWarps * gq * D; i += blockDim.x) o_s[i] = 0.f;
+  for (int i = threadIdx.x; i < kGenWarps * gq; i += blockDim.x) {
+    m_s[i] = -INFINITY;
+    l_s[i] = 0.f;
+  }
+  __syncthreads();
+
+  const int n = read_num_pages(a, b);
+  int lo, hi;
+  split_range(n, s, a.num_splits, lo, hi);
+  const KT *kb = reinterpret_cast<const KT *>(a.k_base);
+  const KT *vb = reinterpret_cast<const KT *>(a.v_base);
+  float *o_w = o_s + warp * gq * D;
+  float *p_w = p_s + warp * 32 * gq;
+  float *m_w = m_s + warp * gq;
+  float *l_w = l_s + warp * gq;
+  float *al_w = al_s + warp * gq;
+  const int dpl = (D + 31) / 32;
+
+  for (int pi = lo + warp; pi < hi; pi += kGenWarps) {
+    const int pid = a.page_table[(int64_t)b * a.pt_stride + pi];
+    const int used = a.page_used[(int64_t)b * a.pt_stride + pi];
+    if (pid < 0 || pid >= a.num_pool_pages) {
+      flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
+      continue;
+    }
+    if (used < 0 || used > a.P) {
+      flag_error(a.error_flag, HELM_DEVERR_PAGE_USED);
+      continue;
+    }
+    const KT *kp = kb + (int64_t)pid * a.page_stride + (int64_t)g * a.head_stride;
+    const KT *vp = vb + (int64_t)pid * a.page_stride + (int64_t)g * a.head_stride;
+    for (int t0 = 0; t0 < used; t0 += 32) {
+      const int t = t0 + lane;
+      const bool valid = t < used;
+      const int nt = min(32, used - t0);
+      for (int h0 = 0; h0 < gq; h0 += kGenHeadChunk) {
+        const int hc = min(kGenHeadChunk, gq - h0);
+        float sc[kGenHeadChunk];
+#pragma unroll
+        for (int j = 0; j < kGenHeadChunk; ++j) sc[j] = 0.f;
+        if (valid) {
+          const KT *kr = kp + (int64_t)t * D;
+          for (int d = 0; d < D; ++d) {
+            const float kv = Elem<KT>::to_f(kr[d]);
+#pragma unroll
+            for (int j = 0; j < kGenHeadChunk; ++j)
+              if (j < hc) sc[j] = fmaf(q_s[(h0 + j) * D + d], kv, sc[j]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kGenHeadChunk; ++j) {
+          if (j >= hc) break;
+          float v = valid ? sc[j] * a.scale_log2 : -INFINITY;
+          float mx = v;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+          const float m_old = m_w[h0 + j];
+          const float m_new = fmaxf(m_old, mx);
+          const float alpha = rescale_weight(m_old, m_new);
+          const float p = valid ? fast_exp2(v - m_new) : 0.f;
+          float ps = p;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+          p_w[lane * gq + h0 + j] = p;
+          __syncwarp();
+          if (lane == 0) {
+            l_w[h0 + j] = l_w[h0 + j] * alpha + ps;
+            m_w[h0 + j] = m_new;
+            al_w[h0 + j] = alpha;
+          }
+          __syncwarp();
+        }
+        // o[h][d] = o[h][d] * alpha[h] + sum_t p[t][h] * v[t][d]
+        float acc[kGenHeadChunk][kGenMaxDPL];
+#pragma unroll
+        for (int j = 0; j < kGenHeadChunk; ++j)
+#pragma unroll
+          for (int i = 0; i < kGenMaxDPL; ++i) {
+            const int d = lane + 32 * i;
+            acc[j][i] = (j < hc && i < dpl && d < D) ? o_w[(h0 + j) * D + d] * al_w[h0 + j] : 0.f;
+          }
+        for (int tt = 0; tt < nt; ++tt) {
+          const KT *vr = vp + (int64_t)(t0 + tt) * D;
+          float vv[kGenMaxDPL];
+#pragma unroll
+          for (int i = 0; i < kGenMaxDPL; ++i) {
+            const int d = lane + 32 * i;
+            vv[i] = (i < dpl && d < D) ? Elem<KT>::to_f(vr[d]) : 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < kGenHeadChunk; ++j) {
+            if (j >= hc) break;
+            const float p = p_w[tt * gq + h0 + j];
+#pragma unroll
+            for (int i = 0; i < kGenMaxDPL; ++i) acc[j][i] = fmaf(p, vv[i], acc[j][i]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kGenHeadChunk; ++j)
+#pragma unroll
+          for (int i = 0; i < kGenMaxDPL; ++i) {
+            const int d = lane + 32 * i;
+            if (j < hc && i < dpl && d < D) o_w[(h0 + j) * D + d] = acc[j][i];
+          }
+        __syncwarp();
+      }
+    }
+  }
+  __syncthreads();
+
+  // Merge the four warps' partial states.
+  for (int i = threadIdx.x; i < gq * D; i += blockDim.x) {
+    const int h = i / D, d = i - h * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kGenWarps; ++w) M = fmaxf(M, m_s[w * gq + h]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGenWarps; ++w) {
+      const float wt = rescale_weight(m_s[w * gq + h], M);
+      L = fmaf(l_s[w * gq + h], wt, L);
+      O = fmaf(o_s[(w * gq + h) * D + d], wt, O);
+    }
+    if (M == -INFINITY) { L = 0.f; O = 0.f; }
+    emit(a, s, b, g * gq + h, d, M, L, O);
+  }
+}
+
+// ===========================================================================
+// TMA + tensor-core kernel (bf16 / fp16 pages, P = 64, D = 128).
+// ===========================================================================
+namespace tc {
+
+constexpr int P = 64;
+constexpr int D = 128;
+constexpr int kStages = 3;
+constexpr int kHalfBytes = P * 128;            // 64 rows x 128 B (64 dims)
+constexpr int kTileBytes = 2 * kHalfBytes;     // one K or V tile: 16 KB
+constexpr int kStageBytes = 2 * kTileBytes;    // K + V: 32 KB
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
+constexpr uint32_t kWaitLimit = 1u << 24;       // bounded mbarrier polls ...
+constexpr uint64_t kWaitNs = 2000000000ull;      // ... and at most 2 s per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Spins until the phase with `parity` completes; gives up (returns false)
+// after kWaitLimit polls or kWaitNs nanoseconds, whichever comes first.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  for (int i = 0; i < 64; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && global_ns() - t0 > kWaitNs) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y,
+                                            int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                          uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+template <typename T> struct Mma;
+template <> struct Mma<__nv_bfloat16> {
+  __device__ __forceinline__ static void run(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+  // Packs (x, y) and their rounding residuals as bf16x2.
+  __device__ __forceinline__ static void split(float x, float y, uint32_t &hi, uint32_t &lo) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    float2 hf = __bfloat1622float2(h);
+    __nv_bfloat162 l = __floats2bfloat162_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<uint32_t *>(&h);
+    lo = *reinterpret_cast<uint32_t *>(&l);
+  }
+};
+template <> struct Mma<__half> {
+  __device__ __forceinline__ static void run(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+  __device__ __forceinline__ static void split(float x, float y, uint32_t &hi, uint32_t &lo) {
+    __half2 h = __floats2half2_rn(x, y);
+    float2 hf = __half22float2(h);
+    __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<uint32_t *>(&h);
+    lo = *reinterpret_cast<uint32_t *>(&l);
+  }
+};
+
+// Byte offset of 16-byte chunk `chunk` (0..15, i.e. dims 8*chunk..8*chunk+7)
+// of row `row` inside one tile stored as two 64-dim halves with the TMA
+// 128-byte swizzle (chunk index XOR row % 8 within each 128-byte row).
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+  const int half = chunk >> 3, c = chunk & 7;
+  return half * kHalfBytes + row * 128 + ((c ^ (row & 7)) << 4);
+}
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kStages];
+  __shared__ __align__(8) uint64_t empty_bar[kStages];
+  __shared__ int stage_used[kStages];
+  __shared__ float m_x[kConsumerWarps][NT * 8];
+  __shared__ float l_x[kConsumerWarps][NT * 8];
+
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = a.gq;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], kConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  const int n = read_num_pages(a, b);
+  int lo, hi;
+  split_range(n, s, a.num_splits, lo, hi);
+  const int npages = hi - lo;
+  const int32_t *pt = a.page_table + (int64_t)b * a.pt_stride;
+  const int32_t *pu = a.page_used + (int64_t)b * a.pt_stride;
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < npages && ok; ++i) {
+        const int st = i % kStages;
+        if (i >= kStages && !mbar_wait(&empty_bar[st], ((i / kStages) - 1) & 1)) {
+          flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        const int pid = pt[lo + i];
+        int used = pu[lo + i];
+        if (pid < 0 || pid >= a.num_pool_pages) {
+          flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
+          used = 0;
+        } else if (used < 0 || used > P) {
+          flag_error(a.error_flag, HELM_DEVERR_PAGE_USED);
+          used = 0;
+        }
+        stage_used[st] = used;
+        if (used > 0) {
+          uint8_t *kd = smem + st * kStageBytes;
+          uint8_t *vd = kd + kTileBytes;
+          mbar_arrive_expect_tx(&full_bar[st], kStageBytes);
+          tma_load_4d(kd, &tmK, &full_bar[st], 0, 0, g, pid);
+          tma_load_4d(kd + kHalfBytes, &tmK, &full_bar[st], 64, 0, g, pid);
+          tma_load_4d(vd, &tmV, &full_bar[st], 0, 0, g, pid);
+          tma_load_4d(vd + kHalfBytes, &tmV, &full_bar[st], 64, 0, g, pid);
+        } else {
+          mbar_arrive(&full_bar[st]);
+        }
+        issued = i + 1;
+      }
+      // Before the CTA can exit, every copy it issued must have landed.
+      const int first = issued > kStages ? issued - kStages : 0;
+      for (int i = first; i < issued; ++i)
+        if (!mbar_wait(&full_bar[i % kStages], (i / kStages) & 1)) flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+    }
+    return;
+  }
+
+  // ------------------------------ consumers -------------------------------
+  const int r = lane >> 2, c = lane & 3;
+  uint32_t qf[NT][8][2];
+  {
+    const T *qp = reinterpret_cast<const T *>(a.q) + ((int64_t)b * a.Hq + (int64_t)g * gq) * D;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int h = nt * 8 + r;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (h < gq) {
+          qf[nt][j][0] = *reinterpret_cast<const uint32_t *>(qp + h * D + 16 * j + 2 * c);
+          qf[nt][j][1] = *reinterpret_cast<const uint32_t *>(qp + h * D + 16 * j + 2 * c + 8);
+        } else {
+          qf[nt][j][0] = 0u;
+          qf[nt][j][1] = 0u;
+        }
+      }
+    }
+  }
+  float o[NT][8][4];
+  float m_run[NT][2], l_run[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[nt][dt][e] = 0.f;
+    m_run[nt][0] = m_run[nt][1] = -INFINITY;
+    l_run[nt][0] = l_run[nt][1] = 0.f;
+  }
+
+  const int row0 = warp * 16;  // this warp's 16 tokens of every page
+  const int mi = lane >> 3, ri = lane & 7;
+  bool alive = true;
+  for (int i = 0; i < npages && alive; ++i) {
+    const int st = i % kStages;
+    if (!mbar_wait(&full_bar[st], (i / kStages) & 1)) {
+      flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+      alive = false;
+      break;
+    }
+    const int used = stage_used[st];
+    const int nvalid = min(16, used - row0);
+    if (nvalid > 0) {
+      uint8_t *kt = smem + st * kStageBytes;
+      uint8_t *vt = kt + kTileBytes;
+      if (nvalid < 16) {
+        // Rows past `used` hold stale data (possibly NaN bit patterns): zero
+        // this warp's invalid V rows so that 0-weight x V stays 0.
+        for (int idx = lane; idx < (16 - nvalid) * 16; idx += 32) {
+          const int rr = row0 + nvalid + idx / 16;
+          const int q16 = idx % 16;
+          *reinterpret_cast<uint4 *>(vt + (q16 >> 3) * kHalfBytes + rr * 128 + (q16 & 7) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncwarp();
+      }
+      const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
+      // S^T[16 tok x 8 heads] = K[16 x 128] * Q^T[128 x 8]
+      float sc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t a0, a1, a2, a3;
+        const int row = row0 + ri + (mi & 1) * 8;
+        ldsm_x4(kbase + tile_off(row, 2 * j + (mi >> 1)), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) Mma<T>::run(sc[nt], a0, a1, a2, a3, qf[nt][j][0], qf[nt][j][1]);
+      }
+      const bool v_lo = r < nvalid, v_hi = r + 8 < nvalid;
+      uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float x0 = v_lo ? sc[nt][0] * a.scale_log2 : -INFINITY;
+        const float x1 = v_lo ? sc[nt][1] * a.scale_log2 : -INFINITY;
+        const float x2 = v_hi ? sc[nt][2] * a.scale_log2 : -INFINITY;
+        const float x3 = v_hi ? sc[nt][3] * a.scale_log2 : -INFINITY;
+        float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+          t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+        }
+        const float mn0 = fmaxf(m_run[nt][0], t0), mn1 = fmaxf(m_run[nt][1], t1);
+        const float al0 = rescale_weight(m_run[nt][0], mn0), al1 = rescale_weight(m_run[nt][1], mn1);
+        m_run[nt][0] = mn0;
+        m_run[nt][1] = mn1;
+        const float p0 = v_lo ? fast_exp2(x0 - mn0) : 0.f;
+        const float p1 = v_lo ? fast_exp2(x1 - mn1) : 0.f;
+        const float p2 = v_hi ? fast_exp2(x2 - mn0) : 0.f;
+        const float p3 = v_hi ? fast_exp2(x3 - mn1) : 0.f;
+        l_run[nt][0] = fmaf(l_run[nt][0], al0, p0 + p2);
+        l_run[nt][1] = fmaf(l_run[nt][1], al1, p1 + p3);
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) {
+          o[nt][dt][0] *= al0;
+          o[nt][dt][1] *= al1;
+          o[nt][dt][2] *= al0;
+          o[nt][dt][3] *= al1;
+        }
+        uint32_t h01, l01, h23, l23;
+        Mma<T>::split(p0, p1, h01, l01);
+        Mma<T>::split(p2, p3, h23, l23);
+        bh[nt][0] = movm_t(h01);
+        bh[nt][1] = movm_t(h23);
+        bl[nt][0] = movm_t(l01);
+        bl[nt][1] = movm_t(l23);
+      }
+      // O^T[128 dims x 8 heads] += V^T[128 x 16 tok] * P^T[16 tok x 8 heads]
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) {
+        uint32_t a0, a1, a2, a3;
+        const int row = row0 + ri + (mi >> 1) * 8;
+        ldsm_x4_t(vbase + tile_off(row, 2 * dt + (mi & 1)), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          Mma<T>::run(o[nt][dt], a0, a1, a2, a3, bh[nt][0], bh[nt][1]);
+          Mma<T>::run(o[nt][dt], a0, a1, a2, a3, bl[nt][0], bl[nt][1]);
+        }
+      }
+      if (nvalid < 16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+  }
+
+  // l is a per-thread partial over this thread's rows: sum the 8 lanes that
+  // share the same head pair.
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float v = l_run[nt][e];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      l_run[nt][e] = v;
+    }
+
+  // All consumer warps must be done with the stage buffers before they are
+  // reused as merge scratch.
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  float *o_x = reinterpret_cast<float *>(smem);  // [4][NT*8][128]
+  constexpr int HN = NT * 8;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int h0 = nt * 8 + 2 * c;
+    if (r == 0) {
+      m_x[warp][h0] = m_run[nt][0];
+      m_x[warp][h0 + 1] = m_run[nt][1];
+      l_x[warp][h0] = l_run[nt][0];
+      l_x[warp][h0 + 1] = l_run[nt][1];
+    }
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      const int d = dt * 16 + r;
+      o_x[(warp * HN + h0) * D + d] = o[nt][dt][0];
+      o_x[(warp * HN + h0 + 1) * D + d] = o[nt][dt][1];
+      o_x[(warp * HN + h0) * D + d + 8] = o[nt][dt][2];
+      o_x[(warp * HN + h0 + 1) * D + d + 8] = o[nt][dt][3];
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  for (int idx = threadIdx.x; idx < gq * D; idx += kConsumerWarps * 32) {
+    const int h = idx / D, d = idx - h * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, m_x[w][h]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) {
+      const float wt = rescale_weight(m_x[w][h], M);
+      L = fmaf(l_x[w][h], wt, L);
+      O = fmaf(o_x[(w * HN + h) * D + d], wt, O);
+    }
+    if (M == -INFINITY) { L = 0.f; O = 0.f; }
+    emit(a, s, b, g * gq + h, d, M, L, O);
+  }
+}
+
+}  // namespace tc
+
+// ===========================================================================
+// Log-sum-exp merge: one CTA per row (query head of a sequence).
+// ===========================================================================
+__global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict__ parts, int S, int64_t pstride,
+                                                       int rows, int D, void *out, int out_dtype,
+                                                       float *out_record) {
+  const int row = blockIdx.x;
+  const int rl = D + 2;
+  const float *base = parts + (int64_t)row * rl;
+  float M = -INFINITY;
+  for (int s = 0; s < S; ++s) M = fmaxf(M, base[s * pstride + D]);
+  float L = 0.f;
+  for (int s = 0; s < S; ++s) {
+    const float *p = base + s * pstride;
+    L = fmaf(p[D + 1], rescale_weight(p[D], M), L);
+  }
+  if (M == -INFINITY) L = 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float O = 0.f;
+    if (M != -INFINITY)
+      for (int s = 0; s < S; ++s) {
+        const float *p = base + s * pstride;
+        O = fmaf(p[d], rescale_weight(p[D], M), O);
+      }
+    if (out) store_f(out, out_dtype, (int64_t)row * D + d, L > 0.f ? O / L : 0.f);
+    if (out_record) {
+      float *rr = out_record + (int64_t)row * rl;
+      rr[d] = O;
+      if (d == 0) { rr[D] = M; rr[D + 1] = L; }
+    }
+  }
+}
+
+// ===========================================================================
+// Host side.
+// ===========================================================================
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 4-D map over the pool: (dim, token, kv head, page), box 64 x 64 x 1 x 1,
+// 128-byte swizzle.
+bool make_pool_map(CUtensorMap *m, const void *base, int kv_dtype, const helm_paged_attn_params *p) {
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  const int es = dtype_size(kv_dtype);
+  cuuint64_t gdim[4] = {(cuuint64_t)p->D, (cuuint64_t)p->P, (cuuint64_t)p->Hkv, (cuuint64_t)p->num_pool_pages};
+  cuuint64_t gstr[3] = {(cuuint64_t)p->D * es, (cuuint64_t)p->head_stride * es, (cuuint64_t)p->page_stride * es};
+  cuuint32_t box[4] = {64, 64, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, kv_dtype == HELM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                   const_cast<void *>(base), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool tc_eligible(const helm_paged_attn_params *p) {
+  if (!(p->kv_dtype == HELM_BF16 || p->kv_dtype == HELM_F16)) return false;
+  if (p->q_dtype != p->kv_dtype) return false;
+  if (p->D != tc::D || p->P != tc::P) return false;
+  const int gq = p->Hq / p->Hkv;
+  if (gq > 16) return false;
+  if ((reinterpret_cast<uintptr_t>(p->k_base) & 15) || (reinterpret_cast<uintptr_t>(p->v_base) & 15)) return false;
+  if ((reinterpret_cast<uintptr_t>(p->q) & 3)) return false;
+  if ((p->page_stride % 8) || (p->head_stride % 8)) return false;
+  if (p->num_pool_pages < 1) return false;
+  if (getenv("HELM_B200_FORCE_GENERIC")) return false;
+  return true;
+}
+
+int resolve_splits(const helm_paged_attn_params *p) {
+  if (p->num_splits > 0) return p->num_splits;
+  const int pairs = p->B * p->Hkv;
+  const int maxp = p->max_pages;
+  if (maxp <= 1 || pairs <= 0) return 1;
+  const int slots = num_sms() * 2;  // two resident CTAs per SM
+  for (int waves = 4; waves >= 1; --waves) {
+    int S = (waves * slots) / pairs;
+    if (S < 1) continue;
+    if (maxp / S >= 8 || (waves == 1 && S > 1)) return S > maxp ? maxp : S;
+  }
+  // Few (sequence, kv head) pairs and short sequences: still fill the GPU.
+  int S = (slots + pairs - 1) / pairs;
+  if (S > maxp) S = maxp;
+  return S < 1 ? 1 : S;
+}
+
+int validate(const helm_paged_attn_params *p) {
+  if (!p) return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: params is null");
+  if (p->B < 0 || p->Hq < 0 || p->Hkv <= 0 || p->D <= 0 || p->P <= 0)
+    return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: bad sizes B=%d Hq=%d Hkv=%d D=%d P=%d", p->B, p->Hq,
+                p->Hkv, p->D, p->P);
+  if (p->Hq % p->Hkv != 0)
+    return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: Hq=%d not a multiple of Hkv=%d", p->Hq, p->Hkv);
+  if (p->D > 256) return fail(HELM_ERR_UNSUPPORTED, "paged_attn: head dim %d > 256", p->D);
+  for (int dt : {p->q_dtype, p->kv_dtype, p->out_dtype})
+    if (dt != HELM_F32 && dt != HELM_F16 && dt != HELM_BF16)
+      return fail(HELM_ERR_UNSUPPORTED, "paged_attn: dtype %d not supported", dt);
+  if (p->B > 0 && p->Hq > 0) {
+    if (!p->q || !p->k_base || !p->v_base || !p->page_table || !p->page_used || !p->num_pages)
+      return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: null input pointer");
+    if (!p->out && !p->out_record) return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: no output requested");
+  }
+  if (p->page_stride < 0 || p->head_stride < 0 || p->page_table_stride < 0 || p->max_pages < 0 ||
+      p->num_pool_pages < 0)
+    return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: negative stride or count");
+  if (p->max_pages > p->page_table_stride)
+    return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: max_pages %d > page_table_stride %d", p->max_pages,
+                p->page_table_stride);
+  if (p->num_splits < 0) return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: negative num_splits");
+  return HELM_OK;
+}
+
+size_t generic_smem_bytes(int gq, int D) {
+  return sizeof(float) * ((size_t)gq * D * (1 + kGenWarps) + (size_t)kGenWarps * 32 * gq + 3 * kGenWarps * gq);
+}
+
+template <typename KT>
+int launch_generic(const AttnArgs &a, cudaStream_t st) {
+  const size_t smem = generic_smem_bytes(a.gq, a.D);
+  if (smem > 200 * 1024) return fail(HELM_ERR_UNSUPPORTED, "paged_attn: gq*D too large for the generic kernel");
+  cudaFuncSetAttribute(attn_generic_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(a.num_splits, a.Hkv, a.B);
+  attn_generic_kernel<KT><<<grid, 128, smem, st>>>(a);
+  return check_launch("attn_generic_kernel");
+}
+
+template <typename T, int NT>
+int launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const AttnArgs &a, cudaStream_t st) {
+  cudaFuncSetAttribute(tc::attn_tc_kernel<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes);
+  dim3 grid(a.num_splits, a.Hkv, a.B);
+  tc::attn_tc_kernel<T, NT><<<grid, tc::kThreads, tc::kSmemBytes, st>>>(mk, mv, a);
+  return check_launch("attn_tc_kernel");
+}
+
+}  // namespace
+}  // namespace helm
+
+using namespace helm;
+
+extern "C" int64_t helm_paged_attn_workspace_bytes(const helm_paged_attn_params *p, int32_t *num_splits_out) {
+  if (validate(p) != HELM_OK) return -1;
+  const int S = resolve_splits(p);
+  if (num_splits_out) *num_splits_out = S;
+  if (S <= 1) return 0;
+  return (int64_t)S * p->B * p->Hq * (p->D + 2) * (int64_t)sizeof(float);
+}
+
+extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *stream) {
+  int rc = validate(p);
+  if (rc != HELM_OK) return rc;
+  if (p->B == 0 || p->Hq == 0) return HELM_OK;
+  cudaStream_t st = as_stream(stream);
+  const int S = resolve_splits(p);
+  const int rows = p->B * p->Hq;
+  const int64_t need = S > 1 ? (int64_t)S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
+  if (need > 0 && (!p->workspace || p->workspace_bytes < need))
+    return fail(HELM_ERR_WORKSPACE, "paged_attn: workspace %lld bytes < %lld needed for %d splits",
+                (long long)p->workspace_bytes, (long long)need, S);
+
+  AttnArgs a{};
+  a.q = p->q;
+  a.k_base = p->k_base;
+  a.v_base = p->v_base;
+  a.page_stride = p->page_stride;
+  a.head_stride = p->head_stride;
+  a.num_pool_pages = p->num_pool_pages;
+  a.page_table = p->page_table;
+  a.page_used = p->page_used;
+  a.num_pages = p->num_pages;
+  a.pt_stride = p->page_table_stride;
+  a.B = p->B;
+  a.Hq = p->Hq;
+  a.Hkv = p->Hkv;
+  a.D = p->D;
+  a.P = p->P;
+  a.gq = p->Hq / p->Hkv;
+  a.q_dtype = p->q_dtype;
+  a.out_dtype = p->out_dtype;
+  a.scale_log2 = p->scale * kLog2e;
+  a.num_splits = S;
+  a.error_flag = p->error_flag;
+  if (S > 1) {
+    a.rec = p->workspace;
+  } else {
+    a.out = p->out;
+    a.out_record = p->out_record;
+  }
+
+  if (tc_eligible(p)) {
+    CUtensorMap mk, mv;
+    if (!make_pool_map(&mk, p->k_base, p->kv_dtype, p) || !make_pool_map(&mv, p->v_base, p->kv_dtype, p))
+      return fail(HELM_ERR_CUDA, "paged_attn: cuTensorMapEncodeTiled failed");
+    const bool two = a.gq > 8;
+    if (p->kv_dtype == HELM_BF16)
+      rc = two ? launch_tc<__nv_bfloat16, 2>(mk, mv, a, st) : launch_tc<__nv_bfloat16, 1>(mk, mv, a, st);
+    else
+      rc = two ? launch_tc<__half, 2>(mk, mv, a, st) : launch_tc<__half, 1>(mk, mv, a, st);
+  } else {
+    switch (p->kv_dtype) {
+      case HELM_F32: rc = launch_generic<float>(a, st); break;
+      case HELM_F16: rc = launch_generic<__half>(a, st); break;
+      default: rc = launch_generic<__nv_bfloat16>(a, st); break;
+    }
+  }
+  if (rc != HELM_OK || S == 1) return rc;
+  lse_merge_kernel<<<rows, 128, 0, st>>>(p->workspace, S, (int64_t)rows * (p->D + 2), rows, p->D, p->out,
+                                         p->out_dtype, p->out_record);
+  return check_launch("lse_merge_kernel");
+}
+
+extern "C" int helm_lse_merge(const float *partials, int32_t num_partials, int64_t partial_stride, int32_t rows,
+                              int32_t D, void *out, int32_t out_dtype, float *out_record, void *stream) {
+  if (rows < 0 || D <= 0 || num_partials < 1 || partial_stride < (int64_t)rows * (D + 2))
+    return fail(HELM_ERR_INVALID_ARGUMENT, "lse_merge: bad sizes rows=%d D=%d partials=%d stride=%lld", rows, D,
+                num_partials, (long long)partial_stride);
+  if (!partials || (!out && !out_record)) return fail(HELM_ERR_INVALID_ARGUMENT, "lse_merge: null pointer");
+  if (out && out_dtype != HELM_F32 && out_dtype != HELM_F16 && out_dtype != HELM_BF16)
+    return fail(HELM_ERR_UNSUPPORTED, "lse_merge: dtype %d", out_dtype);
+  if (rows == 0) return HELM_OK;
+  lse_merge_kernel<<<rows, 128, 0, as_stream(stream)>>>(partials, num_partials, partial_stride, rows, D, out,
+                                                        out_dtype, out_record);
+  return check_launch("lse_merge_kernel");
+}

@@ -1,0 +1,232 @@
+"""Torch-facing wrappers of the C-ABI kernels (one call = one C-ABI call).
+
+Every function takes CUDA tensors, launches on the current torch stream of
+the tensors' device and raises when the native library is missing or returns
+an error.  Nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+_DT = {torch.float32: N.F32, torch.float16: N.F16, torch.bfloat16: N.BF16, torch.int8: N.I8}
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise TypeError(f"helm_b200: unsupported dtype {dt}") from None
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need_cuda(name: str, *ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise ValueError(f"helm_b200.{name}: tensors must be on a CUDA device (got {t.device}); "
+                             "this path has no CPU implementation")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"helm_b200.{name}: tensors on different devices {dev} and {t.device}")
+    if dev is None:
+        raise ValueError(f"helm_b200.{name}: no tensor given")
+    return dev
+
+
+class _Workspace:
+    """Per-device scratch buffer for split-KV records, grown on demand."""
+
+    def __init__(self):
+        self.bufs: dict = {}
+
+    def get(self, dev: torch.device, nbytes: int) -> torch.Tensor:
+        key = (dev.type, dev.index)
+        buf = self.bufs.get(key)
+        if buf is None or buf.numel() * 4 < nbytes:
+            buf = torch.empty((max(nbytes, 1 << 20) + 3) // 4, dtype=torch.float32, device=dev)
+            self.bufs[key] = buf
+        return buf
+
+
+WORKSPACE = _Workspace()
+
+
+def make_attn_params(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tensor, page_table: torch.Tensor,
+                     page_used: torch.Tensor, num_pages: torch.Tensor, *, num_kv_heads: int, page_size: int,
+                     page_stride: int, head_stride: int, num_pool_pages: int, scale: Optional[float] = None,
+                     max_pages: Optional[int] = None, num_splits: int = 0, out: Optional[torch.Tensor] = None,
+                     out_record: Optional[torch.Tensor] = None,
+                     error_flag: Optional[torch.Tensor] = None) -> N.PagedAttnParams:
+    B, Hq, D = q.shape
+    p = N.PagedAttnParams()
+    p.q = q.data_ptr()
+    p.k_base = k_base.data_ptr()
+    p.v_base = v_base.data_ptr()
+    p.page_stride = int(page_stride)
+    p.head_stride = int(head_stride)
+    p.num_pool_pages = int(num_pool_pages)
+    p.page_table = page_table.data_ptr()
+    p.page_used = page_used.data_ptr()
+    p.num_pages = num_pages.data_ptr()
+    p.page_table_stride = page_table.stride(0) if page_table.dim() == 2 else page_table.shape[-1]
+    p.max_pages = int(page_table.shape[-1] if max_pages is None else max_pages)
+    p.B, p.Hq, p.Hkv, p.D, p.P = B, Hq, int(num_kv_heads), D, int(page_size)
+    p.q_dtype = dtype_code(q.dtype)
+    p.kv_dtype = dtype_code(k_base.dtype)
+    p.out_dtype = dtype_code(out.dtype) if out is not None else N.F32
+    p.scale = float(1.0 / math.sqrt(D) if scale is None else scale)
+    p.num_splits = int(num_splits)
+    p.out = _ptr(out)
+    p.out_record = _ptr(out_record)
+    p.error_flag = _ptr(error_flag)
+    return p
+
+
+def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tensor, page_table: torch.Tensor,
+                           page_used: torch.Tensor, num_pages: torch.Tensor, *, num_kv_heads: int,
+                           page_size: int, page_stride: int, head_stride: int, num_pool_pages: int,
+                           scale: Optional[float] = None, max_pages: Optional[int] = None, num_splits: int = 0,
+                           out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                           out_record: Optional[torch.Tensor] = None,
+                           error_flag: Optional[torch.Tensor] = None,
+                           workspace: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """Single-query attention of q [B, Hq, D] over paged K/V (see helm_paged_attn_decode).
+
+    ``page_table``/``page_used`` are int32 [B, max_pages] and ``num_pages``
+    int32 [B], all on q's device.  Returns ``out`` [B, Hq, D] (allocated in
+    ``out_dtype``, default q.dtype, unless given), or None when only
+    ``out_record`` is requested.
+    """
+    dev = _need_cuda("paged_decode_attention", q, k_base, v_base, page_table, page_used, num_pages)
+    if not q.is_contiguous() or q.dim() != 3:
+        raise ValueError("paged_decode_attention: q must be a contiguous [B, Hq, D] tensor")
+    for name, t in (("page_table", page_table), ("page_used", page_used), ("num_pages", num_pages)):
+        if t.dtype != torch.int32:
+            raise TypeError(f"paged_decode_attention: {name} must be int32")
+        if t.stride(-1) != 1:
+            raise ValueError(f"paged_decode_attention: {name} must have unit inner stride")
+    if page_used.stride(0) != page_table.stride(0) if page_table.dim() == 2 else False:
+        raise ValueError("paged_decode_attention: page_used must share page_table's row stride")
+    if out is None and out_record is None:
+        out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=dev)
+    p = make_attn_params(q, k_base, v_base, page_table, page_used, num_pages, num_kv_heads=num_kv_heads,
+                         page_size=page_size, page_stride=page_stride, head_stride=head_stride,
+                         num_pool_pages=num_pool_pages, scale=scale, max_pages=max_pages, num_splits=num_splits,
+                         out=out, out_record=out_record, error_flag=error_flag)
+    lib = N.lib()
+    S = ctypes.c_int32(0)
+    need = lib.helm_paged_attn_workspace_bytes(ctypes.byref(p), ctypes.byref(S))
+    if need < 0:
+        N.check("helm_paged_attn_workspace_bytes", N.ERR_INVALID_ARGUMENT)
+    p.num_splits = S.value
+    if need > 0:
+        ws = workspace if workspace is not None and workspace.numel() * 4 >= need else WORKSPACE.get(dev, need)
+        p.workspace = ws.data_ptr()
+        p.workspace_bytes = ws.numel() * ws.element_size()
+    N.check("helm_paged_attn_decode", lib.helm_paged_attn_decode(ctypes.byref(p), _stream(dev)))
+    return out
+
+
+def lse_merge(partials: torch.Tensor, out: Optional[torch.Tensor] = None, out_dtype=torch.float32,
+              out_record: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """Merges records [S, rows, D+2] (o..., m, l) into out [rows, D] and/or a merged record."""
+    dev = _need_cuda("lse_merge", partials)
+    if partials.dtype != torch.float32 or partials.dim() != 3 or not partials.is_contiguous():
+        raise ValueError("lse_merge: partials must be contiguous float32 [S, rows, D+2]")
+    S, rows, rl = partials.shape
+    D = rl - 2
+    if out is None and out_record is None:
+        out = torch.empty((rows, D), dtype=out_dtype, device=dev)
+    code = N.lib().helm_lse_merge(partials.data_ptr(), S, rows * rl, rows, D, _ptr(out),
+                                  dtype_code(out.dtype) if out is not None else N.F32, _ptr(out_record),
+                                  _stream(dev))
+    N.check("helm_lse_merge", code)
+    return out
+
+
+def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+                bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = (x @ weight.T) * scale + bias with int8 ``weight`` [N, K] and per-row ``scale`` [N]."""
+    dev = _need_cuda("int8_linear", x, weight, scale, bias)
+    if weight.dtype != torch.int8 or weight.dim() != 2 or not weight.is_contiguous():
+        raise ValueError("int8_linear: weight must be a contiguous int8 [N, K] tensor")
+    Nn, K = weight.shape
+    if x.shape[-1] != K:
+        raise ValueError(f"int8_linear: input last dim ({x.shape[-1]}) != weight K ({K})")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if scale.shape != (Nn,) or not scale.is_contiguous():
+        raise ValueError("int8_linear: scale must be a contiguous [N] tensor")
+    if bias is not None:
+        if bias.dtype != x.dtype:
+            bias = bias.to(x.dtype)
+        bias = bias.contiguous()
+    y = out if out is not None else torch.empty((M, Nn), dtype=x.dtype, device=dev)
+    code = N.lib().helm_int8_linear(x2.data_ptr(), dtype_code(x.dtype), weight.data_ptr(), scale.data_ptr(),
+                                    dtype_code(scale.dtype), _ptr(bias), y.data_ptr(), M, Nn, K, _stream(dev))
+    N.check("helm_int8_linear", code)
+    return y.reshape(*lead, Nn)
+
+
+def make_append_params(k_new, v_new, k_base, v_base, *, page_stride, head_stride, num_pool_pages, page_size,
+                       dest=None, page_table=None, page_used=None, num_pages=None, spare_pages=None,
+                       spare_next=None, error_flag=None) -> N.KVAppendParams:
+    B, Hkv, D = k_new.shape
+    p = N.KVAppendParams()
+    p.k_new, p.v_new = k_new.data_ptr(), v_new.data_ptr()
+    p.src_dtype = dtype_code(k_new.dtype)
+    p.k_base, p.v_base = k_base.data_ptr(), v_base.data_ptr()
+    p.page_stride, p.head_stride = int(page_stride), int(head_stride)
+    p.num_pool_pages = int(num_pool_pages)
+    p.kv_dtype = dtype_code(k_base.dtype)
+    p.B, p.Hkv, p.D, p.P = B, Hkv, D, int(page_size)
+    p.dest = _ptr(dest)
+    p.page_table, p.page_used, p.num_pages = _ptr(page_table), _ptr(page_used), _ptr(num_pages)
+    p.page_table_stride = page_table.stride(0) if page_table is not None and page_table.dim() == 2 else 0
+    p.spare_pages, p.spare_next = _ptr(spare_pages), _ptr(spare_next)
+    p.spare_stride = spare_pages.shape[-1] if spare_pages is not None else 0
+    p.error_flag = _ptr(error_flag)
+    return p
+
+
+def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tensor, **kw) -> None:
+    """Writes one token per sequence into the pool (see helm_kv_append)."""
+    dev = _need_cuda("kv_append", k_new, v_new, k_base, v_base)
+    if not (k_new.is_contiguous() and v_new.is_contiguous()) or k_new.dim() != 3 or k_new.shape != v_new.shape:
+        raise ValueError("kv_append: k_new/v_new must be contiguous [B, Hkv, D] tensors of one shape")
+    p = make_append_params(k_new, v_new, k_base, v_base, **kw)
+    N.check("helm_kv_append", N.lib().helm_kv_append(ctypes.byref(p), _stream(dev)))
+
+
+def copy_pages(dst: torch.Tensor, dst_first: int, src: torch.Tensor, src_ids, page_bytes: int,
+               stream: Optional[int] = None) -> int:
+    """Copies pages src[src_ids[i]] -> dst[dst_first + i] (runs merged); returns the copy count."""
+    import numpy as np
+    ids = np.ascontiguousarray(np.asarray(src_ids, dtype=np.int32))
+    dev = dst.device if dst.device.type == "cuda" else src.device
+    st = _stream(dev) if stream is None else stream
+    n = ctypes.c_int32(0)
+    code = N.lib().helm_copy_pages(dst.data_ptr(), int(dst_first), src.data_ptr(),
+                                   ids.ctypes.data_as(ctypes.c_void_p), len(ids), int(page_bytes),
+                                   ctypes.byref(n), st)
+    N.check("helm_copy_pages", code)
+    return n.value

@@ -1,0 +1,211 @@
+/*
+ * helm_b200.h -- C ABI of the B200 decode hot path (paged decode attention,
+ * split-KV log-sum-exp merge, INT8 weight-only linear, KV-slot append).
+ *
+ * Every entry point takes plain pointers, sizes and a cudaStream_t (passed as
+ * void* so that the header needs no CUDA include), never allocates device or
+ * host memory, and returns an int status (HELM_OK == 0).  On a non-zero
+ * status, helm_last_error() returns a thread-local message.  Device-side
+ * index checks never trap: they record a code in the optional int
+ * `error_flag` (device memory) and skip the offending page or row.
+ *
+ * The reference (HELM, Python + one CPU C++ kernel) has no C ABI of its own;
+ * each declaration names the reference interface it replaces (file:line,
+ * paths inside the HELM project).
+ */
+#ifndef HELM_B200_H
+#define HELM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HELM_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------- */
+enum {
+  HELM_OK = 0,
+  HELM_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, bad stride */
+  HELM_ERR_UNSUPPORTED = 2,      /* dtype / shape combination not implemented */
+  HELM_ERR_WORKSPACE = 3,        /* caller's workspace smaller than required */
+  HELM_ERR_CUDA = 4,             /* a CUDA runtime call or launch failed */
+};
+
+/* ---- device-side error flag bits (written with atomicOr) ---------------- */
+enum {
+  HELM_DEVERR_PAGE_ID = 1,     /* page id outside [0, num_pool_pages) */
+  HELM_DEVERR_PAGE_USED = 2,   /* page_used outside [0, page_size] */
+  HELM_DEVERR_NUM_PAGES = 4,   /* num_pages outside [0, page_table_stride] */
+  HELM_DEVERR_TIMEOUT = 8,     /* a bounded mbarrier wait gave up */
+  HELM_DEVERR_APPEND_FULL = 16 /* kv append found no spare page */
+};
+
+/* ---- element types ------------------------------------------------------ */
+typedef enum {
+  HELM_F32 = 0,
+  HELM_F16 = 1,
+  HELM_BF16 = 2,
+  HELM_I8 = 3
+} helm_dtype;
+
+/* Returns HELM_ABI_VERSION of the loaded library. */
+int helm_abi_version(void);
+
+/* Thread-local text of the last non-zero status returned on this thread. */
+const char *helm_last_error(void);
+
+/* ---- paged decode attention -------------------------------------------- */
+/*
+ * Replaces perform_streaming_attention (helm/runtime/kv_cache.py:318-442) and
+ * the decode SDPA calls of _decode_batched (helm/runtime/kv_offload.py:126,160).
+ *
+ * Layout.  One query token per sequence: q is [B, Hq, D] contiguous.  KV
+ * pages live in a pool addressed by int32 page ids.  Element (page p, kv head
+ * h, token t, dim d) of K is at k_base + p*page_stride + h*head_stride + t*D +
+ * d (element units; V likewise from v_base).  The reference page tensor
+ * [1, Hkv, P, D] (helm/runtime/kv_allocator.py:26-28) is exactly one page of
+ * this layout with head_stride = P*D.
+ *
+ * Sequence b attends over pages page_table[b*page_table_stride + i] for
+ * i < num_pages[b], using the first page_used[...] tokens of each page.  A page
+ * with 0 used tokens is skipped (kv_cache.py:350-351); a sequence with no
+ * tokens yields zeros (kv_cache.py:353-354).  Query head hq reads kv head
+ * hq / (Hq/Hkv) (the repeat_interleave mapping of kv_cache.py:356-363).
+ *
+ * Split-KV.  The page list of each (sequence, kv head) is cut into
+ * num_splits contiguous ranges; each range yields one partial record per
+ * query head: float rec[D+2] = { o[0..D-1], m, l }, where m is the running
+ * max of the base-2 logits s*scale*log2(e), l = sum 2^(logit-m) and o the
+ * unnormalised sum of 2^(logit-m) * v.  An empty range has m = -inf, l = 0,
+ * o = 0.  Records are stored [split][B*Hq][D+2] in `workspace`.
+ *
+ * Output.  When `out` is non-null the records are merged (helm_lse_merge
+ * semantics) into out [B, Hq, D] of out_dtype; when `out_record` is non-null
+ * the merged but unnormalised record [B*Hq][D+2] is also written, for a later
+ * cross-GPU merge.  With num_splits == 1 and only `out` requested, no
+ * workspace is touched.
+ */
+typedef struct {
+  const void *q;          /* [B, Hq, D], q_dtype */
+  const void *k_base;     /* pool base of K, kv_dtype */
+  const void *v_base;     /* pool base of V, kv_dtype */
+  int64_t page_stride;    /* elements between consecutive page ids */
+  int64_t head_stride;    /* elements between kv heads inside a page */
+  int32_t num_pool_pages; /* valid page ids: [0, num_pool_pages) */
+  const int32_t *page_table; /* [B, page_table_stride] page ids (device) */
+  const int32_t *page_used;  /* [B, page_table_stride] used tokens (device) */
+  const int32_t *num_pages;  /* [B] listed pages per sequence (device) */
+  int32_t page_table_stride;
+  int32_t max_pages;      /* host-side upper bound of num_pages[b] */
+  int32_t B, Hq, Hkv, D, P;
+  int32_t q_dtype, kv_dtype, out_dtype; /* helm_dtype */
+  float scale;            /* softmax scale; reference default 1/sqrt(D) */
+  int32_t num_splits;     /* >= 1; 0 picks a split count for this GPU */
+  float *workspace;       /* split records, may be null if not needed */
+  int64_t workspace_bytes;
+  void *out;              /* [B, Hq, D] out_dtype, or null */
+  float *out_record;      /* [B*Hq, D+2] merged record, or null */
+  int32_t *error_flag;    /* device int, optional */
+} helm_paged_attn_params;
+
+/* Bytes of workspace helm_paged_attn_decode needs for these params, after
+ * resolving num_splits == 0.  Writes the split count it will use to
+ * *num_splits_out when non-null. */
+int64_t helm_paged_attn_workspace_bytes(const helm_paged_attn_params *p,
+                                        int32_t *num_splits_out);
+
+int helm_paged_attn_decode(const helm_paged_attn_params *p, void *stream);
+
+/* ---- log-sum-exp merge of partial records -------------------------------- */
+/*
+ * No single reference counterpart: it performs, across page ranges (and
+ * across GPUs after an all-gather), the rescale-and-add of the online softmax
+ * at helm/runtime/kv_cache.py:402-410,431-441 and the final
+ * o / clamp(l, 1e-12) of kv_cache.py:441.
+ *
+ * partials: num_partials blocks of `rows` records of D+2 floats, block i at
+ * partials + i*partial_stride (floats).  out [rows, D] of out_dtype (null to
+ * skip); out_record [rows, D+2] receives the merged record (null to skip).
+ */
+int helm_lse_merge(const float *partials, int32_t num_partials,
+                   int64_t partial_stride, int32_t rows, int32_t D,
+                   void *out, int32_t out_dtype, float *out_record,
+                   void *stream);
+
+/* ---- INT8 weight-only linear -------------------------------------------- */
+/*
+ * Replaces helm_fp16_linear (helm/kernels/fp16_gemv.cpp:105-157) and
+ * fp16_linear (helm/kernels/__init__.py:55-88) on the GPU, with INT8 weights:
+ *   y[m, n] = (sum_k x[m, k] * w[n, k]) * w_scale[n] + bias[n]
+ * x [M, K] (F16 or BF16), w [N, K] int8 row-major, w_scale [N] (F16, BF16 or
+ * F32), bias [N] (same dtype as x) or null, y [M, N] of x_dtype.  fp32
+ * accumulation.  Any M >= 1; K must be a multiple of 16.
+ */
+int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
+                     const void *w_scale, int32_t scale_dtype,
+                     const void *bias, void *y, int32_t M, int32_t N,
+                     int32_t K, void *stream);
+
+/* ---- KV append ------------------------------------------------------------ */
+/*
+ * Replaces the slot writes of KVCacheManager.append_decode
+ * (helm/runtime/kv_cache.py:103-110): writes one new token per sequence,
+ * k_new/v_new [B, Hkv, D] (src_dtype, converted to kv_dtype), into the pool.
+ *
+ * Host-directed mode (dest != null): dest is int32 [B, 3] in device memory,
+ * {page id, index of that page in the sequence's page list, token slot}; the
+ * kernel writes the token and, when page_table is non-null, also sets
+ * page_table[b][idx] = page id, page_used[b][idx] = slot+1 and
+ * num_pages[b] = max(num_pages[b], idx+1).
+ *
+ * Device-directed mode (dest == null): the kernel reads the tail page of each
+ * sequence from page_table/page_used/num_pages; when the tail is full it takes
+ * the next id from spare_pages[b*spare_stride + spare_next[b]++] (bounded by
+ * spare_stride, else HELM_DEVERR_APPEND_FULL), so a whole decode loop can run
+ * without a host round trip (and be captured in a CUDA graph).
+ */
+typedef struct {
+  const void *k_new;  /* [B, Hkv, D] */
+  const void *v_new;  /* [B, Hkv, D] */
+  int32_t src_dtype;
+  void *k_base;
+  void *v_base;
+  int64_t page_stride;
+  int64_t head_stride;
+  int32_t num_pool_pages;
+  int32_t kv_dtype;
+  int32_t B, Hkv, D, P;
+  const int32_t *dest;   /* [B, 3] or null */
+  int32_t *page_table;   /* [B, page_table_stride] */
+  int32_t *page_used;
+  int32_t *num_pages;
+  int32_t page_table_stride;
+  const int32_t *spare_pages; /* [B, spare_stride] (device-directed mode) */
+  int32_t *spare_next;        /* [B] */
+  int32_t spare_stride;
+  int32_t *error_flag;
+} helm_kv_append_params;
+
+int helm_kv_append(const helm_kv_append_params *p, void *stream);
+
+/* ---- page gather (host pages -> HBM staging) ------------------------------ */
+/*
+ * Replaces the per-page H2D prefetch of perform_streaming_attention
+ * (helm/runtime/kv_cache.py:412-423): copies `count` pages of page_bytes
+ * bytes each from src_base + src_ids[i]*page_bytes (pinned host or device
+ * memory) to dst_base + (dst_first + i)*page_bytes with cudaMemcpyAsync on
+ * `stream`, merging runs of consecutive ids into one copy.  src_ids is a HOST
+ * array.  Returns the number of cudaMemcpyAsync calls issued in *copies_out.
+ */
+int helm_copy_pages(void *dst_base, int64_t dst_first, const void *src_base,
+                    const int32_t *src_ids, int32_t count, int64_t page_bytes,
+                    int32_t *copies_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HELM_B200_H */

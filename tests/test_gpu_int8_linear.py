@@ -1,0 +1,82 @@
+"""GPU parity of the INT8 weight-only linear (through the C ABI).
+
+Oracles: float64 dequantise-then-matmul (oracle/int8_linear.py) and the
+reference's own AVX2 fp16 GEMV applied to the fp16-dequantised weights
+(tests/golden/fp16_gemv.npz).  Bar: max |y - ref| <= 1e-2 * max |ref|.
+"""
+import pathlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.int8_linear import int8_linear_ref
+
+pytestmark = pytest.mark.gpu
+GOLDEN = pathlib.Path(__file__).resolve().parent / "golden"
+TOL = 1e-2
+
+
+def rel_err(y, ref):
+    y = y.detach().double().cpu().numpy()
+    return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def _inputs(M, N, K, seed, xdtype=torch.float16):
+    rng = np.random.default_rng(seed)
+    w = rng.integers(-127, 128, size=(N, K), dtype=np.int8)
+    s = rng.uniform(0.001, 0.02, size=(N,)).astype(np.float16)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    return w, s, torch.from_numpy(x).to(xdtype)
+
+
+@pytest.mark.parametrize("shape", [(12288, 4096), (4096, 12288), (6144, 4096)])
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_config2_shapes(shape, M, cuda):
+    from helm_b200 import ops
+    N, K = shape
+    w, s, x = _inputs(M, N, K, seed=N + K + M)
+    y = ops.int8_linear(x.to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda))
+    ref = int8_linear_ref(x.double().numpy(), w, s)
+    assert y.shape == (M, N) and y.dtype == torch.float16
+    assert rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 9, 16, 17])
+@pytest.mark.parametrize("xdtype", [torch.float16, torch.bfloat16])
+def test_odd_shapes_bias_bf16(M, xdtype, cuda):
+    from helm_b200 import ops
+    N, K = 333, 528
+    w, s, x = _inputs(M, N, K, seed=M, xdtype=xdtype)
+    bias = torch.randn(N, dtype=torch.float32).to(xdtype)
+    y = ops.int8_linear(x.to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(s).float().to(cuda),
+                        bias=bias.to(cuda))
+    ref = int8_linear_ref(x.double().numpy(), w, s, bias.double().numpy())
+    assert y.dtype == xdtype
+    assert rel_err(y, ref) <= TOL
+
+
+def test_leading_dims_preserved(cuda):
+    from helm_b200 import ops
+    w, s, x = _inputs(6, 64, 256, seed=3)
+    y = ops.int8_linear(x.reshape(2, 3, 256).to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda))
+    assert y.shape == (2, 3, 64)
+
+
+@pytest.mark.parametrize("key", ["256x512", "96x1024"])
+def test_matches_reference_fp16_gemv(key, cuda):
+    """Against the reference AVX2 kernel run on the dequantised weights (fp16 W*s)."""
+    from helm_b200 import ops
+    g = np.load(GOLDEN / "fp16_gemv.npz")
+    w, s, x, y_ref = g[f"{key}/w"], g[f"{key}/s"], g[f"{key}/x"], g[f"{key}/y"]
+    y = ops.int8_linear(torch.from_numpy(x).to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda))
+    assert rel_err(y, y_ref.astype(np.float64)) <= TOL
+
+
+def test_rejects_bad_k(cuda):
+    from helm_b200 import ops
+    from helm_b200._native import HelmError
+    w = torch.zeros(8, 24, dtype=torch.int8, device=cuda)
+    with pytest.raises(HelmError):
+        ops.int8_linear(torch.zeros(1, 24, dtype=torch.float16, device=cuda), w,
+                        torch.ones(8, dtype=torch.float16, device=cuda))
