@@ -875,3 +875,67 @@ extern "C" int helm_lse_merge(const float *partials, int32_t num_partials, int64
                                                         out_dtype, out_record);
   return check_launch("lse_merge_kernel");
 }
+
+// ===========================================================================
+// Allocation-free variant: split records in a file-scope device array.
+// ===========================================================================
+namespace helm {
+namespace {
+
+// Holds the split-KV records of helm_paged_attn_decode_noalloc.  Every GPU that
+// loads this library reserves it (HELM_NOALLOC_SCRATCH_BYTES) until exit.
+static __device__ __align__(256) float g_noalloc_scratch[HELM_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device.  In host code the symbol itself is only a host-side stand-in,
+// so the kernels must be given this address instead.
+int noalloc_scratch(float **out) {
+  static std::mutex mu;
+  static float *addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(HELM_ERR_UNSUPPORTED, "paged_attn_noalloc: device %d >= 64", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(HELM_ERR_CUDA, "paged_attn_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    addr[dev] = static_cast<float *>(p);
+  }
+  *out = addr[dev];
+  return HELM_OK;
+}
+
+}  // namespace
+}  // namespace helm
+
+extern "C" int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, void *stream) {
+  using namespace helm;
+  int rc = validate(p);
+  if (rc != HELM_OK) return rc;
+  if (p->B == 0 || p->Hq == 0) return HELM_OK;
+  const int64_t cap = HELM_NOALLOC_SCRATCH_BYTES;
+  const int64_t per_split = (int64_t)p->B * p->Hq * (p->D + 2) * (int64_t)sizeof(float);
+  int S = resolve_splits(p);
+  if (S > 1 && (int64_t)S * per_split > cap) {
+    if (p->num_splits > 0)
+      return fail(HELM_ERR_WORKSPACE,
+                  "paged_attn_noalloc: %d splits x %lld bytes of records exceed the %lld-byte static scratch; "
+                  "pass fewer splits (at most %lld) or use helm_paged_attn_decode with a workspace",
+                  S, (long long)per_split, (long long)cap, (long long)(cap / per_split));
+    S = (int)(cap / per_split);  // auto mode: as many splits as the scratch holds
+    if (S < 1) S = 1;
+  }
+  helm_paged_attn_params q = *p;
+  q.num_splits = S;
+  q.workspace = nullptr;
+  q.workspace_bytes = 0;
+  if (S > 1) {
+    rc = noalloc_scratch(&q.workspace);
+    if (rc != HELM_OK) return rc;
+    q.workspace_bytes = cap;
+  }
+  return helm_paged_attn_decode(&q, stream);
+}

@@ -119,6 +119,32 @@ int64_t helm_paged_attn_workspace_bytes(const helm_paged_attn_params *p,
 
 int helm_paged_attn_decode(const helm_paged_attn_params *p, void *stream);
 
+/* ---- paged decode attention without any allocation --------------------- */
+/*
+ * No counterpart in the reference: an extra entry point for callers that
+ * cannot allocate device memory themselves -- for example a plugin whose host
+ * application owns the whole device-memory budget, or a foreign-language
+ * caller that has no CUDA allocator to obtain a workspace from.
+ *
+ * Same contract as helm_paged_attn_decode, except that p->workspace and
+ * p->workspace_bytes are ignored: the split-KV records go to a static device
+ * array of HELM_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds
+ * until the process exits.  Nothing is allocated or freed.  With
+ * num_splits == 0 the split count is capped to what the array holds; an
+ * explicit num_splits whose records (num_splits * B*Hq*(D+2)*4 bytes) exceed
+ * it is rejected with HELM_ERR_WORKSPACE.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current) and so should come before any stream capture.  All calls in
+ * the process share the one array per device and it keeps the previous
+ * call's records: calls whose executions overlap on the GPU (different
+ * streams, or several host threads) race on it and must be serialised by the
+ * caller.  The caller still owns q, the pool, the page tables and the output.
+ */
+#define HELM_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, void *stream);
+
 /* ---- log-sum-exp merge of partial records -------------------------------- */
 /*
  * No single reference counterpart: it performs, across page ranges (and
