@@ -44,12 +44,20 @@ WORKLOAD = ("config5: Qwen3-32B-shaped attention stack, 64 layers, 64q/8kv heads
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
-    return ap.parse_args()
+    # Smaller stacks for ncu captures only; the reported workload is config 5 unless these are set.
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--ctx", type=int, default=None)
+    args = ap.parse_args()
+    if args.layers is not None:
+        CFG["layers"] = args.layers
+    if args.ctx is not None:
+        CFG["ctx"] = args.ctx
+    return args
 
 
 def peaks():
@@ -77,7 +85,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
                  "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -86,9 +94,9 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def stop(self):
+    def stop(self, t_from=None, t_to=None):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -99,7 +107,9 @@ class ClockSampler:
         self.t.join(timeout=2)
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ts, ln in self.lines:
+            if (t_from is not None and ts < t_from) or (t_to is not None and ts > t_to):
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -305,6 +315,8 @@ def run_helm(args, rank, local, world):
     stream = torch.cuda.current_stream(dev)
     torch.cuda.synchronize(dev)
 
+    clocks = ClockSampler(gpu_selector(dev, local))
+    clocks.start()
     for _ in range(args.warmup):
         st.step(stream)
     torch.cuda.synchronize(dev)
@@ -314,16 +326,15 @@ def run_helm(args, rank, local, world):
     ev_pairs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
                  for _ in range(st.L)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(gpu_selector(dev, local))
     barrier(world)
     torch.cuda.synchronize(dev)
-    clocks.start()
+    t_load0 = time.time()
     t0.record(stream)
     for s in range(args.steps):
         st.step(stream, ev_pairs[s])
     t1.record(stream)
     torch.cuda.synchronize(dev)
-    clk = clocks.stop()
+    t_load1 = time.time()
     barrier(world)
     ms = t0.elapsed_time(t1)
     ms_max = max_over_ranks(ms, world, dev)
@@ -334,7 +345,10 @@ def run_helm(args, rank, local, world):
 
     # ---------------- end-to-end through the public op API ----------------
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
-    e2e = run_e2e(st, stream, e2e_steps, world, dev)
+    e2e = run_e2e(st, stream, e2e_steps, world, dev) if e2e_steps > 0 else None
+    clk = clocks.stop(t_load0, time.time())
+    clk["window_s"] = round(time.time() - t_load0, 3)
+    clk["timed_region_s"] = round(t_load1 - t_load0, 3)
 
     if rank == 0:
         hbm_peak, peak_kind = peaks()
@@ -350,7 +364,9 @@ def run_helm(args, rank, local, world):
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": c["batch"], "seq_len": c["ctx"],
+            "config": {"workload": WORKLOAD if (c["layers"], c["ctx"]) == (64, 131072) else
+                       f"REDUCED (profiling only): {c['layers']} layers, ctx {c['ctx']}",
+                       "global_batch": c["batch"], "seq_len": c["ctx"],
                        "layers": c["layers"], "parallelism": f"kv-seq-shard{world}",
                        "l2": "inputs larger than L2 (KV %.1f GB per GPU)" % (st.pool.numel() * 2 / 1e9),
                        "num_splits": st.splits},
