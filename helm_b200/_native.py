@@ -55,7 +55,7 @@ class KVAppendParams(ctypes.Structure):
         ("page_stride", _i64), ("head_stride", _i64),
         ("num_pool_pages", _i32), ("kv_dtype", _i32),
         ("B", _i32), ("Hkv", _i32), ("D", _i32), ("P", _i32),
-        ("dest", _p), ("page_table", _p), ("page_used", _p), ("num_pages", _p),
+        ("dest", _p), ("dest_host", _p), ("page_table", _p), ("page_used", _p), ("num_pages", _p),
         ("page_table_stride", _i32),
         ("spare_pages", _p), ("spare_next", _p), ("spare_stride", _i32),
         ("error_flag", _p),

@@ -5,6 +5,8 @@
 
 namespace helm {
 
+constexpr int kHostDestRows = 64;  // host-directed rows carried per launch
+
 struct AppendArgs {
   const void *k_new, *v_new;
   int32_t src_dtype;
@@ -20,21 +22,25 @@ struct AppendArgs {
   int32_t *spare_next;
   int32_t spare_stride;
   int32_t *error_flag;
+  int32_t b0;                          // first sequence of this launch
+  int32_t use_hdest;
+  int32_t hdest[kHostDestRows][3];     // host-directed rows, by value
 };
 
 // One CTA per sequence: thread 0 resolves the destination (page id, slot),
 // then the CTA copies Hkv*D elements of K and of V.
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   __shared__ int s_pid, s_slot;
-  const int b = blockIdx.x;
+  const int b = a.b0 + blockIdx.x;
   if (threadIdx.x == 0) {
     int pid = -1, slot = -1;
     int32_t *pt = a.page_table ? a.page_table + (int64_t)b * a.pt_stride : nullptr;
     int32_t *pu = a.page_used ? a.page_used + (int64_t)b * a.pt_stride : nullptr;
-    if (a.dest) {
-      pid = a.dest[3 * b];
-      const int li = a.dest[3 * b + 1];
-      slot = a.dest[3 * b + 2];
+    if (a.dest || a.use_hdest) {
+      const int32_t *row = a.use_hdest ? a.hdest[blockIdx.x] : a.dest + 3 * b;
+      pid = row[0];
+      const int li = row[1];
+      slot = row[2];
       const bool ok = pid >= 0 && pid < a.num_pool_pages && slot >= 0 && slot < a.P;
       if (!ok) {
         flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
@@ -106,15 +112,48 @@ extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
   if (p->B == 0) return HELM_OK;
   if (!p->k_new || !p->v_new || !p->k_base || !p->v_base)
     return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: null data pointer");
-  if (!p->dest && (!p->page_table || !p->page_used || !p->num_pages || !p->spare_pages || !p->spare_next))
+  const bool directed = p->dest || p->dest_host;
+  if (!directed && (!p->page_table || !p->page_used || !p->num_pages || !p->spare_pages || !p->spare_next))
     return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: device-directed mode needs page table and spare pages");
-  if (p->dest && p->page_table && (!p->page_used || !p->num_pages))
+  if (directed && p->page_table && (!p->page_used || !p->num_pages))
     return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: page_table given without page_used/num_pages");
-  AppendArgs a{p->k_new,       p->v_new,       p->src_dtype,        p->k_base,      p->v_base,
-               p->page_stride, p->head_stride, p->num_pool_pages,   p->kv_dtype,    p->B,
-               p->Hkv,         p->D,           p->P,                p->dest,        p->page_table,
-               p->page_used,   p->num_pages,   p->page_table_stride, p->spare_pages, p->spare_next,
-               p->spare_stride, p->error_flag};
-  kv_append_kernel<<<p->B, 256, 0, as_stream(stream)>>>(a);
-  return check_launch("kv_append_kernel");
+  AppendArgs a{};
+  a.k_new = p->k_new;
+  a.v_new = p->v_new;
+  a.src_dtype = p->src_dtype;
+  a.k_base = p->k_base;
+  a.v_base = p->v_base;
+  a.page_stride = p->page_stride;
+  a.head_stride = p->head_stride;
+  a.num_pool_pages = p->num_pool_pages;
+  a.kv_dtype = p->kv_dtype;
+  a.B = p->B;
+  a.Hkv = p->Hkv;
+  a.D = p->D;
+  a.P = p->P;
+  a.dest = p->dest_host ? nullptr : p->dest;
+  a.page_table = p->page_table;
+  a.page_used = p->page_used;
+  a.num_pages = p->num_pages;
+  a.pt_stride = p->page_table_stride;
+  a.spare_pages = p->spare_pages;
+  a.spare_next = p->spare_next;
+  a.spare_stride = p->spare_stride;
+  a.error_flag = p->error_flag;
+  cudaStream_t st = as_stream(stream);
+  if (!p->dest_host) {
+    kv_append_kernel<<<p->B, 256, 0, st>>>(a);
+    return check_launch("kv_append_kernel");
+  }
+  a.use_hdest = 1;
+  for (int b0 = 0; b0 < p->B; b0 += kHostDestRows) {
+    const int nb = p->B - b0 < kHostDestRows ? p->B - b0 : kHostDestRows;
+    a.b0 = b0;
+    for (int i = 0; i < nb; ++i)
+      for (int j = 0; j < 3; ++j) a.hdest[i][j] = p->dest_host[3 * (b0 + i) + j];
+    kv_append_kernel<<<nb, 256, 0, st>>>(a);
+    int rc = check_launch("kv_append_kernel");
+    if (rc != HELM_OK) return rc;
+  }
+  return HELM_OK;
 }

@@ -121,7 +121,7 @@ def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.
             raise TypeError(f"paged_decode_attention: {name} must be int32")
         if t.stride(-1) != 1:
             raise ValueError(f"paged_decode_attention: {name} must have unit inner stride")
-    if page_used.stride(0) != page_table.stride(0) if page_table.dim() == 2 else False:
+    if page_table.dim() == 2 and page_used.stride(0) != page_table.stride(0):
         raise ValueError("paged_decode_attention: page_used must share page_table's row stride")
     if out is None and out_record is None:
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=dev)
@@ -188,8 +188,10 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
 
 
 def make_append_params(k_new, v_new, k_base, v_base, *, page_stride, head_stride, num_pool_pages, page_size,
-                       dest=None, page_table=None, page_used=None, num_pages=None, spare_pages=None,
-                       spare_next=None, error_flag=None) -> N.KVAppendParams:
+                       dest=None, dest_host=None, page_table=None, page_used=None, num_pages=None,
+                       spare_pages=None, spare_next=None, error_flag=None) -> N.KVAppendParams:
+    """Parameter block of helm_kv_append.  ``dest_host`` is a C-contiguous int32 numpy array [B, 3]
+    (kept alive by the caller until the call returns)."""
     B, Hkv, D = k_new.shape
     p = N.KVAppendParams()
     p.k_new, p.v_new = k_new.data_ptr(), v_new.data_ptr()
@@ -200,6 +202,7 @@ def make_append_params(k_new, v_new, k_base, v_base, *, page_stride, head_stride
     p.kv_dtype = dtype_code(k_base.dtype)
     p.B, p.Hkv, p.D, p.P = B, Hkv, D, int(page_size)
     p.dest = _ptr(dest)
+    p.dest_host = None if dest_host is None else dest_host.ctypes.data
     p.page_table, p.page_used, p.num_pages = _ptr(page_table), _ptr(page_used), _ptr(num_pages)
     p.page_table_stride = page_table.stride(0) if page_table is not None and page_table.dim() == 2 else 0
     p.spare_pages, p.spare_next = _ptr(spare_pages), _ptr(spare_next)

@@ -181,13 +181,15 @@ int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
  * (helm/runtime/kv_cache.py:103-110): writes one new token per sequence,
  * k_new/v_new [B, Hkv, D] (src_dtype, converted to kv_dtype), into the pool.
  *
- * Host-directed mode (dest != null): dest is int32 [B, 3] in device memory,
- * {page id, index of that page in the sequence's page list, token slot}; the
- * kernel writes the token and, when page_table is non-null, also sets
- * page_table[b][idx] = page id, page_used[b][idx] = slot+1 and
+ * Host-directed mode (dest or dest_host non-null): int32 [B, 3] rows
+ * {page id, index of that page in the sequence's page list, token slot}, in
+ * device memory (dest) or in host memory (dest_host, copied into the kernel
+ * parameters at launch, so the caller may reuse it as soon as the call
+ * returns).  The kernel writes the token and, when page_table is non-null,
+ * also sets page_table[b][idx] = page id, page_used[b][idx] = slot+1 and
  * num_pages[b] = max(num_pages[b], idx+1).
  *
- * Device-directed mode (dest == null): the kernel reads the tail page of each
+ * Device-directed mode (both null): the kernel reads the tail page of each
  * sequence from page_table/page_used/num_pages; when the tail is full it takes
  * the next id from spare_pages[b*spare_stride + spare_next[b]++] (bounded by
  * spare_stride, else HELM_DEVERR_APPEND_FULL), so a whole decode loop can run
@@ -204,7 +206,8 @@ typedef struct {
   int32_t num_pool_pages;
   int32_t kv_dtype;
   int32_t B, Hkv, D, P;
-  const int32_t *dest;   /* [B, 3] or null */
+  const int32_t *dest;   /* [B, 3] device array, or null */
+  const int32_t *dest_host; /* [B, 3] host array, or null */
   int32_t *page_table;   /* [B, page_table_stride] */
   int32_t *page_used;
   int32_t *num_pages;

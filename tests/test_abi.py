@@ -1,0 +1,80 @@
+"""The C ABI: the library loads and exports every function include/helm_b200.h declares; the ctypes
+mirrors match the header's structs.  CPU only -- no compute calls."""
+import ctypes
+import pathlib
+import re
+import subprocess
+
+import pytest
+
+from helm_b200 import _native as N
+
+HEADER = pathlib.Path(__file__).resolve().parent.parent / "include" / "helm_b200.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(helm_[a-z_0-9]+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    fns = declared_functions()
+    for name in ("helm_paged_attn_decode", "helm_lse_merge", "helm_int8_linear", "helm_kv_append",
+                 "helm_copy_pages", "helm_paged_attn_workspace_bytes", "helm_abi_version", "helm_last_error"):
+        assert name in fns
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = N.lib()
+    assert lib.helm_abi_version() == N.ABI_VERSION
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", str(N.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (helm_[a-z_0-9]+)", out))
+    assert set(declared_functions()) <= exported
+
+
+def test_every_declared_function_has_a_python_signature_or_is_bound_by_its_test():
+    bound = {s[0] for s in N.SIGNATURES} | {"helm_paged_attn_decode_noalloc"}
+    assert set(declared_functions()) <= bound
+
+
+def _struct_fields(name):
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    m = re.search(r"typedef struct \{([^{}]*)\}\s*" + name + ";", text)
+    body = m.group(1)
+    fields = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        decl = re.sub(r"\s+", " ", decl)
+        typ, names = re.match(r"((?:const )?[a-z_0-9]+ ?\*?)\s*(.*)", decl).groups()
+        for n in names.split(","):
+            n = n.strip().lstrip("*")
+            ptr = "*" in typ or n.startswith("*") or "*" in decl.split(n)[0]
+            fields.append((n, ptr))
+    return fields
+
+
+@pytest.mark.parametrize("cname,pyname", [("helm_paged_attn_params", "PagedAttnParams"),
+                                          ("helm_kv_append_params", "KVAppendParams")])
+def test_ctypes_struct_mirrors_header(cname, pyname):
+    cfields = [f[0] for f in _struct_fields(cname)]
+    pyfields = [f[0] for f in getattr(N, pyname)._fields_]
+    assert cfields == pyfields
+
+
+def test_errors_are_reported_without_a_gpu():
+    """Argument validation runs on the host: a bad call returns a status and a message."""
+    lib = N.lib()
+    p = N.PagedAttnParams()
+    p.B, p.Hq, p.Hkv, p.D, p.P = 1, 3, 2, 128, 64   # Hq not a multiple of Hkv
+    code = lib.helm_paged_attn_decode(ctypes.byref(p), None)
+    assert code == N.ERR_INVALID_ARGUMENT
+    assert b"multiple" in lib.helm_last_error()
+    code = lib.helm_int8_linear(None, N.F16, None, None, N.F16, None, None, 1, 8, 24, None)
+    assert code == N.ERR_UNSUPPORTED
+    with pytest.raises(N.HelmError):
+        N.check("helm_int8_linear", code)
