@@ -287,18 +287,22 @@ class Stack:
         qo = self.B * self.Hq * self.D * (2 + (2 if self.world == 1 else 4))
         return kv + qo
 
-    def step(self, stream, ev_pairs=None):
+    def attend(self, l, stream):
+        """One layer's attention call (the kernel the roofline measures)."""
+        from helm_b200 import _native as N
+        N.check("helm_paged_attn_decode",
+                self.lib.helm_paged_attn_decode(ctypes.byref(self.attn_params[l]), stream.cuda_stream))
+
+    def step(self, stream):
+        """One decode step over all layers: append (tail rank), attention, and for N > 1 the
+        all-gather of the per-head records and their merge."""
         import torch.distributed as dist
         from helm_b200 import _native as N
         sp = stream.cuda_stream
         for l in range(self.L):
             if self.tail:
                 N.check("helm_kv_append", self.lib.helm_kv_append(ctypes.byref(self.append_params[l]), sp))
-            if ev_pairs is not None:
-                ev_pairs[l][0].record(stream)
             N.check("helm_paged_attn_decode", self.lib.helm_paged_attn_decode(ctypes.byref(self.attn_params[l]), sp))
-            if ev_pairs is not None:
-                ev_pairs[l][1].record(stream)
             if self.world > 1:
                 dist.all_gather_into_tensor(self.gathered[l], self.rec[l])
                 self.ops.lse_merge(self.gathered[l], out=self.out[l].view(self.B * self.Hq, self.D))
@@ -309,7 +313,7 @@ def run_helm(args, rank, local, world):
     torch.cuda.set_device(dev)
     dist = init_pg(world, local)
     c = CFG
-    total_steps = args.warmup + args.steps + (args.e2e_steps if args.e2e_steps is not None else args.steps) + 4
+    total_steps = args.warmup + args.steps + (args.e2e_steps if args.e2e_steps is not None else args.steps) + 8
     spare = (total_steps + c["page"] - 1) // c["page"] + 1
     st = Stack(rank, world, dev, spare)
     stream = torch.cuda.current_stream(dev)
@@ -317,21 +321,29 @@ def run_helm(args, rank, local, world):
 
     clocks = ClockSampler(gpu_selector(dev, local))
     clocks.start()
+    # Eager warm-up (also initialises NCCL before graph capture).
     for _ in range(args.warmup):
         st.step(stream)
     torch.cuda.synchronize(dev)
     barrier(world)
 
+    # One decode step (all layers) captured once and replayed: no host work between kernels.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        st.step(torch.cuda.current_stream(dev))
+    torch.cuda.synchronize(dev)
+    graph.replay()  # warm replay (appends one more token, like a warm-up step)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+
     # ---------------- device-timed region ----------------
-    ev_pairs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
-                 for _ in range(st.L)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize(dev)
     t_load0 = time.time()
     t0.record(stream)
     for s in range(args.steps):
-        st.step(stream, ev_pairs[s])
+        graph.replay()
     t1.record(stream)
     torch.cuda.synchronize(dev)
     t_load1 = time.time()
@@ -339,9 +351,22 @@ def run_helm(args, rank, local, world):
     ms = t0.elapsed_time(t1)
     ms_max = max_over_ranks(ms, world, dev)
     ms_step = ms_max / args.steps
-    attn_ms = [p[0].elapsed_time(p[1]) for step in ev_pairs for p in step]
+
+    # Attention-call durations for the roofline: back-to-back calls over every layer, each
+    # bracketed by CUDA events on the launching stream (no other work in between).
+    attn_ms = []
+    for rep in range(2):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(st.L)]
+        for l in range(st.L):
+            evs[l][0].record(stream)
+            st.attend(l, stream)
+            evs[l][1].record(stream)
+        torch.cuda.synchronize(dev)
+        if rep:
+            attn_ms += [a.elapsed_time(b) for a, b in evs]
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
     err = int(st.error_flag.item())
+    del graph
 
     # ---------------- end-to-end through the public op API ----------------
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else args.steps
@@ -352,7 +377,7 @@ def run_helm(args, rank, local, world):
 
     if rank == 0:
         hbm_peak, peak_kind = peaks()
-        tokens_per_seq = st.local_ctx + args.warmup + args.steps // 2
+        tokens_per_seq = st.local_ctx + args.warmup + 1 + args.steps
         bytes_launch = st.attn_bytes(tokens_per_seq)
         achieved = bytes_launch / (attn_avg_ms * 1e-3) / 1e9
         step_bytes_all = bytes_launch * st.L * world
@@ -364,6 +389,7 @@ def run_helm(args, rank, local, world):
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "timing": "CUDA graph of one decode step (all layers) replayed K times; CUDA events, max over ranks",
             "config": {"workload": WORKLOAD if (c["layers"], c["ctx"]) == (64, 131072) else
                        f"REDUCED (profiling only): {c['layers']} layers, ctx {c['ctx']}",
                        "global_batch": c["batch"], "seq_len": c["ctx"],
@@ -373,7 +399,7 @@ def run_helm(args, rank, local, world):
             "hbm_gbs": step_bytes_all / (ms_step * 1e-3) / 1e9 / world,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind,
-                         "kernel": "attn_tc_kernel + lse_merge_kernel (one helm_paged_attn_decode call)",
+                         "kernel": "attn_tc_persistent_kernel (one helm_paged_attn_decode call: counter memset + kernel)",
                          "bytes_per_launch": bytes_launch, "avg_launch_ms": attn_avg_ms},
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -22,6 +22,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 namespace helm {
 
@@ -638,6 +640,503 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent, work-balanced variant (stream-K over pages).
+//
+// The work is the flat list of units u = (sequence b, kv head g, page i) in
+// b-major, g, i order; CTA c of C owns units [c*U/C, (c+1)*U/C), so every CTA
+// streams the same number of pages and its TMA pipeline stays full across
+// (b, g) boundaries.  A maximal run of units of one (b, g) pair inside a CTA is
+// a segment.  At a segment end the four consumer warps merge their states into
+// one CTA record of the pair (through the just-consumed stage buffer, which is
+// held back from the producer until then), store it at slot c + pair of the
+// workspace (unique: a later CTA never starts at an earlier pair) and bump the
+// pair's arrival counter.  The CTA that completes a pair's count merges all of
+// its CTA records after finishing its own units (chunked online log-sum-exp,
+// fixed CTA order), so a single launch yields the attention output.
+// ---------------------------------------------------------------------------
+constexpr int kMaxSeqs = 512;
+constexpr int kMaxPending = 64;  // deferred merges per CTA
+
+struct PersistArgs {
+  float *rec_o;        // [C + pairs][gq][D]: CTA c's unnormalised o for pair p at slot c + p
+  float *rec_ml;       // [C + pairs][gq][2]: its (m, l)
+  uint32_t *counter;   // [pairs], zero at launch
+  int C;               // grid size
+};
+
+// CTA owning unit u when U units are split over C CTAs as [c*U/C, (c+1)*U/C).
+__device__ __forceinline__ int owner_cta(int64_t u, int64_t U, int C) {
+  return (int)(((u + 1) * (int64_t)C - 1) / U);
+}
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_tc_persistent_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                              AttnArgs a, PersistArgs pa) {
+  constexpr int HN = NT * 8;        // padded heads per kv head
+  constexpr int EPT = HN;           // merge elements per consumer thread: HN * D / 128
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kStages];
+  __shared__ __align__(8) uint64_t empty_bar[kStages];
+  __shared__ int stage_used[kStages];
+  __shared__ int stage_pair[kStages];
+  __shared__ int stage_last[kStages];
+  __shared__ int seq_prefix[kMaxSeqs + 1];  // units before sequence b
+  __shared__ int seq_pages[kMaxSeqs];
+  __shared__ float m_x[kConsumerWarps][HN];
+  __shared__ float l_x[kConsumerWarps][HN];
+  __shared__ float mg_m[HN][32];    // merge chunk: maxima, then weights
+  __shared__ float mg_l[HN][32];
+  __shared__ float mg_M[HN], mg_L[HN], mg_A[HN];
+  __shared__ int pending[kMaxPending];
+  __shared__ int npending;
+
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int c = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int gq = a.gq, B = a.B, Hkv = a.Hkv;
+  const int rl = D + 2;
+
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], kConsumerWarps);
+    }
+    npending = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // Units per sequence and their prefix sums (warp 0: chunked scan).
+  if (warp == 0) {
+    const int per = (B + 31) / 32;
+    int local = 0;
+    for (int j = 0; j < per; ++j) {
+      const int b = lane * per + j;
+      if (b < B) {
+        const int n = read_num_pages(a, b);
+        seq_pages[b] = n;
+        local += n * Hkv;
+      }
+    }
+    int incl = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    int run = incl - local;
+    for (int j = 0; j < per; ++j) {
+      const int b = lane * per + j;
+      if (b < B) {
+        seq_prefix[b] = run;
+        run += seq_pages[b] * Hkv;
+      }
+    }
+    if (lane == 31) seq_prefix[B] = incl;
+  }
+  __syncthreads();
+  const int64_t U = seq_prefix[B];
+  // With fewer units than CTAs only the first U CTAs work, so every working CTA owns >= 1 unit
+  // and the CTAs between a pair's first and last owner all hold some of its units.
+  const int C = U < (int64_t)pa.C ? (int)U : pa.C;
+  int64_t u0 = 0, u1 = 0;
+  if (c < C) {
+    u0 = U * c / C;
+    u1 = U * (c + 1) / C;
+  }
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------ producer ------------------------------
+    // The 32 lanes decode and fetch the (page id, used, pair, last) of the next 32 units ahead of
+    // time (double-buffered), so a freed stage gets its TMA issued without a dependent load.
+    if (u1 > u0) {
+      auto fetch = [&](int64_t u, int &pid, int &used, int &pair, int &last) {
+        pid = -1;
+        used = 0;
+        pair = 0;
+        last = 0;
+        if (u >= u1) return;
+        int lo = 0, hi = B - 1;  // last b with seq_prefix[b] <= u and pages > 0
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (seq_prefix[mid] <= u) lo = mid; else hi = mid - 1;
+        }
+        int b = lo;
+        while (seq_pages[b] == 0 && b > 0) --b;
+        const int n = seq_pages[b];
+        const int rem = (int)(u - seq_prefix[b]);
+        const int g = rem / n, pi = rem - g * n;
+        pid = a.page_table[(int64_t)b * a.pt_stride + pi];
+        used = a.page_used[(int64_t)b * a.pt_stride + pi];
+        pair = b * Hkv + g;
+        last = (pi == n - 1) || (u + 1 == u1);
+      };
+      int c_pid, c_used, c_pair, c_last;  // current batch of 32 units, one per lane
+      int n_pid, n_used, n_pair, n_last;  // next batch
+      fetch(u0 + lane, c_pid, c_used, c_pair, c_last);
+      fetch(u0 + 32 + lane, n_pid, n_used, n_pair, n_last);
+      int issued = 0;
+      bool ok = true;
+      const int64_t n_units = u1 - u0;
+      for (int64_t i = 0; i < n_units; ++i) {
+        const int k = (int)(i & 31);
+        if (k == 0 && i > 0) {
+          c_pid = n_pid;
+          c_used = n_used;
+          c_pair = n_pair;
+          c_last = n_last;
+          fetch(u0 + i + 32 + lane, n_pid, n_used, n_pair, n_last);
+        }
+        const int pid = __shfl_sync(0xffffffffu, c_pid, k);
+        int used = __shfl_sync(0xffffffffu, c_used, k);
+        const int pair = __shfl_sync(0xffffffffu, c_pair, k);
+        const int last = __shfl_sync(0xffffffffu, c_last, k);
+        const int st = (int)(i % kStages);
+        if (lane == 0) {
+          if (i >= kStages && !mbar_wait(&empty_bar[st], (uint32_t)(((i / kStages) - 1) & 1))) {
+            flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+            ok = false;
+          } else {
+            if (pid < 0 || pid >= a.num_pool_pages) {
+              flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
+              used = 0;
+            } else if (used < 0 || used > P) {
+              flag_error(a.error_flag, HELM_DEVERR_PAGE_USED);
+              used = 0;
+            }
+            stage_used[st] = used;
+            stage_pair[st] = pair;
+            stage_last[st] = last;
+            if (used > 0) {
+              const int g = pair % Hkv;
+              uint8_t *kd = smem + st * kStageBytes;
+              uint8_t *vd = kd + kTileBytes;
+              mbar_arrive_expect_tx(&full_bar[st], kStageBytes);
+              tma_load_4d(kd, &tmK, &full_bar[st], 0, 0, g, pid);
+              tma_load_4d(kd + kHalfBytes, &tmK, &full_bar[st], 64, 0, g, pid);
+              tma_load_4d(vd, &tmV, &full_bar[st], 0, 0, g, pid);
+              tma_load_4d(vd + kHalfBytes, &tmV, &full_bar[st], 64, 0, g, pid);
+            } else {
+              mbar_arrive(&full_bar[st]);
+            }
+            issued = (int)i + 1;
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, (int)ok, 0)) break;
+      }
+      if (lane == 0) {
+        const int first = issued > kStages ? issued - kStages : 0;
+        for (int i = first; i < issued; ++i)
+          if (!mbar_wait(&full_bar[i % kStages], (i / kStages) & 1)) flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+      }
+    }
+  } else {
+    // ------------------------------ consumers -------------------------------
+    const int r = lane >> 2, cq = lane & 3;
+    const int mi = lane >> 3, ri = lane & 7;
+    const int row0 = warp * 16;
+    uint32_t qf[NT][8][2];
+    float o[NT][8][4];
+    float m_run[NT][2], l_run[NT][2];
+    int cur_pair = -1;
+
+    auto load_q = [&](int pair) {
+      const int b = pair / Hkv, g = pair - b * Hkv;
+      const T *qp = reinterpret_cast<const T *>(a.q) + ((int64_t)b * a.Hq + (int64_t)g * gq) * D;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int h = nt * 8 + r;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          qf[nt][j][0] = h < gq ? *reinterpret_cast<const uint32_t *>(qp + h * D + 16 * j + 2 * cq) : 0u;
+          qf[nt][j][1] = h < gq ? *reinterpret_cast<const uint32_t *>(qp + h * D + 16 * j + 2 * cq + 8) : 0u;
+        }
+      }
+    };
+    auto reset_state = [&]() {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[nt][dt][e] = 0.f;
+        m_run[nt][0] = m_run[nt][1] = -INFINITY;
+        l_run[nt][0] = l_run[nt][1] = 0.f;
+      }
+    };
+    reset_state();
+
+    const int64_t n_units = u1 - u0;
+    for (int64_t i = 0; i < n_units; ++i) {
+      const int st = (int)(i % kStages);
+      if (!mbar_wait(&full_bar[st], (uint32_t)((i / kStages) & 1))) {
+        flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+        break;
+      }
+      const int used = stage_used[st];
+      const int pair = stage_pair[st];
+      const int last = stage_last[st];
+      if (pair != cur_pair) {
+        load_q(pair);
+        cur_pair = pair;
+      }
+      const int nvalid = min(16, used - row0);
+      uint8_t *kt = smem + st * kStageBytes;
+      if (nvalid > 0) {
+        uint8_t *vt = kt + kTileBytes;
+        if (nvalid < 16) {
+          for (int idx = lane; idx < (16 - nvalid) * 16; idx += 32) {
+            const int rr = row0 + nvalid + idx / 16;
+            const int q16 = idx % 16;
+            *reinterpret_cast<uint4 *>(vt + (q16 >> 3) * kHalfBytes + rr * 128 + (q16 & 7) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+          __syncwarp();
+        }
+        const uint32_t kbase = smem_u32(kt), vbase = smem_u32(vt);
+        float sc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint32_t a0, a1, a2, a3;
+          const int row = row0 + ri + (mi & 1) * 8;
+          ldsm_x4(kbase + tile_off(row, 2 * j + (mi >> 1)), a0, a1, a2, a3);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) Mma<T>::run(sc[nt], a0, a1, a2, a3, qf[nt][j][0], qf[nt][j][1]);
+        }
+        const bool v_lo = r < nvalid, v_hi = r + 8 < nvalid;
+        uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float x0 = v_lo ? sc[nt][0] * a.scale_log2 : -INFINITY;
+          const float x1 = v_lo ? sc[nt][1] * a.scale_log2 : -INFINITY;
+          const float x2 = v_hi ? sc[nt][2] * a.scale_log2 : -INFINITY;
+          const float x3 = v_hi ? sc[nt][3] * a.scale_log2 : -INFINITY;
+          float t0 = fmaxf(x0, x2), t1 = fmaxf(x1, x3);
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) {
+            t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+            t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+          }
+          const float mn0 = fmaxf(m_run[nt][0], t0), mn1 = fmaxf(m_run[nt][1], t1);
+          const float al0 = rescale_weight(m_run[nt][0], mn0), al1 = rescale_weight(m_run[nt][1], mn1);
+          m_run[nt][0] = mn0;
+          m_run[nt][1] = mn1;
+          const float p0 = v_lo ? fast_exp2(x0 - mn0) : 0.f;
+          const float p1 = v_lo ? fast_exp2(x1 - mn1) : 0.f;
+          const float p2 = v_hi ? fast_exp2(x2 - mn0) : 0.f;
+          const float p3 = v_hi ? fast_exp2(x3 - mn1) : 0.f;
+          l_run[nt][0] = fmaf(l_run[nt][0], al0, p0 + p2);
+          l_run[nt][1] = fmaf(l_run[nt][1], al1, p1 + p3);
+          if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+            for (int dt = 0; dt < 8; ++dt) {
+              o[nt][dt][0] *= al0;
+              o[nt][dt][1] *= al1;
+              o[nt][dt][2] *= al0;
+              o[nt][dt][3] *= al1;
+            }
+          }
+          uint32_t h01, l01, h23, l23;
+          Mma<T>::split(p0, p1, h01, l01);
+          Mma<T>::split(p2, p3, h23, l23);
+          bh[nt][0] = movm_t(h01);
+          bh[nt][1] = movm_t(h23);
+          bl[nt][0] = movm_t(l01);
+          bl[nt][1] = movm_t(l23);
+        }
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) {
+          uint32_t a0, a1, a2, a3;
+          const int row = row0 + ri + (mi >> 1) * 8;
+          ldsm_x4_t(vbase + tile_off(row, 2 * dt + (mi & 1)), a0, a1, a2, a3);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            Mma<T>::run(o[nt][dt], a0, a1, a2, a3, bh[nt][0], bh[nt][1]);
+            Mma<T>::run(o[nt][dt], a0, a1, a2, a3, bl[nt][0], bl[nt][1]);
+          }
+        }
+      }
+
+      if (last) {
+        // ---- segment end: merge the four warps into one CTA record of the pair ----
+        // Every consumer warp is done with this stage's K/V (barrier), and the stage is not
+        // released to the producer until the merge below has read it: use it as scratch.
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        float *sx = reinterpret_cast<float *>(kt);  // [4][HN][D]
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int h0 = nt * 8 + 2 * cq;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float v = l_run[nt][e];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            if (r == 0) {
+              m_x[warp][h0 + e] = m_run[nt][e];
+              l_x[warp][h0 + e] = v;
+            }
+          }
+#pragma unroll
+          for (int dt = 0; dt < 8; ++dt) {
+            const int d = dt * 16 + r;
+            sx[(warp * HN + h0) * D + d] = o[nt][dt][0];
+            sx[(warp * HN + h0 + 1) * D + d] = o[nt][dt][1];
+            sx[(warp * HN + h0) * D + d + 8] = o[nt][dt][2];
+            sx[(warp * HN + h0 + 1) * D + d + 8] = o[nt][dt][3];
+          }
+        }
+        reset_state();
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        float *rec_o = pa.rec_o + (int64_t)(c + pair) * gq * D;
+        float *rec_ml = pa.rec_ml + (int64_t)(c + pair) * gq * 2;
+        for (int idx4 = tid; idx4 < gq * (D / 4); idx4 += kConsumerWarps * 32) {
+          const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
+          float M = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, m_x[w][h]);
+          float L = 0.f;
+          float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w) {
+            const float wt = rescale_weight(m_x[w][h], M);
+            L = fmaf(l_x[w][h], wt, L);
+            const float4 v = *reinterpret_cast<const float4 *>(sx + (w * HN + h) * D + d);
+            O.x = fmaf(v.x, wt, O.x);
+            O.y = fmaf(v.y, wt, O.y);
+            O.z = fmaf(v.z, wt, O.z);
+            O.w = fmaf(v.w, wt, O.w);
+          }
+          *reinterpret_cast<float4 *>(rec_o + h * D + d) = O;
+          if (d == 0) {
+            rec_ml[2 * h] = M;
+            rec_ml[2 * h + 1] = L;
+          }
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (tid == 0) {
+          const int b = pair / Hkv, g = pair - b * Hkv;
+          const int64_t up = seq_prefix[b] + (int64_t)g * seq_pages[b];
+          const int c0 = owner_cta(up, U, C), c1 = owner_cta(up + seq_pages[b] - 1, U, C);
+          const uint32_t old = atomicAdd(&pa.counter[pair], 1u);
+          if (old + 1 == (uint32_t)(c1 - c0 + 1)) pending[npending++] = pair;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      } else if (nvalid > 0 && nvalid < 16) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[st]);
+    }
+
+    // ---- deferred merges: pairs whose last CTA record this CTA wrote ----
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    __threadfence();
+    const int np = npending;
+    for (int k = 0; k < np; ++k) {
+      const int pair = pending[k];
+      const int b = pair / Hkv, g = pair - b * Hkv;
+      const int64_t up = seq_prefix[b] + (int64_t)g * seq_pages[b];
+      const int c0 = owner_cta(up, U, C), c1 = owner_cta(up + seq_pages[b] - 1, U, C);
+      const int nrec = c1 - c0 + 1;
+      const float *ro = pa.rec_o + (int64_t)(c0 + pair) * gq * D;    // CTA c0+j: + j*gq*D
+      const float *rml = pa.rec_ml + (int64_t)(c0 + pair) * gq * 2;  // CTA c0+j: + j*gq*2
+      constexpr int F4 = HN / 4;  // float4 elements per thread: HN*D/4/128
+      float4 acc[F4];
+#pragma unroll
+      for (int e = 0; e < F4; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (tid < gq) {
+        mg_M[tid] = -INFINITY;
+        mg_L[tid] = 0.f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+      for (int r0 = 0; r0 < nrec; r0 += 32) {
+        const int nr = min(32, nrec - r0);
+        for (int idx = tid; idx < gq * 32; idx += kConsumerWarps * 32) {
+          const int h = idx >> 5, rr = idx & 31;
+          if (rr < nr) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(rml + (int64_t)(r0 + rr) * gq * 2 + 2 * h));
+            mg_m[h][rr] = ml.x;
+            mg_l[h][rr] = ml.y;
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        if (tid < gq) {
+          const int h = tid;
+          float Mc = mg_M[h];
+          for (int rr = 0; rr < nr; ++rr) Mc = fmaxf(Mc, mg_m[h][rr]);
+          const float al = rescale_weight(mg_M[h], Mc);
+          float L = mg_L[h] * al;
+          for (int rr = 0; rr < nr; ++rr) {
+            const float wr = rescale_weight(mg_m[h][rr], Mc);
+            L = fmaf(mg_l[h][rr], wr, L);
+            mg_m[h][rr] = wr;
+          }
+          mg_A[h] = al;
+          mg_M[h] = Mc;
+          mg_L[h] = L;
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+#pragma unroll
+        for (int e = 0; e < F4; ++e) {
+          const int idx4 = tid + e * kConsumerWarps * 32;
+          if (idx4 < gq * (D / 4)) {
+            const int h = idx4 / (D / 4);
+            const float al = mg_A[h];
+            acc[e].x *= al;
+            acc[e].y *= al;
+            acc[e].z *= al;
+            acc[e].w *= al;
+          }
+        }
+#pragma unroll 4
+        for (int rr = 0; rr < nr; ++rr) {
+#pragma unroll
+          for (int e = 0; e < F4; ++e) {
+            const int idx4 = tid + e * kConsumerWarps * 32;
+            if (idx4 < gq * (D / 4)) {
+              const int h = idx4 / (D / 4);
+              const float w = mg_m[h][rr];
+              const float4 v = __ldcg(reinterpret_cast<const float4 *>(ro + (int64_t)(r0 + rr) * gq * D) + idx4);
+              acc[e].x = fmaf(w, v.x, acc[e].x);
+              acc[e].y = fmaf(w, v.y, acc[e].y);
+              acc[e].z = fmaf(w, v.z, acc[e].z);
+              acc[e].w = fmaf(w, v.w, acc[e].w);
+            }
+          }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+      }
+#pragma unroll
+      for (int e = 0; e < F4; ++e) {
+        const int idx4 = tid + e * kConsumerWarps * 32;
+        if (idx4 < gq * (D / 4)) {
+          const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
+          const float M = mg_M[h];
+          const float L = M == -INFINITY ? 0.f : mg_L[h];
+          const float vals[4] = {acc[e].x, acc[e].y, acc[e].z, acc[e].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) emit(a, 0, b, g * gq + h, d + j, M, L, M == -INFINITY ? 0.f : vals[j]);
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    }
+  }
+
+  // Sequences without pages: zero output (no CTA holds a unit of theirs).
+  if (warp < kConsumerWarps)
+    for (int pq = c; pq < B * Hkv; pq += gridDim.x) {
+      const int b = pq / Hkv, g = pq - b * Hkv;
+      if (seq_pages[b] != 0) continue;
+      for (int idx = tid; idx < gq * D; idx += kConsumerWarps * 32)
+        emit(a, 0, b, g * gq + idx / D, idx % D, -INFINITY, 0.f, 0.f);
+    }
+}
+
 }  // namespace tc
 
 // ===========================================================================
@@ -692,8 +1191,45 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 // 4-D map over the pool: (dim, token, kv head, page), box 64 x 64 x 1 x 1,
-// 128-byte swizzle.
+// 128-byte swizzle.  Encoded maps are cached (keyed by everything they encode), since
+// a decode step calls with the same pool every layer.
+struct MapKey {
+  const void *base;
+  int dtype, D, P, Hkv, pages;
+  int64_t head_stride, page_stride;
+  bool operator==(const MapKey &o) const {
+    return base == o.base && dtype == o.dtype && D == o.D && P == o.P && Hkv == o.Hkv && pages == o.pages &&
+           head_stride == o.head_stride && page_stride == o.page_stride;
+  }
+};
+
+bool encode_pool_map(CUtensorMap *m, const void *base, int kv_dtype, const helm_paged_attn_params *p);
+
 bool make_pool_map(CUtensorMap *m, const void *base, int kv_dtype, const helm_paged_attn_params *p) {
+  constexpr int kSlots = 32;
+  static std::mutex mu;
+  static MapKey keys[kSlots];
+  static CUtensorMap maps[kSlots];
+  static int filled = 0, next = 0;
+  const MapKey key{base, kv_dtype, p->D, p->P, p->Hkv, p->num_pool_pages, p->head_stride, p->page_stride};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < filled; ++i)
+      if (keys[i] == key) {
+        *m = maps[i];
+        return true;
+      }
+  }
+  if (!encode_pool_map(m, base, kv_dtype, p)) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  keys[next] = key;
+  maps[next] = *m;
+  next = (next + 1) % kSlots;
+  if (filled < kSlots) ++filled;
+  return true;
+}
+
+bool encode_pool_map(CUtensorMap *m, const void *base, int kv_dtype, const helm_paged_attn_params *p) {
   auto enc = get_encode_fn();
   if (!enc) return false;
   const int es = dtype_size(kv_dtype);
@@ -707,6 +1243,28 @@ bool make_pool_map(CUtensorMap *m, const void *base, int kv_dtype, const helm_pa
   return r == CUDA_SUCCESS;
 }
 
+// Debug switches, read on every call so that tests can flip them between calls (cheap: no
+// allocation, a short environment scan).
+bool env_flag(const char *name) {
+  const char *v = getenv(name);
+  return v && v[0] && v[0] != '0';
+}
+
+// cudaFuncSetAttribute once per (kernel, device).
+template <typename K>
+void ensure_smem_attr(K kernel, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void *, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void *key = reinterpret_cast<const void *>(kernel);
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto &d : done)
+    if (d.first == key && d.second == dev) return;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  done.emplace_back(key, dev);
+}
+
 bool tc_eligible(const helm_paged_attn_params *p) {
   if (!(p->kv_dtype == HELM_BF16 || p->kv_dtype == HELM_F16)) return false;
   if (p->q_dtype != p->kv_dtype) return false;
@@ -717,7 +1275,7 @@ bool tc_eligible(const helm_paged_attn_params *p) {
   if ((reinterpret_cast<uintptr_t>(p->q) & 3)) return false;
   if ((p->page_stride % 8) || (p->head_stride % 8)) return false;
   if (p->num_pool_pages < 1) return false;
-  if (getenv("HELM_B200_FORCE_GENERIC")) return false;
+  if (env_flag("HELM_B200_FORCE_GENERIC")) return false;
   return true;
 }
 
@@ -736,6 +1294,46 @@ int resolve_splits(const helm_paged_attn_params *p) {
   int S = (slots + pairs - 1) / pairs;
   if (S > maxp) S = maxp;
   return S < 1 ? 1 : S;
+}
+
+// Launch plan.  num_splits == 0 on a tensor-core-eligible call selects the persistent kernel
+// (one launch, C CTAs, fused merge); otherwise the split grid + lse_merge_kernel.
+struct Plan {
+  bool persistent = false;
+  int S = 1;          // split mode: splits
+  int C = 0;          // persistent mode: CTAs
+  int64_t rec_bytes = 0;
+  int64_t ml_off = 0;
+  int64_t counter_off = 0;
+  int64_t bytes = 0;  // workspace needed
+};
+
+Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
+  Plan pl;
+  const int rows = p->B * p->Hq;
+  const int pairs_all = p->B * p->Hkv;
+  const int64_t units_max = (int64_t)pairs_all * (p->max_pages > 0 ? p->max_pages : 1);
+  int64_t Cp = (int64_t)num_sms() * 2;
+  if (Cp > units_max) Cp = units_max;
+  if (Cp < 1) Cp = 1;
+  // a CTA covers at most units_max/C + 1 units, hence at most that many + 1 pairs
+  const bool pending_ok = pairs_all <= tc::kMaxPending || units_max / Cp + 2 <= tc::kMaxPending;
+  if (p->num_splits == 0 && eligible && p->B <= tc::kMaxSeqs && pending_ok && units_max < (1ll << 31) &&
+      !env_flag("HELM_B200_NO_PERSISTENT")) {
+    pl.persistent = true;
+    const int pairs = pairs_all;
+    pl.C = (int)Cp;
+    const int gq = p->Hq / p->Hkv;
+    const int64_t slots = pl.C + (int64_t)pairs;
+    pl.rec_bytes = slots * gq * p->D * (int64_t)sizeof(float);                 // o
+    pl.ml_off = (pl.rec_bytes + 255) / 256 * 256;
+    pl.counter_off = (pl.ml_off + slots * gq * 2 * (int64_t)sizeof(float) + 255) / 256 * 256;
+    pl.bytes = pl.counter_off + (int64_t)pairs * sizeof(uint32_t);
+    return pl;
+  }
+  pl.S = resolve_splits(p);
+  pl.bytes = pl.S > 1 ? (int64_t)pl.S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
+  return pl;
 }
 
 int validate(const helm_paged_attn_params *p) {
@@ -779,8 +1377,16 @@ int launch_generic(const AttnArgs &a, cudaStream_t st) {
 }
 
 template <typename T, int NT>
+int launch_tc_persistent(const CUtensorMap &mk, const CUtensorMap &mv, const AttnArgs &a,
+                         const tc::PersistArgs &pa, cudaStream_t st) {
+  ensure_smem_attr(tc::attn_tc_persistent_kernel<T, NT>, tc::kSmemBytes);
+  tc::attn_tc_persistent_kernel<T, NT><<<pa.C, tc::kThreads, tc::kSmemBytes, st>>>(mk, mv, a, pa);
+  return check_launch("attn_tc_persistent_kernel");
+}
+
+template <typename T, int NT>
 int launch_tc(const CUtensorMap &mk, const CUtensorMap &mv, const AttnArgs &a, cudaStream_t st) {
-  cudaFuncSetAttribute(tc::attn_tc_kernel<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes);
+  ensure_smem_attr(tc::attn_tc_kernel<T, NT>, tc::kSmemBytes);
   dim3 grid(a.num_splits, a.Hkv, a.B);
   tc::attn_tc_kernel<T, NT><<<grid, tc::kThreads, tc::kSmemBytes, st>>>(mk, mv, a);
   return check_launch("attn_tc_kernel");
@@ -793,10 +1399,9 @@ using namespace helm;
 
 extern "C" int64_t helm_paged_attn_workspace_bytes(const helm_paged_attn_params *p, int32_t *num_splits_out) {
   if (validate(p) != HELM_OK) return -1;
-  const int S = resolve_splits(p);
-  if (num_splits_out) *num_splits_out = S;
-  if (S <= 1) return 0;
-  return (int64_t)S * p->B * p->Hq * (p->D + 2) * (int64_t)sizeof(float);
+  const Plan pl = make_plan(p, tc_eligible(p));
+  if (num_splits_out) *num_splits_out = pl.persistent ? 0 : pl.S;
+  return pl.bytes;
 }
 
 extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *stream) {
@@ -804,12 +1409,14 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
   if (rc != HELM_OK) return rc;
   if (p->B == 0 || p->Hq == 0) return HELM_OK;
   cudaStream_t st = as_stream(stream);
-  const int S = resolve_splits(p);
+  const bool eligible = tc_eligible(p);
+  const Plan pl = make_plan(p, eligible);
+  const int S = pl.persistent ? 1 : pl.S;
   const int rows = p->B * p->Hq;
-  const int64_t need = S > 1 ? (int64_t)S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
+  const int64_t need = pl.bytes;
   if (need > 0 && (!p->workspace || p->workspace_bytes < need))
-    return fail(HELM_ERR_WORKSPACE, "paged_attn: workspace %lld bytes < %lld needed for %d splits",
-                (long long)p->workspace_bytes, (long long)need, S);
+    return fail(HELM_ERR_WORKSPACE, "paged_attn: workspace %lld bytes < %lld needed", (long long)p->workspace_bytes,
+                (long long)need);
 
   AttnArgs a{};
   a.q = p->q;
@@ -840,11 +1447,29 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
     a.out_record = p->out_record;
   }
 
-  if (tc_eligible(p)) {
+  if (eligible) {
     CUtensorMap mk, mv;
     if (!make_pool_map(&mk, p->k_base, p->kv_dtype, p) || !make_pool_map(&mv, p->v_base, p->kv_dtype, p))
       return fail(HELM_ERR_CUDA, "paged_attn: cuTensorMapEncodeTiled failed");
     const bool two = a.gq > 8;
+    if (pl.persistent) {
+      tc::PersistArgs pa;
+      pa.rec_o = p->workspace;
+      pa.rec_ml = reinterpret_cast<float *>(reinterpret_cast<char *>(p->workspace) + pl.ml_off);
+      pa.counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(p->workspace) + pl.counter_off);
+      pa.C = pl.C;
+      cudaError_t e = cudaMemsetAsync(pa.counter, 0, (size_t)p->B * p->Hkv * sizeof(uint32_t), st);
+      if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: cudaMemsetAsync: %s", cudaGetErrorString(e));
+      a.rec = nullptr;
+      a.out = p->out;
+      a.out_record = p->out_record;
+      a.num_splits = 1;
+      if (p->kv_dtype == HELM_BF16)
+        return two ? launch_tc_persistent<__nv_bfloat16, 2>(mk, mv, a, pa, st)
+                   : launch_tc_persistent<__nv_bfloat16, 1>(mk, mv, a, pa, st);
+      return two ? launch_tc_persistent<__half, 2>(mk, mv, a, pa, st)
+                 : launch_tc_persistent<__half, 1>(mk, mv, a, pa, st);
+    }
     if (p->kv_dtype == HELM_BF16)
       rc = two ? launch_tc<__nv_bfloat16, 2>(mk, mv, a, st) : launch_tc<__nv_bfloat16, 1>(mk, mv, a, st);
     else

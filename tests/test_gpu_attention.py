@@ -261,3 +261,63 @@ def test_full_size_config5_layer(cuda):
             ref = (p @ v).cpu()
             err = attn_error(out[b, g * 8:(g + 1) * 8], ref)
             assert err <= 2e-3, (b, g, err)
+
+
+@pytest.mark.parametrize("lens", [[0, 1, 64 * 3 + 5, 64 * 40, 17], [64 * 7], [1, 1, 1], [0, 0], [5000, 0, 3000, 64]])
+@pytest.mark.parametrize("gq", [8, 5, 16])
+def test_persistent_kernel_matches_split_kernel(lens, gq, cuda):
+    """The persistent (work-balanced, fused-merge) launch against the split-grid launch and the
+    oracle, with ragged / empty sequences; twice in a row (the arrival counters are reset)."""
+    torch.manual_seed(sum(lens) + gq)
+    Hkv, D, P = 4, 128, 64
+    npages = [math.ceil(n / P) for n in lens]
+    total = max(1, sum(npages)) + 3
+    kp = torch.randn(total, Hkv, P, D, device=cuda).to(torch.bfloat16)
+    vp = torch.randn(total, Hkv, P, D, device=cuda).to(torch.bfloat16)
+    perm = torch.randperm(total).tolist()
+    tables, useds, i = [], [], 0
+    for n, npg in zip(lens, npages):
+        tables.append(perm[i:i + npg])
+        useds.append([P] * (npg - 1) + [n - P * (npg - 1)] if npg else [])
+        i += npg
+    q = torch.randn(len(lens), Hkv * gq, D, device=cuda).to(torch.bfloat16)
+    a1 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=0, out_dtype=torch.float32)
+    a2 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=0, out_dtype=torch.float32)
+    s1 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=1, out_dtype=torch.float32)
+    assert torch.equal(a1, a2)
+    assert float((a1 - s1).abs().max()) < 1e-4
+    width = max(1, max(npages))
+    ref = OA.paged_attention_torch(q.cpu(), kp.cpu(), vp.cpu(),
+                                   torch.tensor([t + [0] * (width - len(t)) for t in tables]),
+                                   torch.tensor([u + [0] * (width - len(u)) for u in useds]), torch.tensor(npages))
+    assert_attn_close(a1, ref, torch.bfloat16, f"persistent lens={lens}")
+    for b, n in enumerate(lens):
+        if n == 0:
+            assert torch.all(a1[b] == 0)
+
+
+def test_persistent_out_record_merges_across_calls(cuda):
+    """out_record of the persistent launch, merged over two halves of a sequence, equals the
+    one-call output (the multi-GPU merge contract)."""
+    from helm_b200 import ops
+    torch.manual_seed(21)
+    Hkv, D, P, gq, B = 8, 128, 64, 8, 3
+    kp = torch.randn(300, Hkv, P, D, device=cuda).to(torch.bfloat16)
+    vp = torch.randn(300, Hkv, P, D, device=cuda).to(torch.bfloat16)
+    q = torch.randn(B, Hkv * gq, D, device=cuda).to(torch.bfloat16)
+    perm = torch.randperm(300, device=cuda).to(torch.int32)
+    pt = perm[:B * 90].reshape(B, 90).contiguous()
+    pu = torch.full((B, 90), P, dtype=torch.int32, device=cuda)
+    full = ops.paged_decode_attention(q, kp, vp, pt, pu, torch.full((B,), 90, dtype=torch.int32, device=cuda),
+                                      num_kv_heads=Hkv, page_size=P, page_stride=Hkv * P * D, head_stride=P * D,
+                                      num_pool_pages=300, out_dtype=torch.float32)
+    recs = []
+    for lo, hi in ((0, 37), (37, 90)):
+        rec = torch.empty(B * Hkv * gq, D + 2, device=cuda)
+        ops.paged_decode_attention(q, kp, vp, pt[:, lo:hi].contiguous(), pu[:, lo:hi].contiguous(),
+                                   torch.full((B,), hi - lo, dtype=torch.int32, device=cuda), num_kv_heads=Hkv,
+                                   page_size=P, page_stride=Hkv * P * D, head_stride=P * D, num_pool_pages=300,
+                                   out_record=rec)
+        recs.append(rec)
+    merged = ops.lse_merge(torch.stack(recs).contiguous(), out=torch.empty(B * Hkv * gq, D, device=cuda))
+    assert float((merged.reshape(B, -1, D) - full).abs().max()) < 1e-5
