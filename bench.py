@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="cross-GPU record exchange for N > 1")
     # Smaller stacks for ncu captures only; the reported workload is config 5 unless these are set.
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=None)
@@ -204,7 +206,7 @@ def run_reference(args, rank):
 class Stack:
     """Device state of the sharded attention stack on one rank."""
 
-    def __init__(self, rank, world, dev, spare_pages):
+    def __init__(self, rank, world, dev, spare_pages, exchange="p2p"):
         from helm_b200 import ops
         self.ops = ops
         c = CFG
@@ -239,7 +241,10 @@ class Stack:
         self.out = torch.empty((self.L, self.B, self.Hq, self.D), dtype=torch.bfloat16, device=dev)
         rows = self.B * self.Hq
         self.rec = torch.empty((self.L, rows, self.D + 2), dtype=torch.float32, device=dev)
-        self.gathered = torch.empty((self.L, world, rows, self.D + 2), dtype=torch.float32, device=dev)
+        self.shard = None
+        if world > 1:
+            from helm_b200.runtime.sharded import KVShardGroup
+            self.shard = KVShardGroup(rows, self.D, dev, exchange=exchange)
         self.k_base = self.pool[:, 0]
         self.v_base = self.pool[:, 1]
         self.page_stride = 2 * self.Hkv * self.P * self.D
@@ -304,8 +309,7 @@ class Stack:
                 N.check("helm_kv_append", self.lib.helm_kv_append(ctypes.byref(self.append_params[l]), sp))
             N.check("helm_paged_attn_decode", self.lib.helm_paged_attn_decode(ctypes.byref(self.attn_params[l]), sp))
             if self.world > 1:
-                dist.all_gather_into_tensor(self.gathered[l], self.rec[l])
-                self.ops.lse_merge(self.gathered[l], out=self.out[l].view(self.B * self.Hq, self.D))
+                self.shard.gather_merge(self.rec[l], out=self.out[l].view(self.B * self.Hq, self.D))
 
 
 def run_helm(args, rank, local, world):
@@ -315,7 +319,7 @@ def run_helm(args, rank, local, world):
     c = CFG
     total_steps = args.warmup + args.steps + (args.e2e_steps if args.e2e_steps is not None else args.steps) + 8
     spare = (total_steps + c["page"] - 1) // c["page"] + 1
-    st = Stack(rank, world, dev, spare)
+    st = Stack(rank, world, dev, spare, exchange=args.exchange)
     stream = torch.cuda.current_stream(dev)
     torch.cuda.synchronize(dev)
 
@@ -409,6 +413,8 @@ def run_helm(args, rank, local, world):
         }
         print(json.dumps(line), flush=True)
     barrier(world)
+    if st.shard is not None:
+        st.shard.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -453,8 +459,7 @@ def run_e2e(st, stream, steps, world, dev):
                                            st.num_pages[l], num_kv_heads=st.Hkv, page_size=st.P,
                                            page_stride=st.page_stride, head_stride=st.head_stride,
                                            num_pool_pages=st.n_pool, out_record=st.rec[l], workspace=st.ws)
-                dist.all_gather_into_tensor(st.gathered[l], st.rec[l])
-                ops.lse_merge(st.gathered[l], out=st.out[l].view(B * st.Hq, st.D))
+                st.shard.gather_merge(st.rec[l], out=st.out[l].view(B * st.Hq, st.D))
         out_h.copy_(st.out, non_blocking=True)
     t1.record(stream)
     torch.cuda.synchronize(dev)

@@ -62,6 +62,19 @@ class KVAppendParams(ctypes.Structure):
     ]
 
 
+MAX_RANKS = 8
+
+
+class GatherMergeParams(ctypes.Structure):
+    _fields_ = [
+        ("rank", _i32), ("world", _i32), ("rows", _i32), ("D", _i32),
+        ("record", _p),
+        ("peer_recv", _p * MAX_RANKS), ("peer_flags", _p * MAX_RANKS),
+        ("recv_local", _p), ("flags_local", _p), ("counters", _p),
+        ("out", _p), ("out_dtype", _i32), ("out_record", _p), ("error_flag", _p),
+    ]
+
+
 # (name, restype, argtypes) for every entry point of include/helm_b200.h
 SIGNATURES = [
     ("helm_abi_version", _c.c_int, []),
@@ -72,6 +85,12 @@ SIGNATURES = [
     ("helm_int8_linear", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
     ("helm_kv_append", _c.c_int, [_c.POINTER(KVAppendParams), _p]),
     ("helm_copy_pages", _c.c_int, [_p, _i64, _p, _p, _i32, _i64, _c.POINTER(_i32), _p]),
+    ("helm_gather_merge_state_bytes", _i64, [_i32, _i32, _i32, _c.POINTER(_i64), _c.POINTER(_i64),
+                                              _c.POINTER(_i64)]),
+    ("helm_gather_merge", _c.c_int, [_c.POINTER(GatherMergeParams), _p]),
+    ("helm_ipc_export", _c.c_int, [_p, _p, _c.POINTER(_i64)]),
+    ("helm_ipc_import", _c.c_int, [_p, _i64, _c.POINTER(_p), _c.POINTER(_p)]),
+    ("helm_ipc_close", _c.c_int, [_p]),
 ]
 
 _lib = None

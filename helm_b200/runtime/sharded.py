@@ -1,0 +1,123 @@
+"""KV sequence sharding over the GPUs of one node (one process per GPU).
+
+No counterpart in HELM (its runtime is single-process).  Rank g of G holds
+pages [g*n/G, (g+1)*n/G) of every sequence and layer; the last rank holds the
+tail and receives new tokens.  Per layer every rank runs the paged attention
+over its pages into a merged record (o, m, l) per (sequence, query head), and
+KVShardGroup.gather_merge exchanges those records and merges them so every
+rank ends with the same attention output.
+
+Two exchanges are provided:
+* "p2p" (default): helm_gather_merge -- one kernel that stores the records
+  into every rank's receive buffer over NVLink (CUDA IPC mappings) and merges
+  them; no NCCL call on the decode path;
+* "nccl": torch.distributed.all_gather_into_tensor + helm_lse_merge.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from .. import _native as N
+from .. import ops
+
+
+def shard_bounds(n: int, rank: int, world: int) -> Tuple[int, int]:
+    """Contiguous share [lo, hi) of n items (pages) for `rank`: floor(n*g/G) .. floor(n*(g+1)/G)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} / world {world}")
+    return (n * rank) // world, (n * (rank + 1)) // world
+
+
+class KVShardGroup:
+    def __init__(self, rows: int, head_dim: int, device, group=None, exchange: str = "p2p"):
+        import torch.distributed as dist
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rows, self.D = rows, head_dim
+        self.device = torch.device(device)
+        self.exchange = exchange
+        self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._bases = []
+        self.params = None
+        if self.world > N.MAX_RANKS:
+            raise ValueError(f"KVShardGroup: at most {N.MAX_RANKS} ranks")
+        if exchange == "nccl" or self.world == 1:
+            self.gathered = torch.empty((self.world, rows, head_dim + 2), dtype=torch.float32, device=self.device)
+            return
+        if exchange != "p2p":
+            raise ValueError(f"unknown exchange {exchange!r}")
+        lib = N.lib()
+        rb, fb, cb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        if lib.helm_gather_merge_state_bytes(self.world, rows, head_dim, ctypes.byref(rb), ctypes.byref(fb),
+                                             ctypes.byref(cb)) < 0:
+            N.check("helm_gather_merge_state_bytes", N.ERR_INVALID_ARGUMENT)
+        self.recv_bytes = rb.value
+        # receive slots + flags in one allocation (shared with the peers), counters local
+        self.buf = torch.zeros(rb.value + fb.value, dtype=torch.uint8, device=self.device)
+        self.counters = torch.zeros(max(cb.value, 4), dtype=torch.uint8, device=self.device)
+        torch.cuda.synchronize(self.device)
+        handle = (ctypes.c_char * 64)()
+        off = ctypes.c_int64()
+        N.check("helm_ipc_export", lib.helm_ipc_export(self.buf.data_ptr(), handle, ctypes.byref(off)))
+        infos = [None] * self.world
+        dist.all_gather_object(infos, (bytes(handle), off.value), group=group)
+        p = N.GatherMergeParams()
+        p.rank, p.world, p.rows, p.D = self.rank, self.world, rows, head_dim
+        for r in range(self.world):
+            if r == self.rank:
+                ptr = self.buf.data_ptr()
+            else:
+                h = (ctypes.c_char * 64).from_buffer_copy(infos[r][0])
+                out_ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+                N.check("helm_ipc_import", lib.helm_ipc_import(h, infos[r][1], ctypes.byref(out_ptr),
+                                                               ctypes.byref(base)))
+                self._bases.append(base.value)
+                ptr = out_ptr.value
+            p.peer_recv[r] = ptr
+            p.peer_flags[r] = ptr + rb.value
+        p.recv_local = self.buf.data_ptr()
+        p.flags_local = self.buf.data_ptr() + rb.value
+        p.counters = self.counters.data_ptr()
+        p.error_flag = self.error_flag.data_ptr()
+        self.params = p
+        dist.barrier(group=group)
+
+    def gather_merge(self, record: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     out_record: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+        """Exchanges this rank's record [rows, D+2] (fp32) and writes the merged result to out
+        [rows, D] and/or out_record [rows, D+2] on every rank."""
+        if record.shape != (self.rows, self.D + 2) or record.dtype != torch.float32 or not record.is_contiguous():
+            raise ValueError("gather_merge: record must be contiguous fp32 [rows, D+2]")
+        if self.world == 1:
+            return ops.lse_merge(record.unsqueeze(0), out=out, out_record=out_record)
+        if self.params is None:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(self.gathered, record, group=self.group)
+            return ops.lse_merge(self.gathered, out=out, out_record=out_record)
+        p = self.params
+        p.record = record.data_ptr()
+        p.out = None if out is None else out.data_ptr()
+        p.out_dtype = ops.dtype_code(out.dtype) if out is not None else N.F32
+        p.out_record = None if out_record is None else out_record.data_ptr()
+        N.check("helm_gather_merge", N.lib().helm_gather_merge(ctypes.byref(p),
+                                                               torch.cuda.current_stream(self.device).cuda_stream))
+        return out
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (call on every rank, after the last exchange)."""
+        import torch.distributed as dist
+        if self._bases:
+            torch.cuda.synchronize(self.device)
+            if dist.is_initialized():
+                dist.barrier(group=self.group)
+            lib = N.lib()
+            for base in self._bases:
+                lib.helm_ipc_close(base)
+            self._bases = []
+            if dist.is_initialized():
+                dist.barrier(group=self.group)
+        self.params = None

@@ -220,6 +220,52 @@ typedef struct {
 
 int helm_kv_append(const helm_kv_append_params *p, void *stream);
 
+/* ---- KV sequence sharding: cross-GPU record exchange + merge ------------- */
+/*
+ * No reference counterpart (HELM has no multi-GPU path): with each sequence's
+ * pages split across `world` GPUs, every rank computes a merged record
+ * [rows][D+2] (helm_paged_attn_decode's out_record) over its pages; this call
+ * exchanges the records over NVLink and merges them (helm_lse_merge semantics,
+ * fixed rank order) into out [rows, D] on every rank.
+ *
+ * Each rank owns one exchange buffer of helm_gather_merge_state_bytes():
+ * recv_bytes of receive slots followed by flags_bytes of flags, zeroed once
+ * before the first call and shared with the other ranks through CUDA IPC
+ * (helm_ipc_export / helm_ipc_import).  peer_recv[r] / peer_flags[r] are rank
+ * r's buffer parts as mapped in this process (this rank's own entries are its
+ * local pointers).  `counters` (counters_bytes, zeroed once) stays local.
+ * Every rank must make the same sequence of calls with the same rows and D.
+ * Waits for peers are bounded (2 s); a wait that gives up sets
+ * HELM_DEVERR_TIMEOUT in error_flag and leaves zeros in the affected rows.
+ */
+#define HELM_MAX_RANKS 8
+
+typedef struct {
+  int32_t rank, world, rows, D;
+  const float *record;                  /* [rows][D+2], this rank's */
+  float *peer_recv[HELM_MAX_RANKS];
+  uint32_t *peer_flags[HELM_MAX_RANKS];
+  float *recv_local;
+  uint32_t *flags_local;
+  uint32_t *counters;
+  void *out;                            /* [rows, D] or null */
+  int32_t out_dtype;
+  float *out_record;                    /* [rows, D+2] or null */
+  int32_t *error_flag;
+} helm_gather_merge_params;
+
+int64_t helm_gather_merge_state_bytes(int32_t world, int32_t rows, int32_t D, int64_t *recv_bytes_out,
+                                      int64_t *flags_bytes_out, int64_t *counters_bytes_out);
+
+int helm_gather_merge(const helm_gather_merge_params *p, void *stream);
+
+/* CUDA IPC: export the allocation containing a device pointer (64-byte handle
+ * + the pointer's offset in it); import a peer's handle (returns the pointer
+ * and the mapping base to close). */
+int helm_ipc_export(const void *ptr, void *handle_out, int64_t *offset_out);
+int helm_ipc_import(const void *handle, int64_t offset, void **ptr_out, void **base_out);
+int helm_ipc_close(void *base);
+
 /* ---- page gather (host pages -> HBM staging) ------------------------------ */
 /*
  * Replaces the per-page H2D prefetch of perform_streaming_attention
