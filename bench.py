@@ -204,37 +204,49 @@ def run_reference(args, rank):
 # helm arm
 # ----------------------------------------------------------------------------
 class Stack:
-    """Device state of the sharded attention stack on one rank."""
+    """The sharded attention stack on one rank, held by the drop-in runtime: a KVAllocator whose
+    device slab holds every page, one KVCacheManager per sequence (prefilled through
+    append_prefill) and the batch's device page tables (DecodeBatch)."""
 
     def __init__(self, rank, world, dev, spare_pages, exchange="p2p"):
         from helm_b200 import ops
+        from helm_b200.runtime import KVAllocator, KVCacheManager
+        from helm_b200.runtime.paged import DecodeBatch
+        from helm_b200.runtime.sharded import shard_bounds
         self.ops = ops
         c = CFG
         self.rank, self.world, self.dev = rank, world, dev
         self.L, self.B, self.Hq, self.Hkv, self.D, self.P = (c["layers"], c["batch"], c["q_heads"], c["kv_heads"],
                                                              c["head_dim"], c["page"])
-        assert c["ctx"] % (world * self.P) == 0
-        self.local_ctx = c["ctx"] // world
-        self.npg = self.local_ctx // self.P
+        plo, phi = shard_bounds(c["ctx"] // self.P, rank, world)
+        self.npg = phi - plo
+        self.local_ctx = self.npg * self.P
         self.tail = rank == world - 1
         self.spare = spare_pages if self.tail else 0
-        width = self.npg + self.spare
-        n_pool = self.L * self.B * width
-        self.n_pool = n_pool
+        self.alloc = KVAllocator(num_layers=self.L, num_kv_heads=self.Hkv, head_dim=self.D, page_size=self.P,
+                                 dtype=torch.bfloat16)
+        self.alloc.reserve_capacity(dev, self.L * self.B * (self.npg + self.spare) + 4 * self.L * self.B + 64)
+        self.kvcms = [KVCacheManager(self.alloc, gpu_high_watermark_bytes=1 << 62) for _ in range(self.B)]
+        self.batch = DecodeBatch(self.kvcms, self.L, dev, width=self.npg + self.spare + 8)
         g = torch.Generator(device=dev).manual_seed(1234 + rank)
-        # pool [pages, K/V, Hkv, P, D]
-        self.pool = torch.empty((n_pool, 2, self.Hkv, self.P, self.D), dtype=torch.bfloat16, device=dev)
-        chunk = 2048
-        for i in range(0, n_pool, chunk):
-            self.pool[i:i + chunk].normal_(generator=g)
-        perm = torch.randperm(n_pool, device=dev, generator=g).to(torch.int32).reshape(self.L, self.B, width)
-        self.page_table = perm[:, :, :].clone()
-        self.spare_ids = perm[:, :, self.npg:].contiguous()
-        self.page_used = torch.full((self.L, self.B, width), self.P, dtype=torch.int32, device=dev)
-        self.page_used[:, :, self.npg:] = 0
-        self.num_pages = torch.full((self.L, self.B), self.npg, dtype=torch.int32, device=dev)
+        for l in range(self.L):
+            for b in range(self.B):
+                K = torch.randn((1, self.Hkv, self.local_ctx, self.D), generator=g, device=dev, dtype=torch.bfloat16)
+                V = torch.randn((1, self.Hkv, self.local_ctx, self.D), generator=g, device=dev, dtype=torch.bfloat16)
+                self.kvcms[b].append_prefill(l, K, V)
+                self.batch.sync_row(l, b)
+        del K, V
+        self.store = self.alloc.store(dev)
+        self.n_pool = self.store.capacity
+        # spare pages for the device-directed appends of the graph-captured step (tail rank)
+        spare_ids = torch.zeros((self.L, self.B, max(self.spare, 1)), dtype=torch.int32)
+        for l in range(self.L):
+            for b in range(self.B):
+                for j in range(self.spare):
+                    spare_ids[l, b, j] = self.alloc.allocate(dev).slot
+        self.spare_ids = spare_ids.to(dev)
         self.spare_next = torch.zeros((self.L, self.B), dtype=torch.int32, device=dev)
-        self.error_flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.error_flag = self.batch.error_flag
         self.q = torch.randn((self.L, self.B, self.Hq, self.D), generator=g, device=dev).to(torch.bfloat16)
         self.k_new = torch.randn((self.L, self.B, self.Hkv, self.D), generator=g, device=dev).to(torch.bfloat16)
         self.v_new = torch.randn((self.L, self.B, self.Hkv, self.D), generator=g, device=dev).to(torch.bfloat16)
@@ -245,10 +257,9 @@ class Stack:
         if world > 1:
             from helm_b200.runtime.sharded import KVShardGroup
             self.shard = KVShardGroup(rows, self.D, dev, exchange=exchange)
-        self.k_base = self.pool[:, 0]
-        self.v_base = self.pool[:, 1]
-        self.page_stride = 2 * self.Hkv * self.P * self.D
-        self.head_stride = self.P * self.D
+        self.k_base, self.v_base = self.store.base_ptrs()
+        self.page_stride = self.store.page_elems
+        self.head_stride = self.store.head_stride
         self._build_params()
 
     def _build_params(self):
@@ -257,12 +268,13 @@ class Stack:
         self.lib = N.lib()
         self.attn_params, self.append_params = [], []
         ws_need = 0
+        bt = self.batch
         for l in range(self.L):
             p = ops.make_attn_params(
-                self.q[l], self.k_base, self.v_base, self.page_table[l], self.page_used[l], self.num_pages[l],
+                self.q[l], self.k_base, self.v_base, bt.table[l], bt.used[l], bt.npages[l],
                 num_kv_heads=self.Hkv, page_size=self.P, page_stride=self.page_stride,
-                head_stride=self.head_stride, num_pool_pages=self.n_pool,
-                max_pages=self.page_table.shape[-1], out=self.out[l] if self.world == 1 else None,
+                head_stride=self.head_stride, num_pool_pages=self.n_pool, max_pages=bt.width,
+                out=self.out[l] if self.world == 1 else None,
                 out_record=self.rec[l] if self.world > 1 else None, error_flag=self.error_flag)
             S = ctypes.c_int32(0)
             need = self.lib.helm_paged_attn_workspace_bytes(ctypes.byref(p), ctypes.byref(S))
@@ -273,15 +285,14 @@ class Stack:
                 a = ops.make_append_params(
                     self.k_new[l], self.v_new[l], self.k_base, self.v_base, page_stride=self.page_stride,
                     head_stride=self.head_stride, num_pool_pages=self.n_pool, page_size=self.P,
-                    page_table=self.page_table[l], page_used=self.page_used[l], num_pages=self.num_pages[l],
+                    page_table=bt.table[l], page_used=bt.used[l], num_pages=bt.npages[l],
                     spare_pages=self.spare_ids[l], spare_next=self.spare_next[l], error_flag=self.error_flag)
                 self.append_params.append(a)
         self.splits = self.attn_params[0].num_splits
-        self.ws = torch.empty(max(ws_need // 4, 1), dtype=torch.float32, device=self.dev)
+        self.ws = torch.zeros(max(ws_need // 4, 1), dtype=torch.float32, device=self.dev)
         for p in self.attn_params:
             p.workspace = self.ws.data_ptr()
             p.workspace_bytes = self.ws.numel() * 4
-        # launches per step of our own kernels
         per_layer = (1 if self.tail else 0) + 1 + (1 if self.splits > 1 else 0) + (1 if self.world > 1 else 0)
         self.launches_per_step = self.L * per_layer
 
@@ -299,9 +310,8 @@ class Stack:
                 self.lib.helm_paged_attn_decode(ctypes.byref(self.attn_params[l]), stream.cuda_stream))
 
     def step(self, stream):
-        """One decode step over all layers: append (tail rank), attention, and for N > 1 the
-        all-gather of the per-head records and their merge."""
-        import torch.distributed as dist
+        """One decode step over all layers on the device-resident state (device-directed append
+        on the tail rank, attention, and for N > 1 the record exchange + merge)."""
         from helm_b200 import _native as N
         sp = stream.cuda_stream
         for l in range(self.L):
@@ -317,7 +327,7 @@ def run_helm(args, rank, local, world):
     torch.cuda.set_device(dev)
     dist = init_pg(world, local)
     c = CFG
-    total_steps = args.warmup + args.steps + (args.e2e_steps if args.e2e_steps is not None else args.steps) + 8
+    total_steps = args.warmup + args.steps + 8
     spare = (total_steps + c["page"] - 1) // c["page"] + 1
     st = Stack(rank, world, dev, spare, exchange=args.exchange)
     stream = torch.cuda.current_stream(dev)
@@ -394,11 +404,13 @@ def run_helm(args, rank, local, world):
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "timing": "CUDA graph of one decode step (all layers) replayed K times; CUDA events, max over ranks",
+            "setup": {"prefill": "append_prefill per (layer, sequence) through KVCacheManager",
+                      "pool_gb": round(st.store.slab.numel() * 2 / 1e9, 1)},
             "config": {"workload": WORKLOAD if (c["layers"], c["ctx"]) == (64, 131072) else
                        f"REDUCED (profiling only): {c['layers']} layers, ctx {c['ctx']}",
                        "global_batch": c["batch"], "seq_len": c["ctx"],
                        "layers": c["layers"], "parallelism": f"kv-seq-shard{world}",
-                       "l2": "inputs larger than L2 (KV %.1f GB per GPU)" % (st.pool.numel() * 2 / 1e9),
+                       "l2": "inputs larger than L2 (KV %.1f GB per GPU)" % (st.store.slab.numel() * 2 / 1e9),
                        "num_splits": st.splits},
             "hbm_gbs": step_bytes_all / (ms_step * 1e-3) / 1e9 / world,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -420,11 +432,14 @@ def run_helm(args, rank, local, world):
 
 
 def run_e2e(st, stream, steps, world, dev):
-    """The same decode steps through the public op API with the step's inputs (q, new K/V of
-    every layer) copied from pinned host memory and the outputs read back every step."""
-    from helm_b200 import ops
-    import torch.distributed as dist
+    """The same decode steps through the drop-in runtime API: per layer
+    helm_b200.runtime.kv_offload._decode_batched (the call the patched attention forward makes)
+    with the step's inputs (q and the new K/V of every layer) copied from pinned host memory and
+    the outputs read back every step."""
+    from helm_b200.runtime.kv_offload import _decode_batched
     L, B = st.L, st.B
+    # the graph-captured steps advanced the device tables on their own: resync them from the host
+    st.batch.synced = [[None] * st.B for _ in range(st.L)]
     q_h = st.q.cpu().pin_memory()
     k_h = st.k_new.cpu().pin_memory()
     v_h = st.v_new.cpu().pin_memory()
@@ -432,40 +447,34 @@ def run_e2e(st, stream, steps, world, dev):
     q_d = torch.empty_like(st.q)
     k_d = torch.empty_like(st.k_new)
     v_d = torch.empty_like(st.v_new)
-    h2d = q_h.numel() * 2 + (k_h.numel() * 2 * 2 if st.tail else 0)
+    out_d = torch.empty_like(st.out)
+    h2d = q_h.numel() * 2 + k_h.numel() * 2 * 2
     d2h = out_h.numel() * 2
+    scale = 1.0 / math.sqrt(st.D)
+    shard = st.shard
+
+    def one_step():
+        q_d.copy_(q_h, non_blocking=True)
+        k_d.copy_(k_h, non_blocking=True)
+        v_d.copy_(v_h, non_blocking=True)
+        for l in range(L):
+            out_d[l] = _decode_batched(st.kvcms, q_d[l].unsqueeze(2), k_d[l].unsqueeze(2), v_d[l].unsqueeze(2),
+                                       l, scale, shard=shard)[:, :, 0]
+        out_h.copy_(out_d, non_blocking=True)
+
+    one_step()  # warm
     torch.cuda.synchronize(dev)
     barrier(world)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for _ in range(steps):
-        q_d.copy_(q_h, non_blocking=True)
-        if st.tail:
-            k_d.copy_(k_h, non_blocking=True)
-            v_d.copy_(v_h, non_blocking=True)
-        for l in range(L):
-            if st.tail:
-                ops.kv_append(k_d[l], v_d[l], st.k_base, st.v_base, page_stride=st.page_stride,
-                              head_stride=st.head_stride, num_pool_pages=st.n_pool, page_size=st.P,
-                              page_table=st.page_table[l], page_used=st.page_used[l], num_pages=st.num_pages[l],
-                              spare_pages=st.spare_ids[l], spare_next=st.spare_next[l], error_flag=st.error_flag)
-            if world == 1:
-                ops.paged_decode_attention(q_d[l], st.k_base, st.v_base, st.page_table[l], st.page_used[l],
-                                           st.num_pages[l], num_kv_heads=st.Hkv, page_size=st.P,
-                                           page_stride=st.page_stride, head_stride=st.head_stride,
-                                           num_pool_pages=st.n_pool, out=st.out[l], workspace=st.ws)
-            else:
-                ops.paged_decode_attention(q_d[l], st.k_base, st.v_base, st.page_table[l], st.page_used[l],
-                                           st.num_pages[l], num_kv_heads=st.Hkv, page_size=st.P,
-                                           page_stride=st.page_stride, head_stride=st.head_stride,
-                                           num_pool_pages=st.n_pool, out_record=st.rec[l], workspace=st.ws)
-                st.shard.gather_merge(st.rec[l], out=st.out[l].view(B * st.Hq, st.D))
-        out_h.copy_(st.out, non_blocking=True)
+        one_step()
     t1.record(stream)
     torch.cuda.synchronize(dev)
     ms = max_over_ranks(t0.elapsed_time(t1), world, dev) / steps
     return {"value": CFG["batch"] / (ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "api": "helm_b200.ops (C ABI per layer)"}
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms,
+            "api": "helm_b200.runtime.kv_offload._decode_batched per layer (KVCacheManager/KVAllocator state)"}
 
 
 def cpu_baseline():

@@ -158,18 +158,22 @@ class KVCacheManager:
         seq_len = K_prefill.size(2)
         page_size = self.allocator.page_size
         device = K_prefill.device
+        pending = _PrefillWrites(K_prefill, V_prefill)
         for start_idx in range(0, seq_len, page_size):
             chunk_len = min(page_size, seq_len - start_idx)
-            end_idx = start_idx + chunk_len
             page = self.allocator.allocate(device)
             page.layer_id = layer_id
             page.start_token = layer.total_tokens
             page.used_tokens = chunk_len
-            _write_tokens(page, 0, K_prefill[:, :, start_idx:end_idx, :], V_prefill[:, :, start_idx:end_idx, :])
+            pending.add(page, start_idx, chunk_len)
             self._append_page(layer, page)
             layer._version += 1
             layer.total_tokens += chunk_len
+            # An eviction copies pages out: their data must be written first.
+            if self._gpu_evictable_bytes() > self.gpu_high_watermark_bytes:
+                pending.flush()
             self._enforce_residency_policy()
+        pending.flush()
 
     def append_decode(self, layer_id: int, K_new: torch.Tensor, V_new: torch.Tensor,
                       skip_residency: bool = False):
@@ -383,6 +387,42 @@ class KVCacheManager:
                 elif page.state == "CPU":
                     cpu_bytes += page_bytes
         return {"gpu_active_bytes": gpu_bytes, "cpu_active_bytes": cpu_bytes}
+
+
+class _PrefillWrites:
+    """Prefill chunks waiting to be written: pages in consecutive slots of one store are written
+    with one copy per K and V (a fresh pool hands out consecutive slots), others one by one."""
+
+    def __init__(self, K: torch.Tensor, V: torch.Tensor):
+        self.K, self.V = K, V
+        self.items = []   # (page, start token in K, tokens)
+
+    def add(self, page, start: int, n: int) -> None:
+        self.items.append((page, start, n))
+
+    def flush(self) -> None:
+        items, self.items = self.items, []
+        i = 0
+        while i < len(items):
+            page, start, n = items[i]
+            j = i + 1
+            if page.has_store() and n == page.capacity_tokens:
+                P = n
+                while (j < len(items) and items[j][0].has_store() and items[j][0].store is page.store
+                       and items[j][0].slot == page.slot + (j - i) and items[j][2] == P
+                       and items[j][1] == start + (j - i) * P):
+                    j += 1
+            if j - i > 1:
+                run = j - i
+                st = page.store
+                Hkv, D = self.K.shape[1], self.K.shape[3]
+                src_k = self.K[0, :, start:start + run * P].reshape(Hkv, run, P, D).transpose(0, 1)
+                src_v = self.V[0, :, start:start + run * P].reshape(Hkv, run, P, D).transpose(0, 1)
+                st.slab[page.slot:page.slot + run, 0].copy_(src_k)
+                st.slab[page.slot:page.slot + run, 1].copy_(src_v)
+            else:
+                _write_tokens(page, 0, self.K[:, :, start:start + n, :], self.V[:, :, start:start + n, :])
+            i = j
 
 
 def _write_tokens(page: KVPage, idx: int, K: torch.Tensor, V: torch.Tensor) -> None:

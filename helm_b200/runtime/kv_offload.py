@@ -77,16 +77,25 @@ def _batch_of(kvcms):
     return batch
 
 
-def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float):
+def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float, *, shard=None):
     """Decode step shared by all architecture forward patches; returns [bsz, Hq, 1, D].
 
     Path selection follows the reference: (1) contiguous buffers while the sequence fits,
     else migrate them to pages; (2)/(3) paged, appending with skip_residency when every
-    page of the layer is GPU-resident (kv_offload.py:133-138)."""
+    page of the layer is GPU-resident (kv_offload.py:133-138).
+
+    shard (a KVShardGroup, multi-GPU only): the managers hold this rank's share of every
+    sequence's pages; only the last rank appends the new token, and the per-rank records are
+    exchanged and merged so that every rank returns the full attention output."""
     bsz = q.shape[0]
     if q.device.type != "cuda":
         raise RuntimeError("helm_b200 decode attention runs on CUDA devices only")
     batch = _batch_of(kvcms)
+    if shard is not None and shard.world > 1:
+        if batch is None or kvcms[0].use_contiguous:
+            raise RuntimeError("sharded decode needs a registered batch in paged mode (cont_capacity=0)")
+        all_gpu = all(kvcms[i].all_gpu_resident(layer_idx) for i in range(bsz))
+        return _decode_paged_batch(batch, layer_idx, q, k, v, scale, all_gpu, shard=shard)
 
     if kvcms[0].use_contiguous:
         if kvcms[0].cont_seq_len < kvcms[0].cont_capacity:
@@ -108,12 +117,40 @@ def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float):
     return torch.cat(outs, dim=0)
 
 
-def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_gpu: bool):
+def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_gpu: bool, shard=None):
     kvcms = batch.kvcms
     B = batch.B
     dev = q.device
     alloc = kvcms[0].allocator
     store = alloc.store(dev)
+    append = shard is None or shard.rank == shard.world - 1
+    if append:
+        _append_batch(batch, l, k, v, all_gpu, store, dev)
+    else:
+        for b, m in enumerate(kvcms):
+            layer = m.layers.get(l)
+            if layer is not None and not batch.in_sync(l, b) and not layer._n_off:
+                batch.sync_row(l, b)
+    mixed = any(m.layers[l]._n_off for m in kvcms if l in m.layers)
+    Hq, D = q.shape[1], q.shape[-1]
+    q3 = q.reshape(B, Hq, D)
+    if not q3.is_contiguous():
+        q3 = q3.contiguous()
+    out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
+    if shard is not None:
+        rec = batch.record_buffer(B * Hq, D)
+        _attend_batch(batch, l, q3, scale, store, mixed, out=None, out_record=rec)
+        shard.gather_merge(rec, out=out.view(B * Hq, D))
+    else:
+        _attend_batch(batch, l, q3, scale, store, mixed, out=out, out_record=None)
+    return out.reshape(B, Hq, 1, D)
+
+
+def _append_batch(batch: DecodeBatch, l: int, k, v, all_gpu: bool, store, dev):
+    """Host bookkeeping of append_decode for every sequence + one kernel writing the tokens and
+    their device page-table entries; rows changed structurally are re-uploaded."""
+    kvcms = batch.kvcms
+    B = batch.B
     reserved = []
     dest = batch.dest
     max_li = 0
@@ -140,31 +177,28 @@ def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_g
         m._commit_decode_slot(l, reserved[b], all_gpu)
     # The append mirrored the new token on the device; after a structural change (prefill,
     # eviction, clear) the row is rebuilt from the page list.
-    mixed = False
     for b, m in enumerate(kvcms):
         layer = m.layers[l]
         if in_sync[b] and batch.synced[l][b] == (id(layer), layer._version):
             continue
         if layer._n_off:
-            mixed = True
             continue
         batch.sync_row(l, b)
-    Hq, D = q.shape[1], q.shape[-1]
-    q3 = q.reshape(B, Hq, D)
-    if not q3.is_contiguous():
-        q3 = q3.contiguous()
-    out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
+
+
+def _attend_batch(batch: DecodeBatch, l: int, q3, scale, store, mixed: bool, out, out_record):
     if not mixed:
         k_base, v_base = store.base_ptrs()
         ops.paged_decode_attention(q3, k_base, v_base, batch.table[l], batch.used[l], batch.npages[l],
                                    num_kv_heads=store.Hkv, page_size=store.P, page_stride=store.page_elems,
                                    head_stride=store.head_stride, num_pool_pages=store.capacity, scale=scale,
-                                   max_pages=batch.width, out=out, error_flag=batch.error_flag)
-        return out.reshape(B, Hq, 1, D)
-    return _decode_mixed(batch, l, q3, scale, out, store).reshape(B, Hq, 1, D)
+                                   max_pages=batch.width, out=out, out_record=out_record,
+                                   error_flag=batch.error_flag)
+        return
+    _decode_mixed(batch, l, q3, scale, out, store, out_record=out_record)
 
 
-def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store):
+def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store, out_record=None):
     """Some pages of layer l live on the host: stage them into device slots and attend over a
     per-call table (the reference's Path 3, kv_cache.py:382-442)."""
     kvcms = batch.kvcms
@@ -201,7 +235,7 @@ def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store):
     ops.paged_decode_attention(q3, k_base, v_base, t, u, n, num_kv_heads=store.Hkv, page_size=store.P,
                                page_stride=store.page_elems, head_stride=store.head_stride,
                                num_pool_pages=store.capacity, scale=scale, max_pages=width, out=out,
-                               error_flag=batch.error_flag)
+                               out_record=out_record, error_flag=batch.error_flag)
     return out
 
 
@@ -312,10 +346,22 @@ def _attend_contiguous_single(q, K, V, n, scale):
 # Patched forwards (kv_offload.py:174-322)
 # ---------------------------------------------------------------------------------------------
 
-def _prefill(attn_self, kvcms, q, k, v, attention_mask, scale, k_exp, v_exp):
+def _shard_tokens(n_tokens: int, page_size: int, shard):
+    """Token range [lo, hi) of the prompt that this rank stores: its share of whole pages."""
+    if shard is None or shard.world == 1:
+        return 0, n_tokens
+    from .sharded import shard_bounds
+    npg = (n_tokens + page_size - 1) // page_size
+    plo, phi = shard_bounds(npg, shard.rank, shard.world)
+    return plo * page_size, min(phi * page_size, n_tokens)
+
+
+def _prefill(attn_self, kvcms, q, k, v, attention_mask, scale, k_exp, v_exp, shard=None):
     bsz = q.shape[0]
+    lo, hi = _shard_tokens(k.shape[2], kvcms[0].allocator.page_size, shard)
     for i in range(bsz):
-        kvcms[i].append_prefill(attn_self.layer_idx, k[i:i + 1], v[i:i + 1])
+        if hi > lo:
+            kvcms[i].append_prefill(attn_self.layer_idx, k[i:i + 1, :, lo:hi], v[i:i + 1, :, lo:hi])
         if kvcms[i].use_contiguous:
             kvcms[i].prefill_contiguous(attn_self.layer_idx, k[i:i + 1], v[i:i + 1])
     return F.scaled_dot_product_attention(
@@ -323,7 +369,7 @@ def _prefill(attn_self, kvcms, q, k, v, attention_mask, scale, k_exp, v_exp):
         dropout_p=attn_self.attention_dropout if attn_self.training else 0.0, scale=scale)
 
 
-def _make_qwen2_forward(kvcms):
+def _make_qwen2_forward(kvcms, shard=None):
     def forward(attn_self, hidden_states, position_embeddings, attention_mask=None, past_key_values=None,
                 cache_position=None, **kwargs):
         from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
@@ -338,15 +384,15 @@ def _make_qwen2_forward(kvcms):
         groups = q.shape[1] // k.shape[1]
         if q_len > 1:
             out = _prefill(attn_self, kvcms, q, k, v, attention_mask, scale,
-                           k.repeat_interleave(groups, dim=1), v.repeat_interleave(groups, dim=1))
+                           k.repeat_interleave(groups, dim=1), v.repeat_interleave(groups, dim=1), shard)
         else:
-            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale)
+            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale, shard=shard)
         out = out.transpose(1, 2).contiguous().reshape(bsz, q_len, -1)
         return attn_self.o_proj(out), None
     return forward
 
 
-def _make_qwen3_forward(kvcms):
+def _make_qwen3_forward(kvcms, shard=None):
     def forward(attn_self, hidden_states, position_embeddings, attention_mask=None, past_key_values=None,
                 cache_position=None, **kwargs):
         from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb, repeat_kv
@@ -360,15 +406,16 @@ def _make_qwen3_forward(kvcms):
         scale = 1.0 / math.sqrt(attn_self.head_dim)
         if q_len > 1:
             out = _prefill(attn_self, kvcms, q, k, v, attention_mask, scale,
-                           repeat_kv(k, attn_self.num_key_value_groups), repeat_kv(v, attn_self.num_key_value_groups))
+                           repeat_kv(k, attn_self.num_key_value_groups), repeat_kv(v, attn_self.num_key_value_groups),
+                           shard)
         else:
-            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale)
+            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale, shard=shard)
         out = out.transpose(1, 2).contiguous().reshape(bsz, q_len, -1)
         return attn_self.o_proj(out), None
     return forward
 
 
-def _make_llama_forward(kvcms):
+def _make_llama_forward(kvcms, shard=None):
     def forward(attn_self, hidden_states, position_embeddings, attention_mask=None, past_key_values=None,
                 cache_position=None, **kwargs):
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
@@ -383,9 +430,9 @@ def _make_llama_forward(kvcms):
         groups = q.shape[1] // k.shape[1]
         if q_len > 1:
             out = _prefill(attn_self, kvcms, q, k, v, attention_mask, scale,
-                           k.repeat_interleave(groups, dim=1), v.repeat_interleave(groups, dim=1))
+                           k.repeat_interleave(groups, dim=1), v.repeat_interleave(groups, dim=1), shard)
         else:
-            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale)
+            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale, shard=shard)
         out = out.transpose(1, 2).contiguous().reshape(bsz, q_len, -1)
         return attn_self.o_proj(out), None
     return forward
@@ -400,9 +447,15 @@ class KVOffloadManager:
     One KVCacheManager per batch item, all sharing one KVAllocator; the batch's page tables
     live on the device (DecodeBatch)."""
 
-    def __init__(self, model, config: KVOffloadConfig, batch_size: int = 1):
+    def __init__(self, model, config: KVOffloadConfig, batch_size: int = 1, shard_group=None):
+        """shard_group (a KVShardGroup; extension, multi-GPU only): store this rank's share of every
+        sequence's KV pages and merge the ranks' attention records on each decode step.  Requires
+        config.cont_capacity == 0 (paged mode)."""
         self.config = config
         self.batch_size = batch_size
+        self.shard_group = shard_group
+        if shard_group is not None and shard_group.world > 1 and config.cont_capacity > 0:
+            raise ValueError("KVOffloadManager: sharded decode needs cont_capacity=0")
         self.allocator = KVAllocator(num_layers=config.num_layers, num_kv_heads=config.num_kv_heads,
                                      head_dim=config.head_dim, page_size=config.page_size, dtype=config.dtype)
         watermark_per_item = max(config.gpu_watermark_bytes // batch_size, 1)
@@ -462,13 +515,13 @@ class KVOffloadManager:
     def _patch(self, arch: str):
         if arch == "qwen2":
             import transformers.models.qwen2.modeling_qwen2 as m
-            cls, new_fwd = m.Qwen2Attention, _make_qwen2_forward(self.kvcms)
+            cls, new_fwd = m.Qwen2Attention, _make_qwen2_forward(self.kvcms, self.shard_group)
         elif arch == "qwen3":
             import transformers.models.qwen3.modeling_qwen3 as m
-            cls, new_fwd = m.Qwen3Attention, _make_qwen3_forward(self.kvcms)
+            cls, new_fwd = m.Qwen3Attention, _make_qwen3_forward(self.kvcms, self.shard_group)
         elif arch == "llama":
             import transformers.models.llama.modeling_llama as m
-            cls, new_fwd = m.LlamaAttention, _make_llama_forward(self.kvcms)
+            cls, new_fwd = m.LlamaAttention, _make_llama_forward(self.kvcms, self.shard_group)
         else:
             raise ValueError(arch)
         self._patched[arch] = (cls, cls.forward)

@@ -182,6 +182,7 @@ class DecodeBatch:
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.dest = np.zeros((self.B, 3), dtype=np.int32)
         self.cont = None          # ContiguousBatch when the contiguous fast path is active
+        self._rec = None
         for i, m in enumerate(self.kvcms):
             m._batch = (self, i)
 
@@ -217,6 +218,12 @@ class DecodeBatch:
             return
         self._upload_row(l, b, [p.slot for p in layer.pages], [p.used_tokens for p in layer.pages])
         self.synced[l][b] = (id(layer), layer._version)
+
+    def record_buffer(self, rows: int, D: int) -> torch.Tensor:
+        """Scratch [rows, D+2] fp32 for the per-rank attention record of sharded decode."""
+        if self._rec is None or tuple(self._rec.shape) != (rows, D + 2):
+            self._rec = torch.empty((rows, D + 2), dtype=torch.float32, device=self.device)
+        return self._rec
 
     def in_sync(self, l: int, b: int) -> bool:
         layer = self.kvcms[b].layers.get(l)
