@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
-    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+    ap.add_argument("--exchange", default="fused", choices=["fused", "p2p", "nccl"],
                     help="cross-GPU record exchange for N > 1")
     # Smaller stacks for ncu captures only; the reported workload is config 5 unless these are set.
     ap.add_argument("--layers", type=int, default=None)
@@ -208,7 +208,7 @@ class Stack:
     device slab holds every page, one KVCacheManager per sequence (prefilled through
     append_prefill) and the batch's device page tables (DecodeBatch)."""
 
-    def __init__(self, rank, world, dev, spare_pages, exchange="p2p"):
+    def __init__(self, rank, world, dev, spare_pages, exchange="fused"):
         from helm_b200 import ops
         from helm_b200.runtime import KVAllocator, KVCacheManager
         from helm_b200.runtime.paged import DecodeBatch
@@ -257,6 +257,7 @@ class Stack:
         if world > 1:
             from helm_b200.runtime.sharded import KVShardGroup
             self.shard = KVShardGroup(rows, self.D, dev, exchange=exchange)
+        self.fused = self.shard is not None and self.shard.fused
         self.k_base, self.v_base = self.store.base_ptrs()
         self.page_stride = self.store.page_elems
         self.head_stride = self.store.head_stride
@@ -274,8 +275,11 @@ class Stack:
                 self.q[l], self.k_base, self.v_base, bt.table[l], bt.used[l], bt.npages[l],
                 num_kv_heads=self.Hkv, page_size=self.P, page_stride=self.page_stride,
                 head_stride=self.head_stride, num_pool_pages=self.n_pool, max_pages=bt.width,
-                out=self.out[l] if self.world == 1 else None,
-                out_record=self.rec[l] if self.world > 1 else None, error_flag=self.error_flag)
+                out=self.out[l] if (self.world == 1 or self.fused) else None,
+                out_record=self.rec[l] if (self.world > 1 and not self.fused) else None,
+                error_flag=self.error_flag)
+            if self.fused:
+                p.exchange = self.shard.xparams_ptr
             S = ctypes.c_int32(0)
             need = self.lib.helm_paged_attn_workspace_bytes(ctypes.byref(p), ctypes.byref(S))
             p.num_splits = S.value
@@ -293,7 +297,8 @@ class Stack:
         for p in self.attn_params:
             p.workspace = self.ws.data_ptr()
             p.workspace_bytes = self.ws.numel() * 4
-        per_layer = (1 if self.tail else 0) + 1 + (1 if self.splits > 1 else 0) + (1 if self.world > 1 else 0)
+        per_layer = (1 if self.tail else 0) + 1 + (1 if self.splits > 1 else 0) + \
+            (1 if (self.world > 1 and not self.fused) else 0)
         self.launches_per_step = self.L * per_layer
 
     def attn_bytes(self, tokens_per_seq):
@@ -318,7 +323,7 @@ class Stack:
             if self.tail:
                 N.check("helm_kv_append", self.lib.helm_kv_append(ctypes.byref(self.append_params[l]), sp))
             N.check("helm_paged_attn_decode", self.lib.helm_paged_attn_decode(ctypes.byref(self.attn_params[l]), sp))
-            if self.world > 1:
+            if self.world > 1 and not self.fused:
                 self.shard.gather_merge(self.rec[l], out=self.out[l].view(self.B * self.Hq, self.D))
 
 
@@ -327,7 +332,7 @@ def run_helm(args, rank, local, world):
     torch.cuda.set_device(dev)
     dist = init_pg(world, local)
     c = CFG
-    total_steps = args.warmup + args.steps + 8
+    total_steps = args.warmup + args.steps + 16
     spare = (total_steps + c["page"] - 1) // c["page"] + 1
     st = Stack(rank, world, dev, spare, exchange=args.exchange)
     stream = torch.cuda.current_stream(dev)
@@ -379,6 +384,7 @@ def run_helm(args, rank, local, world):
         if rep:
             attn_ms += [a.elapsed_time(b) for a, b in evs]
     attn_avg_ms = sum(attn_ms) / len(attn_ms)
+    breakdown = component_breakdown(st, stream, world, dev)
     err = int(st.error_flag.item())
     del graph
 
@@ -417,6 +423,7 @@ def run_helm(args, rank, local, world):
                          "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind,
                          "kernel": "attn_tc_persistent_kernel (one helm_paged_attn_decode call: counter memset + kernel)",
                          "bytes_per_launch": bytes_launch, "avg_launch_ms": attn_avg_ms},
+            "breakdown_ms_per_layer": breakdown,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": st.launches_per_step * args.steps,
@@ -429,6 +436,38 @@ def run_helm(args, rank, local, world):
         st.shard.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def component_breakdown(st, stream, world, dev, reps=3):
+    """Per-layer device time of each part of a decode step (append, attention, exchange + merge),
+    from CUDA events around each launch in an eager pass; max over ranks of the mean."""
+    from helm_b200 import _native as N
+    sums = [0.0, 0.0, 0.0]
+    n = 0
+    for rep in range(reps):
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(st.L)]
+        barrier(world)
+        for l in range(st.L):
+            e = evs[l]
+            e[0].record(stream)
+            if st.tail:
+                N.check("helm_kv_append", st.lib.helm_kv_append(ctypes.byref(st.append_params[l]), stream.cuda_stream))
+            e[1].record(stream)
+            st.attend(l, stream)
+            e[2].record(stream)
+            if world > 1 and not st.fused:
+                st.shard.gather_merge(st.rec[l], out=st.out[l].view(st.B * st.Hq, st.D))
+            e[3].record(stream)
+        torch.cuda.synchronize(dev)
+        if rep == 0:
+            continue
+        for e in evs:
+            sums[0] += e[0].elapsed_time(e[1])
+            sums[1] += e[1].elapsed_time(e[2])
+            sums[2] += e[2].elapsed_time(e[3])
+            n += 1
+    out = {k: max_over_ranks(v / n, world, dev) for k, v in zip(("append", "attention", "exchange_merge"), sums)}
+    return {k: round(v, 4) for k, v in out.items()}
 
 
 def run_e2e(st, stream, steps, world, dev):

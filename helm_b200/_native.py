@@ -14,7 +14,7 @@ import pathlib
 LIB_PATH = pathlib.Path(os.environ.get(
     "HELM_B200_LIB", pathlib.Path(__file__).resolve().parent / "lib" / "libhelm_b200.so"))
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # helm_dtype
 F32, F16, BF16, I8 = 0, 1, 2, 3
@@ -31,6 +31,17 @@ _i32 = ctypes.c_int32
 _i64 = ctypes.c_int64
 
 
+MAX_RANKS = 8
+
+
+class ShardExchange(ctypes.Structure):
+    _fields_ = [
+        ("rank", _i32), ("world", _i32),
+        ("peer_recv", _p * MAX_RANKS), ("peer_flags", _p * MAX_RANKS),
+        ("recv_local", _p), ("flags_local", _p), ("counters", _p),
+    ]
+
+
 class PagedAttnParams(ctypes.Structure):
     _fields_ = [
         ("q", _p), ("k_base", _p), ("v_base", _p),
@@ -45,6 +56,7 @@ class PagedAttnParams(ctypes.Structure):
         ("workspace", _p), ("workspace_bytes", _i64),
         ("out", _p), ("out_record", _p),
         ("error_flag", _p),
+        ("exchange", _c.POINTER(ShardExchange)),
     ]
 
 
@@ -60,9 +72,6 @@ class KVAppendParams(ctypes.Structure):
         ("spare_pages", _p), ("spare_next", _p), ("spare_stride", _i32),
         ("error_flag", _p),
     ]
-
-
-MAX_RANKS = 8
 
 
 class GatherMergeParams(ctypes.Structure):
@@ -91,6 +100,8 @@ SIGNATURES = [
     ("helm_ipc_export", _c.c_int, [_p, _p, _c.POINTER(_i64)]),
     ("helm_ipc_import", _c.c_int, [_p, _i64, _c.POINTER(_p), _c.POINTER(_p)]),
     ("helm_ipc_close", _c.c_int, [_p]),
+    ("helm_shard_exchange_bytes", _i64, [_i32, _i32, _i32, _c.POINTER(_i64), _c.POINTER(_i64),
+                                          _c.POINTER(_i64)]),
 ]
 
 _lib = None

@@ -48,8 +48,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
   return v;
 }
 
-__device__ __forceinline__ void red_release_sys_add(uint32_t *p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_relaxed_sys_add(uint32_t *p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ uint64_t now_ns() {
@@ -72,20 +72,30 @@ __global__ void __launch_bounds__(kThreads) gather_merge_kernel(GatherArgs a) {
     s_ok = 1;
   }
   __syncthreads();
-  // 1) push this rank's rows into every rank's receive slot (sent parity, source = this rank)
+  // 1) push this rank's rows into every rank's receive slot (sent parity, source = this rank);
+  //    16-byte stores when the block is 16-byte aligned (rows*(D+2) floats per block)
   const int n = nrows * rl;
   const float *src = a.record + (int64_t)row0 * rl;
   const uint32_t slot = s_sent & 1u;
+  const bool vec = ((n & 3) == 0) && ((((int64_t)row0 * rl) & 3) == 0) && ((((int64_t)a.rows * rl) & 3) == 0);
   for (int dst = 0; dst < G; ++dst) {
     float *d = a.recv[dst] + (((int64_t)slot * G + a.rank) * a.rows + row0) * rl;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = src[i];
+    if (vec) {
+      const float4 *s4 = reinterpret_cast<const float4 *>(src);
+      float4 *d4 = reinterpret_cast<float4 *>(d);
+      for (int i = threadIdx.x; i < n / 4; i += blockDim.x) d4[i] = s4[i];
+    } else {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) d[i] = src[i];
+    }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  // Publish: after the barrier, one thread per destination fences at system scope (making the
+  // whole block's stores visible) and bumps that destination's counter.
+  if (threadIdx.x < G) {
     __threadfence_system();
-    for (int dst = 0; dst < G; ++dst) red_release_sys_add(a.flags[dst] + a.rank * a.nblocks + rb, 1u);
-    a.sent[rb] = s_sent + 1;
+    red_relaxed_sys_add(a.flags[threadIdx.x] + a.rank * a.nblocks + rb, 1u);
   }
+  if (threadIdx.x == 0) a.sent[rb] = s_sent + 1;
   // 2) wait until every source's counter for this block covers the call we consume next
   if (threadIdx.x < G) {
     const int s = threadIdx.x;

@@ -663,7 +663,27 @@ struct PersistArgs {
   float *rec_ml;       // [C + pairs][gq][2]: its (m, l)
   uint32_t *counter;   // [pairs], zero at launch
   int C;               // grid size
+  // fused cross-GPU exchange (xworld > 1); records of stride D + 4 floats: o[D], m, l, pad
+  int xrank, xworld;
+  float *xrecv[HELM_MAX_RANKS];     // [2][G][B*Hq][D+4] of each rank
+  uint32_t *xflags[HELM_MAX_RANKS]; // [G][pairs] of each rank
+  float *xrecv_local;
+  uint32_t *xflags_local;
+  uint32_t *xsent;                  // [pairs]
+  uint32_t *xseen;                  // [G][pairs]
 };
+
+constexpr uint64_t kExchangeWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_relaxed_sys_add_u32(uint32_t *p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // CTA owning unit u when U units are split over C CTAs as [c*U/C, (c+1)*U/C).
 __device__ __forceinline__ int owner_cta(int64_t u, int64_t U, int C) {
@@ -691,6 +711,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   __shared__ float mg_M[HN], mg_L[HN], mg_A[HN];
   __shared__ int pending[kMaxPending];
   __shared__ int npending;
+  __shared__ uint32_t xs_slot, xs_src_slot[HELM_MAX_RANKS];
+  __shared__ int xs_ok;
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int c = blockIdx.x;
@@ -867,6 +889,104 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
     reset_state();
 
+    // Emits pair (b, g) from its rank-local record: mg_M / mg_L (per head) and acc (this thread's
+    // float4 slice of o).  With the exchange on, the record first goes to every rank and the G
+    // records are merged in rank order.
+    auto exchange_emit = [&](int pair, int b, int g, const float4 (&acc)[HN / 4]) {
+      constexpr int F4x = HN / 4;
+      if (pa.xworld <= 1) {
+#pragma unroll
+        for (int e = 0; e < F4x; ++e) {
+          const int idx4 = tid + e * kConsumerWarps * 32;
+          if (idx4 < gq * (D / 4)) {
+            const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
+            const float M = mg_M[h];
+            const float L = M == -INFINITY ? 0.f : mg_L[h];
+            const float vals[4] = {acc[e].x, acc[e].y, acc[e].z, acc[e].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) emit(a, 0, b, g * gq + h, d + j, M, L, M == -INFINITY ? 0.f : vals[j]);
+          }
+        }
+        return;
+      }
+      const int G = pa.xworld, R = pa.xrank;
+      const int rows = B * a.Hq, pairs = B * Hkv;
+      constexpr int XL = D + 4;
+      if (tid == 0) {
+        xs_slot = pa.xsent[pair] & 1u;
+        xs_ok = 1;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+      const uint32_t slot = xs_slot;
+      for (int dst = 0; dst < G; ++dst) {
+#pragma unroll
+        for (int e = 0; e < F4x; ++e) {
+          const int idx4 = tid + e * kConsumerWarps * 32;
+          if (idx4 < gq * (D / 4)) {
+            const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
+            const float M = mg_M[h];
+            const bool empty = M == -INFINITY;
+            float *dst_row = pa.xrecv[dst] + (((int64_t)slot * G + R) * rows + (int64_t)b * a.Hq + g * gq + h) * XL;
+            *reinterpret_cast<float4 *>(dst_row + d) = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc[e];
+            if (d == 0) *reinterpret_cast<float2 *>(dst_row + D) = make_float2(M, empty ? 0.f : mg_L[h]);
+          }
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+      if (tid < G) {
+        __threadfence_system();
+        red_relaxed_sys_add_u32(pa.xflags[tid] + R * pairs + pair, 1u);
+        const uint32_t want = pa.xseen[tid * pairs + pair] + 1;
+        const uint32_t *f = pa.xflags_local + tid * pairs + pair;
+        bool ok = ld_acquire_sys_u32(f) >= want;
+        if (!ok) {
+          const uint64_t t0 = global_ns();
+          while (!(ok = ld_acquire_sys_u32(f) >= want))
+            if (global_ns() - t0 > kExchangeWaitNs) break;
+        }
+        if (!ok) {
+          flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+          atomicExch(&xs_ok, 0);
+        }
+        xs_src_slot[tid] = (want - 1) & 1u;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+      __threadfence();
+#pragma unroll
+      for (int e = 0; e < F4x; ++e) {
+        const int idx4 = tid + e * kConsumerWarps * 32;
+        if (idx4 < gq * (D / 4)) {
+          const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
+          const int64_t row = (int64_t)b * a.Hq + g * gq + h;
+          float M = -INFINITY;
+          for (int t = 0; t < G; ++t) {
+            const float *rr = pa.xrecv_local + (((int64_t)xs_src_slot[t] * G + t) * rows + row) * XL;
+            M = fmaxf(M, __ldcg(rr + D));
+          }
+          float L = 0.f;
+          float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int t = 0; t < G; ++t) {
+            const float *rr = pa.xrecv_local + (((int64_t)xs_src_slot[t] * G + t) * rows + row) * XL;
+            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(rr + D));
+            const float w = rescale_weight(ml.x, M);
+            L = fmaf(ml.y, w, L);
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(rr + d));
+            O.x = fmaf(v.x, w, O.x);
+            O.y = fmaf(v.y, w, O.y);
+            O.z = fmaf(v.z, w, O.z);
+            O.w = fmaf(v.w, w, O.w);
+          }
+          const bool none = M == -INFINITY || !xs_ok;
+          const float vals[4] = {O.x, O.y, O.z, O.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) emit(a, 0, b, g * gq + h, d + j, M, none ? 0.f : L, none ? 0.f : vals[j]);
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+      if (tid < G) pa.xseen[tid * pairs + pair] += 1;
+      if (tid == 0) pa.xsent[pair] += 1;
+    };
+
     const int64_t n_units = u1 - u0;
     for (int64_t i = 0; i < n_units; ++i) {
       const int st = (int)(i % kStages);
@@ -1034,6 +1154,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     // ---- deferred merges: pairs whose last CTA record this CTA wrote ----
+    constexpr int F4 = HN / 4;  // float4 elements per thread: HN*D/4/128
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
     __threadfence();
     const int np = npending;
@@ -1045,7 +1166,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int nrec = c1 - c0 + 1;
       const float *ro = pa.rec_o + (int64_t)(c0 + pair) * gq * D;    // CTA c0+j: + j*gq*D
       const float *rml = pa.rec_ml + (int64_t)(c0 + pair) * gq * 2;  // CTA c0+j: + j*gq*2
-      constexpr int F4 = HN / 4;  // float4 elements per thread: HN*D/4/128
       float4 acc[F4];
 #pragma unroll
       for (int e = 0; e < F4; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1111,30 +1231,26 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
       }
+      exchange_emit(pair, b, g, acc);
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    }
+    // Sequences without pages on this rank: an empty record (zeros when not exchanging).
+    for (int pq = c; pq < B * Hkv; pq += gridDim.x) {
+      const int b = pq / Hkv, g = pq - b * Hkv;
+      if (seq_pages[b] != 0) continue;
+      float4 acc[F4];
 #pragma unroll
-      for (int e = 0; e < F4; ++e) {
-        const int idx4 = tid + e * kConsumerWarps * 32;
-        if (idx4 < gq * (D / 4)) {
-          const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
-          const float M = mg_M[h];
-          const float L = M == -INFINITY ? 0.f : mg_L[h];
-          const float vals[4] = {acc[e].x, acc[e].y, acc[e].z, acc[e].w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) emit(a, 0, b, g * gq + h, d + j, M, L, M == -INFINITY ? 0.f : vals[j]);
-        }
+      for (int e = 0; e < F4; ++e) acc[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (tid < HN) {
+        mg_M[tid] = -INFINITY;
+        mg_L[tid] = 0.f;
       }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+      exchange_emit(pq, b, g, acc);
       asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
     }
   }
 
-  // Sequences without pages: zero output (no CTA holds a unit of theirs).
-  if (warp < kConsumerWarps)
-    for (int pq = c; pq < B * Hkv; pq += gridDim.x) {
-      const int b = pq / Hkv, g = pq - b * Hkv;
-      if (seq_pages[b] != 0) continue;
-      for (int idx = tid; idx < gq * D; idx += kConsumerWarps * 32)
-        emit(a, 0, b, g * gq + idx / D, idx % D, -INFINITY, 0.f, 0.f);
-    }
 }
 
 }  // namespace tc
@@ -1359,6 +1475,18 @@ int validate(const helm_paged_attn_params *p) {
     return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: max_pages %d > page_table_stride %d", p->max_pages,
                 p->page_table_stride);
   if (p->num_splits < 0) return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: negative num_splits");
+  if (p->exchange && p->exchange->world > 1) {
+    const helm_shard_exchange *x = p->exchange;
+    if (x->world > HELM_MAX_RANKS || x->rank < 0 || x->rank >= x->world)
+      return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: bad exchange rank %d / world %d", x->rank, x->world);
+    if (!x->recv_local || !x->flags_local || !x->counters)
+      return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: exchange buffers missing");
+    for (int r = 0; r < x->world; ++r)
+      if (!x->peer_recv[r] || !x->peer_flags[r])
+        return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: exchange peer %d missing", r);
+    if (p->num_splits != 0)
+      return fail(HELM_ERR_UNSUPPORTED, "paged_attn: the fused exchange needs num_splits == 0");
+  }
   return HELM_OK;
 }
 
@@ -1447,6 +1575,10 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
     a.out_record = p->out_record;
   }
 
+  if (p->exchange && p->exchange->world > 1 && !pl.persistent)
+    return fail(HELM_ERR_UNSUPPORTED,
+                "paged_attn: the fused exchange needs the persistent kernel (bf16/fp16 q == kv, D=128, P=64, "
+                "num_splits=0, B <= 512)");
   if (eligible) {
     CUtensorMap mk, mv;
     if (!make_pool_map(&mk, p->k_base, p->kv_dtype, p) || !make_pool_map(&mv, p->v_base, p->kv_dtype, p))
@@ -1458,6 +1590,21 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
       pa.rec_ml = reinterpret_cast<float *>(reinterpret_cast<char *>(p->workspace) + pl.ml_off);
       pa.counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(p->workspace) + pl.counter_off);
       pa.C = pl.C;
+      pa.xrank = 0;
+      pa.xworld = 0;
+      if (p->exchange && p->exchange->world > 1) {
+        const helm_shard_exchange *x = p->exchange;
+        pa.xrank = x->rank;
+        pa.xworld = x->world;
+        for (int r = 0; r < x->world; ++r) {
+          pa.xrecv[r] = x->peer_recv[r];
+          pa.xflags[r] = x->peer_flags[r];
+        }
+        pa.xrecv_local = x->recv_local;
+        pa.xflags_local = x->flags_local;
+        pa.xsent = x->counters;
+        pa.xseen = x->counters + (int64_t)p->B * p->Hq;
+      }
       cudaError_t e = cudaMemsetAsync(pa.counter, 0, (size_t)p->B * p->Hkv * sizeof(uint32_t), st);
       if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: cudaMemsetAsync: %s", cudaGetErrorString(e));
       a.rec = nullptr;
@@ -1563,4 +1710,22 @@ extern "C" int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, v
     q.workspace_bytes = cap;
   }
   return helm_paged_attn_decode(&q, stream);
+}
+
+extern "C" int64_t helm_shard_exchange_bytes(int32_t world, int32_t rows, int32_t D, int64_t *recv_bytes_out,
+                                             int64_t *flags_bytes_out, int64_t *counters_bytes_out) {
+  using namespace helm;
+  if (world < 1 || world > HELM_MAX_RANKS || rows < 0 || D <= 0) {
+    fail(HELM_ERR_INVALID_ARGUMENT, "shard_exchange_bytes: bad sizes world=%d rows=%d D=%d", world, rows, D);
+    return -1;
+  }
+  // receive slots [2][G][rows][D+4] floats; flags [G][rows] (>= [G][pairs]); counters sent[rows] +
+  // seen[G][rows].
+  const int64_t recv = 2ll * world * rows * (D + 4) * (int64_t)sizeof(float);
+  const int64_t flags = (int64_t)world * rows * (int64_t)sizeof(uint32_t);
+  const int64_t counters = (1 + (int64_t)world) * rows * (int64_t)sizeof(uint32_t);
+  if (recv_bytes_out) *recv_bytes_out = recv;
+  if (flags_bytes_out) *flags_bytes_out = flags;
+  if (counters_bytes_out) *counters_bytes_out = counters;
+  return recv + flags + counters;
 }

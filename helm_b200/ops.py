@@ -105,13 +105,14 @@ def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.
                            out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                            out_record: Optional[torch.Tensor] = None,
                            error_flag: Optional[torch.Tensor] = None,
-                           workspace: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+                           workspace: Optional[torch.Tensor] = None, exchange=None) -> Optional[torch.Tensor]:
     """Single-query attention of q [B, Hq, D] over paged K/V (see helm_paged_attn_decode).
 
     ``page_table``/``page_used`` are int32 [B, max_pages] and ``num_pages``
     int32 [B], all on q's device.  Returns ``out`` [B, Hq, D] (allocated in
     ``out_dtype``, default q.dtype, unless given), or None when only
-    ``out_record`` is requested.
+    ``out_record`` is requested.  ``exchange``: a ctypes pointer to a ShardExchange (KV sequence
+    sharding with the cross-GPU exchange fused into the kernel).
     """
     dev = _need_cuda("paged_decode_attention", q, k_base, v_base, page_table, page_used, num_pages)
     if not q.is_contiguous() or q.dim() != 3:
@@ -129,6 +130,8 @@ def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.
                          page_size=page_size, page_stride=page_stride, head_stride=head_stride,
                          num_pool_pages=num_pool_pages, scale=scale, max_pages=max_pages, num_splits=num_splits,
                          out=out, out_record=out_record, error_flag=error_flag)
+    if exchange is not None:
+        p.exchange = exchange
     lib = N.lib()
     S = ctypes.c_int32(0)
     need = lib.helm_paged_attn_workspace_bytes(ctypes.byref(p), ctypes.byref(S))

@@ -19,6 +19,7 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
+from .. import _native as N
 from .. import ops
 from .kv_allocator import KVAllocator
 from .kv_cache import KVCacheManager, perform_streaming_attention
@@ -137,6 +138,15 @@ def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_g
     if not q3.is_contiguous():
         q3 = q3.contiguous()
     out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
+    if shard is not None and shard.fused and not getattr(shard, "_fused_unsupported", False):
+        try:
+            _attend_batch(batch, l, q3, scale, store, mixed, out=out, out_record=None,
+                          exchange=shard.xparams_ptr)
+            return out.reshape(B, Hq, 1, D)
+        except N.HelmError as e:
+            if e.code != N.ERR_UNSUPPORTED:
+                raise
+            shard._fused_unsupported = True   # e.g. fp32 pages: exchange as a separate kernel
     if shard is not None:
         rec = batch.record_buffer(B * Hq, D)
         _attend_batch(batch, l, q3, scale, store, mixed, out=None, out_record=rec)
@@ -186,19 +196,19 @@ def _append_batch(batch: DecodeBatch, l: int, k, v, all_gpu: bool, store, dev):
         batch.sync_row(l, b)
 
 
-def _attend_batch(batch: DecodeBatch, l: int, q3, scale, store, mixed: bool, out, out_record):
+def _attend_batch(batch: DecodeBatch, l: int, q3, scale, store, mixed: bool, out, out_record, exchange=None):
     if not mixed:
         k_base, v_base = store.base_ptrs()
         ops.paged_decode_attention(q3, k_base, v_base, batch.table[l], batch.used[l], batch.npages[l],
                                    num_kv_heads=store.Hkv, page_size=store.P, page_stride=store.page_elems,
                                    head_stride=store.head_stride, num_pool_pages=store.capacity, scale=scale,
                                    max_pages=batch.width, out=out, out_record=out_record,
-                                   error_flag=batch.error_flag)
+                                   error_flag=batch.error_flag, exchange=exchange)
         return
-    _decode_mixed(batch, l, q3, scale, out, store, out_record=out_record)
+    _decode_mixed(batch, l, q3, scale, out, store, out_record=out_record, exchange=exchange)
 
 
-def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store, out_record=None):
+def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store, out_record=None, exchange=None):
     """Some pages of layer l live on the host: stage them into device slots and attend over a
     per-call table (the reference's Path 3, kv_cache.py:382-442)."""
     kvcms = batch.kvcms
@@ -235,7 +245,7 @@ def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store, out_record=
     ops.paged_decode_attention(q3, k_base, v_base, t, u, n, num_kv_heads=store.Hkv, page_size=store.P,
                                page_stride=store.page_elems, head_stride=store.head_stride,
                                num_pool_pages=store.capacity, scale=scale, max_pages=width, out=out,
-                               out_record=out_record, error_flag=batch.error_flag)
+                               out_record=out_record, error_flag=batch.error_flag, exchange=exchange)
     return out
 
 

@@ -7,10 +7,14 @@ over its pages into a merged record (o, m, l) per (sequence, query head), and
 KVShardGroup.gather_merge exchanges those records and merges them so every
 rank ends with the same attention output.
 
-Two exchanges are provided:
-* "p2p" (default): helm_gather_merge -- one kernel that stores the records
-  into every rank's receive buffer over NVLink (CUDA IPC mappings) and merges
-  them; no NCCL call on the decode path;
+Three exchanges are provided:
+* "fused" (default): inside the attention kernel itself (helm_paged_attn_decode
+  with params.exchange): the CTA that completes a (sequence, kv head) pair
+  stores the pair's record into every rank's receive buffer over NVLink (CUDA
+  IPC mappings), waits for the other ranks' records and merges them -- the
+  collective overlaps the tail of the attention, and no extra launch runs;
+* "p2p": helm_gather_merge, the same exchange as a separate kernel after the
+  attention (used when the attention cannot run the persistent kernel);
 * "nccl": torch.distributed.all_gather_into_tensor + helm_lse_merge.
 """
 from __future__ import annotations
@@ -32,7 +36,7 @@ def shard_bounds(n: int, rank: int, world: int) -> Tuple[int, int]:
 
 
 class KVShardGroup:
-    def __init__(self, rows: int, head_dim: int, device, group=None, exchange: str = "p2p"):
+    def __init__(self, rows: int, head_dim: int, device, group=None, exchange: str = "fused"):
         import torch.distributed as dist
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -43,48 +47,76 @@ class KVShardGroup:
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._bases = []
         self.params = None
+        self.xparams_ptr = None
         if self.world > N.MAX_RANKS:
             raise ValueError(f"KVShardGroup: at most {N.MAX_RANKS} ranks")
         if exchange == "nccl" or self.world == 1:
             self.gathered = torch.empty((self.world, rows, head_dim + 2), dtype=torch.float32, device=self.device)
             return
-        if exchange != "p2p":
+        if exchange not in ("p2p", "fused"):
             raise ValueError(f"unknown exchange {exchange!r}")
         lib = N.lib()
+        # state of the separate exchange kernel (helm_gather_merge) ...
         rb, fb, cb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
         if lib.helm_gather_merge_state_bytes(self.world, rows, head_dim, ctypes.byref(rb), ctypes.byref(fb),
                                              ctypes.byref(cb)) < 0:
             N.check("helm_gather_merge_state_bytes", N.ERR_INVALID_ARGUMENT)
-        self.recv_bytes = rb.value
-        # receive slots + flags in one allocation (shared with the peers), counters local
+        # ... and of the exchange fused into the attention kernel
+        xr, xf, xc = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        if lib.helm_shard_exchange_bytes(self.world, rows, head_dim, ctypes.byref(xr), ctypes.byref(xf),
+                                         ctypes.byref(xc)) < 0:
+            N.check("helm_shard_exchange_bytes", N.ERR_INVALID_ARGUMENT)
+        # receive slots + flags in one allocation each (shared with the peers), counters local
         self.buf = torch.zeros(rb.value + fb.value, dtype=torch.uint8, device=self.device)
         self.counters = torch.zeros(max(cb.value, 4), dtype=torch.uint8, device=self.device)
+        self.xbuf = torch.zeros(xr.value + xf.value, dtype=torch.uint8, device=self.device)
+        self.xcounters = torch.zeros(max(xc.value, 4), dtype=torch.uint8, device=self.device)
         torch.cuda.synchronize(self.device)
-        handle = (ctypes.c_char * 64)()
-        off = ctypes.c_int64()
-        N.check("helm_ipc_export", lib.helm_ipc_export(self.buf.data_ptr(), handle, ctypes.byref(off)))
+        mine = []
+        for t in (self.buf, self.xbuf):
+            handle = (ctypes.c_char * 64)()
+            off = ctypes.c_int64()
+            N.check("helm_ipc_export", lib.helm_ipc_export(t.data_ptr(), handle, ctypes.byref(off)))
+            mine.append((bytes(handle), off.value))
         infos = [None] * self.world
-        dist.all_gather_object(infos, (bytes(handle), off.value), group=group)
-        p = N.GatherMergeParams()
-        p.rank, p.world, p.rows, p.D = self.rank, self.world, rows, head_dim
+        dist.all_gather_object(infos, mine, group=group)
+        ptrs = [[0, 0] for _ in range(self.world)]
         for r in range(self.world):
-            if r == self.rank:
-                ptr = self.buf.data_ptr()
-            else:
-                h = (ctypes.c_char * 64).from_buffer_copy(infos[r][0])
+            for i, t in enumerate((self.buf, self.xbuf)):
+                if r == self.rank:
+                    ptrs[r][i] = t.data_ptr()
+                    continue
+                h = (ctypes.c_char * 64).from_buffer_copy(infos[r][i][0])
                 out_ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
-                N.check("helm_ipc_import", lib.helm_ipc_import(h, infos[r][1], ctypes.byref(out_ptr),
+                N.check("helm_ipc_import", lib.helm_ipc_import(h, infos[r][i][1], ctypes.byref(out_ptr),
                                                                ctypes.byref(base)))
                 self._bases.append(base.value)
-                ptr = out_ptr.value
-            p.peer_recv[r] = ptr
-            p.peer_flags[r] = ptr + rb.value
+                ptrs[r][i] = out_ptr.value
+        p = N.GatherMergeParams()
+        p.rank, p.world, p.rows, p.D = self.rank, self.world, rows, head_dim
+        x = N.ShardExchange()
+        x.rank, x.world = self.rank, self.world
+        for r in range(self.world):
+            p.peer_recv[r] = ptrs[r][0]
+            p.peer_flags[r] = ptrs[r][0] + rb.value
+            x.peer_recv[r] = ptrs[r][1]
+            x.peer_flags[r] = ptrs[r][1] + xr.value
         p.recv_local = self.buf.data_ptr()
         p.flags_local = self.buf.data_ptr() + rb.value
         p.counters = self.counters.data_ptr()
         p.error_flag = self.error_flag.data_ptr()
+        x.recv_local = self.xbuf.data_ptr()
+        x.flags_local = self.xbuf.data_ptr() + xr.value
+        x.counters = self.xcounters.data_ptr()
         self.params = p
+        self.xparams = x
+        self.xparams_ptr = ctypes.pointer(x)
         dist.barrier(group=group)
+
+    @property
+    def fused(self) -> bool:
+        """True when the attention call itself should do the exchange."""
+        return self.exchange == "fused" and self.params is not None and self.world > 1
 
     def gather_merge(self, record: torch.Tensor, out: Optional[torch.Tensor] = None,
                      out_record: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
@@ -121,3 +153,4 @@ class KVShardGroup:
             if dist.is_initialized():
                 dist.barrier(group=self.group)
         self.params = None
+        self.xparams_ptr = None

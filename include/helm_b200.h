@@ -23,7 +23,8 @@
 extern "C" {
 #endif
 
-#define HELM_ABI_VERSION 1
+#define HELM_ABI_VERSION 2
+#define HELM_MAX_RANKS 8
 
 /* ---- status codes ------------------------------------------------------- */
 enum {
@@ -88,6 +89,30 @@ const char *helm_last_error(void);
  * cross-GPU merge.  With num_splits == 1 and only `out` requested, no
  * workspace is touched.
  */
+/* Cross-GPU exchange fused into helm_paged_attn_decode (KV sequence sharding).
+ * With params.exchange set, each rank's pages are its share of every sequence:
+ * the CTA that completes a (sequence, kv head) pair's rank-local merge stores
+ * the pair's record into every rank's receive slot over NVLink (CUDA IPC
+ * mappings), waits (bounded, 2 s) for the other ranks' records of that pair
+ * and merges them in rank order, so `out` / `out_record` hold the attention
+ * over the whole sequence on every rank.  Buffers: per rank one exchange
+ * buffer of helm_shard_exchange_bytes() (receive slots, then flags; zeroed once,
+ * shared through helm_ipc_export / helm_ipc_import) and local counters
+ * (zeroed once).  Every rank makes the same sequence of calls with the same
+ * B, Hq, Hkv, D.  No counterpart in the reference (single-process). */
+typedef struct {
+  int32_t rank, world;
+  float *peer_recv[HELM_MAX_RANKS];      /* receive slots of rank r, as mapped here */
+  uint32_t *peer_flags[HELM_MAX_RANKS];  /* flags of rank r, as mapped here */
+  float *recv_local;                     /* == peer_recv[rank] */
+  uint32_t *flags_local;                 /* == peer_flags[rank] */
+  uint32_t *counters;                    /* local */
+} helm_shard_exchange;
+
+/* Sizes for rows = B*Hq records of D dims: receive slots, flags, local counters. */
+int64_t helm_shard_exchange_bytes(int32_t world, int32_t rows, int32_t D, int64_t *recv_bytes_out,
+                                  int64_t *flags_bytes_out, int64_t *counters_bytes_out);
+
 typedef struct {
   const void *q;          /* [B, Hq, D], q_dtype */
   const void *k_base;     /* pool base of K, kv_dtype */
@@ -109,6 +134,7 @@ typedef struct {
   void *out;              /* [B, Hq, D] out_dtype, or null */
   float *out_record;      /* [B*Hq, D+2] merged record, or null */
   int32_t *error_flag;    /* device int, optional */
+  const helm_shard_exchange *exchange; /* null, or the fused cross-GPU exchange */
 } helm_paged_attn_params;
 
 /* Bytes of workspace helm_paged_attn_decode needs for these params, after
@@ -238,8 +264,6 @@ int helm_kv_append(const helm_kv_append_params *p, void *stream);
  * Waits for peers are bounded (2 s); a wait that gives up sets
  * HELM_DEVERR_TIMEOUT in error_flag and leaves zeros in the affected rows.
  */
-#define HELM_MAX_RANKS 8
-
 typedef struct {
   int32_t rank, world, rows, D;
   const float *record;                  /* [rows][D+2], this rank's */

@@ -30,32 +30,50 @@ def _worker(rank, world, port, exchange, result_q):
     try:
         from helm_b200 import ops
         from helm_b200.runtime.sharded import KVShardGroup, shard_bounds
-        B, Hq, Hkv, D, P, npg = 3, 32, 4, 128, 64, 50
+        Hq, Hkv, D, P = 32, 4, 128, 64
+        npgs = [50, 1, 17]                               # sequence 1 has no pages on rank 0
+        B = len(npgs)
+        total = sum(npgs)
         g = torch.Generator().manual_seed(7)            # same data on every rank
-        kp = torch.randn(B * npg, Hkv, P, D, generator=g).to(torch.bfloat16)
-        vp = torch.randn(B * npg, Hkv, P, D, generator=g).to(torch.bfloat16)
-        pt = torch.randperm(B * npg, generator=g).to(torch.int32).reshape(B, npg)
-        pu = torch.full((B, npg), P, dtype=torch.int32)
-        pu[:, -1] = 29
-        kp, vp = kp.to(dev), vp.to(dev)
+        kp = torch.randn(total, Hkv, P, D, generator=g).to(torch.bfloat16).to(dev)
+        vp = torch.randn(total, Hkv, P, D, generator=g).to(torch.bfloat16).to(dev)
+        perm = torch.randperm(total, generator=g).to(torch.int32)
+        width = max(npgs)
+        pt = torch.zeros((B, width), dtype=torch.int32)
+        pu = torch.zeros((B, width), dtype=torch.int32)
+        lpt = torch.zeros((B, width), dtype=torch.int32)
+        lpu = torch.zeros((B, width), dtype=torch.int32)
+        lnp = torch.zeros((B,), dtype=torch.int32)
+        i = 0
+        for b, n in enumerate(npgs):
+            pt[b, :n] = perm[i:i + n]
+            pu[b, :n] = P
+            pu[b, n - 1] = 29
+            i += n
+            lo, hi = shard_bounds(n, rank, world)
+            lpt[b, :hi - lo] = pt[b, lo:hi]
+            lpu[b, :hi - lo] = pu[b, lo:hi]
+            lnp[b] = hi - lo
         common = dict(num_kv_heads=Hkv, page_size=P, page_stride=Hkv * P * D, head_stride=P * D,
-                      num_pool_pages=B * npg)
+                      num_pool_pages=total)
         rows = B * Hq
         group = KVShardGroup(rows, D, dev, exchange=exchange)
-        lo, hi = shard_bounds(npg, rank, world)
         errs = []
         for call in range(5):
             q = torch.randn(B, Hq, D, generator=g).to(torch.bfloat16).to(dev)
             full = ops.paged_decode_attention(q, kp, vp, pt.to(dev), pu.to(dev),
-                                              torch.full((B,), npg, dtype=torch.int32, device=dev),
+                                              torch.tensor(npgs, dtype=torch.int32, device=dev),
                                               out_dtype=torch.float32, **common)
-            rec = torch.empty(rows, D + 2, device=dev)
-            ops.paged_decode_attention(q, kp, vp, pt[:, lo:hi].contiguous().to(dev),
-                                       pu[:, lo:hi].contiguous().to(dev),
-                                       torch.full((B,), hi - lo, dtype=torch.int32, device=dev),
-                                       out_record=rec, **common)
-            out = torch.empty(rows, D, device=dev, dtype=torch.float32)
-            group.gather_merge(rec, out=out)
+            if exchange == "fused":
+                out = ops.paged_decode_attention(q, kp, vp, lpt.to(dev), lpu.to(dev), lnp.to(dev),
+                                                 out_dtype=torch.float32, exchange=group.xparams_ptr,
+                                                 error_flag=group.error_flag, **common)
+            else:
+                rec = torch.empty(rows, D + 2, device=dev)
+                ops.paged_decode_attention(q, kp, vp, lpt.to(dev), lpu.to(dev), lnp.to(dev), out_record=rec,
+                                           **common)
+                out = torch.empty(rows, D, device=dev, dtype=torch.float32)
+                group.gather_merge(rec, out=out)
             torch.cuda.synchronize(dev)
             errs.append(float((out.reshape(B, Hq, D) - full).abs().max()))
         flag = int(group.error_flag.item())
@@ -65,7 +83,7 @@ def _worker(rank, world, port, exchange, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+@pytest.mark.parametrize("exchange", ["fused", "p2p", "nccl"])
 def test_two_gpu_exchange_matches_single_gpu(exchange):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
