@@ -663,27 +663,30 @@ struct PersistArgs {
   float *rec_ml;       // [C + pairs][gq][2]: its (m, l)
   uint32_t *counter;   // [pairs], zero at launch
   int C;               // grid size
-  // fused cross-GPU exchange (xworld > 1); records of stride D + 4 floats: o[D], m, l, pad
+  // Fused cross-GPU exchange (xworld > 1).  Receive slots of every rank: [2][G][B*Hq][D+2] words
+  // of 64 bits, each one value (o[0..D), m, l) in the low half and the call's epoch in the high
+  // half, so a reader knows a word has arrived from the word itself (no fence, no flag).
   int xrank, xworld;
-  float *xrecv[HELM_MAX_RANKS];     // [2][G][B*Hq][D+4] of each rank
-  uint32_t *xflags[HELM_MAX_RANKS]; // [G][pairs] of each rank
-  float *xrecv_local;
-  uint32_t *xflags_local;
-  uint32_t *xsent;                  // [pairs]
-  uint32_t *xseen;                  // [G][pairs]
+  uint64_t *xrecv[HELM_MAX_RANKS];
+  uint64_t *xrecv_local;
+  uint32_t *xsent;                  // [pairs]: exchanges done per pair (epoch of the next is +1)
 };
 
 constexpr uint64_t kExchangeWaitNs = 2000000000ull;
 
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t epoch) {
+  return ((uint64_t)epoch << 32) | __float_as_uint(v);
 }
 
-__device__ __forceinline__ void red_relaxed_sys_add_u32(uint32_t *p, uint32_t v) {
-  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_volatile_v2_u64(uint64_t *p, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
+
+__device__ __forceinline__ void ld_volatile_v2_u64(const uint64_t *p, uint64_t &a, uint64_t &b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ bool ll_ok(uint64_t w, uint32_t epoch) { return (uint32_t)(w >> 32) == epoch; }
 
 // CTA owning unit u when U units are split over C CTAs as [c*U/C, (c+1)*U/C).
 __device__ __forceinline__ int owner_cta(int64_t u, int64_t U, int C) {
@@ -711,8 +714,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   __shared__ float mg_M[HN], mg_L[HN], mg_A[HN];
   __shared__ int pending[kMaxPending];
   __shared__ int npending;
-  __shared__ uint32_t xs_slot, xs_src_slot[HELM_MAX_RANKS];
-  __shared__ int xs_ok;
+  __shared__ uint32_t xs_epoch;
+  __shared__ int xs_dead;  // a wait of this CTA ran out: later exchanges do not wait again
+  __shared__ uint64_t *xs_peer[HELM_MAX_RANKS];  // pa.xrecv (dynamic indexing of a kernel parameter array
+                                                 // would copy it to local memory)
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int c = blockIdx.x;
@@ -727,6 +732,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&empty_bar[i], kConsumerWarps);
     }
     npending = 0;
+    xs_dead = 0;
+#pragma unroll
+    for (int r = 0; r < HELM_MAX_RANKS; ++r) xs_peer[r] = pa.xrecv[r];
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // Units per sequence and their prefix sums (warp 0: chunked scan).
@@ -909,82 +917,127 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         return;
       }
+      // Exchange: this rank's record of the pair goes to every other rank as 64-bit words
+      // (value | epoch << 32), then the G records are merged in rank order (the own one from
+      // registers), exactly as helm_lse_merge merges them.  Row layout (D + 2 words): o[4c], o[4c+1]
+      // at words 2c, 2c+1; o[4c+2], o[4c+3] at D/2 + 2c, D/2 + 2c + 1; then m, l -- so a warp's
+      // 16-byte stores (and the readers' loads) cover 512 contiguous bytes.  Slot parity (epoch & 1)
+      // keeps call n+1's words from overwriting call n's before every reader is done: a rank
+      // starts call n+1 only after its call n received every rank's words of call n, which each
+      // rank sends after it finished reading call n-1.
       const int G = pa.xworld, R = pa.xrank;
-      const int rows = B * a.Hq, pairs = B * Hkv;
-      constexpr int XL = D + 4;
+      const int64_t rows = (int64_t)B * a.Hq;
+      constexpr int XW = D + 2;
       if (tid == 0) {
-        xs_slot = pa.xsent[pair] & 1u;
-        xs_ok = 1;
+        xs_epoch = pa.xsent[pair] + 1;
+        if (*(volatile int *)a.error_flag == HELM_DEVERR_TIMEOUT) xs_dead = 1;
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-      const uint32_t slot = xs_slot;
-      for (int dst = 0; dst < G; ++dst) {
-#pragma unroll
-        for (int e = 0; e < F4x; ++e) {
-          const int idx4 = tid + e * kConsumerWarps * 32;
-          if (idx4 < gq * (D / 4)) {
-            const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
-            const float M = mg_M[h];
-            const bool empty = M == -INFINITY;
-            float *dst_row = pa.xrecv[dst] + (((int64_t)slot * G + R) * rows + (int64_t)b * a.Hq + g * gq + h) * XL;
-            *reinterpret_cast<float4 *>(dst_row + d) = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc[e];
-            if (d == 0) *reinterpret_cast<float2 *>(dst_row + D) = make_float2(M, empty ? 0.f : mg_L[h]);
-          }
-        }
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-      if (tid < G) {
-        __threadfence_system();
-        red_relaxed_sys_add_u32(pa.xflags[tid] + R * pairs + pair, 1u);
-        const uint32_t want = pa.xseen[tid * pairs + pair] + 1;
-        const uint32_t *f = pa.xflags_local + tid * pairs + pair;
-        bool ok = ld_acquire_sys_u32(f) >= want;
-        if (!ok) {
-          const uint64_t t0 = global_ns();
-          while (!(ok = ld_acquire_sys_u32(f) >= want))
-            if (global_ns() - t0 > kExchangeWaitNs) break;
-        }
-        if (!ok) {
-          flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
-          atomicExch(&xs_ok, 0);
-        }
-        xs_src_slot[tid] = (want - 1) & 1u;
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-      __threadfence();
+      const uint32_t ep = xs_epoch;
+      const int64_t slot_base = (int64_t)(ep & 1u) * G;
 #pragma unroll
       for (int e = 0; e < F4x; ++e) {
         const int idx4 = tid + e * kConsumerWarps * 32;
         if (idx4 < gq * (D / 4)) {
-          const int h = idx4 / (D / 4), d = (idx4 - h * (D / 4)) * 4;
-          const int64_t row = (int64_t)b * a.Hq + g * gq + h;
-          float M = -INFINITY;
-          for (int t = 0; t < G; ++t) {
-            const float *rr = pa.xrecv_local + (((int64_t)xs_src_slot[t] * G + t) * rows + row) * XL;
-            M = fmaxf(M, __ldcg(rr + D));
+          const int h = idx4 / (D / 4), cq = idx4 - h * (D / 4);
+          const float M = mg_M[h];
+          const bool empty = M == -INFINITY;
+          const float4 v = empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc[e];
+          const uint64_t w0 = ll_word(v.x, ep), w1 = ll_word(v.y, ep), w2 = ll_word(v.z, ep),
+                         w3 = ll_word(v.w, ep);
+          const uint64_t wm = ll_word(M, ep), wl = ll_word(empty ? 0.f : mg_L[h], ep);
+          const int64_t off = ((slot_base + R) * rows + (int64_t)b * a.Hq + g * gq + h) * XW;
+          for (int k = 1; k < G; ++k) {
+            const int dst = R + k < G ? R + k : R + k - G;  // spread the first stores over peers
+            uint64_t *row = xs_peer[dst] + off;
+            st_volatile_v2_u64(row + 2 * cq, w0, w1);
+            st_volatile_v2_u64(row + D / 2 + 2 * cq, w2, w3);
+            if (cq == 0) st_volatile_v2_u64(row + D, wm, wl);
           }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < F4x; ++e) {
+        const int idx4 = tid + e * kConsumerWarps * 32;
+        if (idx4 < gq * (D / 4)) {
+          const int h = idx4 / (D / 4), cq = idx4 - h * (D / 4);
+          const int64_t row = (int64_t)b * a.Hq + g * gq + h;
+          const float own_M = mg_M[h];
+          const bool own_empty = own_M == -INFINITY;
+          // Every rank's words of this thread's slice, loaded four ranks at a time (register
+          // budget) and re-polled (bounded) until all carry this call's epoch.
+          float m_t[HELM_MAX_RANKS], l_t[HELM_MAX_RANKS];
+          float4 o_t[HELM_MAX_RANKS];
+          bool ok = true;
+          uint64_t t0 = 0;
+          bool timed = false;
+#pragma unroll
+          for (int t_lo = 0; t_lo < HELM_MAX_RANKS; t_lo += 4) {
+            while (ok) {
+              bool all = true;
+#pragma unroll
+              for (int t = t_lo; t < t_lo + 4; ++t) {
+                if (t < G && t != R) {
+                  const uint64_t *src = pa.xrecv_local + ((slot_base + t) * rows + row) * XW;
+                  uint64_t wm, wl, w0, w1, w2, w3;
+                  ld_volatile_v2_u64(src + D, wm, wl);
+                  ld_volatile_v2_u64(src + 2 * cq, w0, w1);
+                  ld_volatile_v2_u64(src + D / 2 + 2 * cq, w2, w3);
+                  m_t[t] = __uint_as_float((uint32_t)wm);
+                  l_t[t] = __uint_as_float((uint32_t)wl);
+                  o_t[t] = make_float4(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1),
+                                       __uint_as_float((uint32_t)w2), __uint_as_float((uint32_t)w3));
+                  all = all && ll_ok(wm, ep) && ll_ok(wl, ep) && ll_ok(w0, ep) && ll_ok(w1, ep) &&
+                        ll_ok(w2, ep) && ll_ok(w3, ep);
+                } else {
+                  m_t[t] = own_M;
+                  l_t[t] = own_empty ? 0.f : mg_L[h];
+                  o_t[t] = own_empty ? make_float4(0.f, 0.f, 0.f, 0.f) : acc[e];
+                }
+              }
+              if (all) break;
+              if (*(volatile int *)&xs_dead) {
+                ok = false;
+                break;
+              }
+              if (!timed) {
+                t0 = global_ns();
+                timed = true;
+              } else if (global_ns() - t0 > kExchangeWaitNs) {
+                ok = false;
+                break;
+              }
+            }
+          }
+          float M = -INFINITY;
+#pragma unroll
+          for (int t = 0; t < HELM_MAX_RANKS; ++t)
+            if (t < G && ok) M = fmaxf(M, m_t[t]);
           float L = 0.f;
           float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int t = 0; t < G; ++t) {
-            const float *rr = pa.xrecv_local + (((int64_t)xs_src_slot[t] * G + t) * rows + row) * XL;
-            const float2 ml = __ldcg(reinterpret_cast<const float2 *>(rr + D));
-            const float w = rescale_weight(ml.x, M);
-            L = fmaf(ml.y, w, L);
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(rr + d));
-            O.x = fmaf(v.x, w, O.x);
-            O.y = fmaf(v.y, w, O.y);
-            O.z = fmaf(v.z, w, O.z);
-            O.w = fmaf(v.w, w, O.w);
+#pragma unroll
+          for (int t = 0; t < HELM_MAX_RANKS; ++t) {
+            if (t >= G || !ok) continue;
+            const float w = rescale_weight(m_t[t], M);
+            L = fmaf(l_t[t], w, L);
+            O.x = fmaf(o_t[t].x, w, O.x);
+            O.y = fmaf(o_t[t].y, w, O.y);
+            O.z = fmaf(o_t[t].z, w, O.z);
+            O.w = fmaf(o_t[t].w, w, O.w);
           }
-          const bool none = M == -INFINITY || !xs_ok;
+          if (!ok) {
+            flag_error(a.error_flag, HELM_DEVERR_TIMEOUT);
+            xs_dead = 1;
+          }
+          const bool none = M == -INFINITY || !ok;
+          const int d = cq * 4;
           const float vals[4] = {O.x, O.y, O.z, O.w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) emit(a, 0, b, g * gq + h, d + j, M, none ? 0.f : L, none ? 0.f : vals[j]);
         }
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-      if (tid < G) pa.xseen[tid * pairs + pair] += 1;
-      if (tid == 0) pa.xsent[pair] += 1;
+      if (tid == 0) pa.xsent[pair] = ep;
     };
 
     const int64_t n_units = u1 - u0;
@@ -1479,11 +1532,16 @@ int validate(const helm_paged_attn_params *p) {
     const helm_shard_exchange *x = p->exchange;
     if (x->world > HELM_MAX_RANKS || x->rank < 0 || x->rank >= x->world)
       return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: bad exchange rank %d / world %d", x->rank, x->world);
-    if (!x->recv_local || !x->flags_local || !x->counters)
+    if (!x->recv_local || !x->counters)
       return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: exchange buffers missing");
-    for (int r = 0; r < x->world; ++r)
-      if (!x->peer_recv[r] || !x->peer_flags[r])
+    if (x->recv_local != x->peer_recv[x->rank])
+      return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: exchange recv_local != peer_recv[rank]");
+    for (int r = 0; r < x->world; ++r) {
+      if (!x->peer_recv[r])
         return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: exchange peer %d missing", r);
+      if (reinterpret_cast<uintptr_t>(x->peer_recv[r]) % 16 != 0)
+        return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: exchange slots of rank %d not 16-byte aligned", r);
+    }
     if (p->num_splits != 0)
       return fail(HELM_ERR_UNSUPPORTED, "paged_attn: the fused exchange needs num_splits == 0");
   }
@@ -1585,7 +1643,7 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
       return fail(HELM_ERR_CUDA, "paged_attn: cuTensorMapEncodeTiled failed");
     const bool two = a.gq > 8;
     if (pl.persistent) {
-      tc::PersistArgs pa;
+      tc::PersistArgs pa{};
       pa.rec_o = p->workspace;
       pa.rec_ml = reinterpret_cast<float *>(reinterpret_cast<char *>(p->workspace) + pl.ml_off);
       pa.counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(p->workspace) + pl.counter_off);
@@ -1596,14 +1654,9 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
         const helm_shard_exchange *x = p->exchange;
         pa.xrank = x->rank;
         pa.xworld = x->world;
-        for (int r = 0; r < x->world; ++r) {
-          pa.xrecv[r] = x->peer_recv[r];
-          pa.xflags[r] = x->peer_flags[r];
-        }
-        pa.xrecv_local = x->recv_local;
-        pa.xflags_local = x->flags_local;
+        for (int r = 0; r < x->world; ++r) pa.xrecv[r] = reinterpret_cast<uint64_t *>(x->peer_recv[r]);
+        pa.xrecv_local = reinterpret_cast<uint64_t *>(x->recv_local);
         pa.xsent = x->counters;
-        pa.xseen = x->counters + (int64_t)p->B * p->Hq;
       }
       cudaError_t e = cudaMemsetAsync(pa.counter, 0, (size_t)p->B * p->Hkv * sizeof(uint32_t), st);
       if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: cudaMemsetAsync: %s", cudaGetErrorString(e));
@@ -1719,11 +1772,10 @@ extern "C" int64_t helm_shard_exchange_bytes(int32_t world, int32_t rows, int32_
     fail(HELM_ERR_INVALID_ARGUMENT, "shard_exchange_bytes: bad sizes world=%d rows=%d D=%d", world, rows, D);
     return -1;
   }
-  // receive slots [2][G][rows][D+4] floats; flags [G][rows] (>= [G][pairs]); counters sent[rows] +
-  // seen[G][rows].
-  const int64_t recv = 2ll * world * rows * (D + 4) * (int64_t)sizeof(float);
-  const int64_t flags = (int64_t)world * rows * (int64_t)sizeof(uint32_t);
-  const int64_t counters = (1 + (int64_t)world) * rows * (int64_t)sizeof(uint32_t);
+  // receive slots [2][G][rows][D+2] words of 64 bits; no flags; counters sent[rows] (>= pairs).
+  const int64_t recv = 2ll * world * rows * (D + 2) * (int64_t)sizeof(uint64_t);
+  const int64_t flags = 0;
+  const int64_t counters = (int64_t)rows * (int64_t)sizeof(uint32_t);
   if (recv_bytes_out) *recv_bytes_out = recv;
   if (flags_bytes_out) *flags_bytes_out = flags;
   if (counters_bytes_out) *counters_bytes_out = counters;

@@ -10,9 +10,10 @@ rank ends with the same attention output.
 Three exchanges are provided:
 * "fused" (default): inside the attention kernel itself (helm_paged_attn_decode
   with params.exchange): the CTA that completes a (sequence, kv head) pair
-  stores the pair's record into every rank's receive buffer over NVLink (CUDA
-  IPC mappings), waits for the other ranks' records and merges them -- the
-  collective overlaps the tail of the attention, and no extra launch runs;
+  stores the pair's record into every other rank's receive buffer over NVLink
+  (CUDA IPC mappings) as 64-bit (value, epoch) words, waits for the other
+  ranks' words and merges them -- the collective overlaps the tail of the
+  attention, and no extra launch runs;
 * "p2p": helm_gather_merge, the same exchange as a separate kernel after the
   attention (used when the attention cannot run the persistent kernel);
 * "nccl": torch.distributed.all_gather_into_tensor + helm_lse_merge.
@@ -100,13 +101,11 @@ class KVShardGroup:
             p.peer_recv[r] = ptrs[r][0]
             p.peer_flags[r] = ptrs[r][0] + rb.value
             x.peer_recv[r] = ptrs[r][1]
-            x.peer_flags[r] = ptrs[r][1] + xr.value
         p.recv_local = self.buf.data_ptr()
         p.flags_local = self.buf.data_ptr() + rb.value
         p.counters = self.counters.data_ptr()
         p.error_flag = self.error_flag.data_ptr()
         x.recv_local = self.xbuf.data_ptr()
-        x.flags_local = self.xbuf.data_ptr() + xr.value
         x.counters = self.xcounters.data_ptr()
         self.params = p
         self.xparams = x

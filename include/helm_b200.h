@@ -92,24 +92,28 @@ const char *helm_last_error(void);
 /* Cross-GPU exchange fused into helm_paged_attn_decode (KV sequence sharding).
  * With params.exchange set, each rank's pages are its share of every sequence:
  * the CTA that completes a (sequence, kv head) pair's rank-local merge stores
- * the pair's record into every rank's receive slot over NVLink (CUDA IPC
- * mappings), waits (bounded, 2 s) for the other ranks' records of that pair
- * and merges them in rank order, so `out` / `out_record` hold the attention
- * over the whole sequence on every rank.  Buffers: per rank one exchange
- * buffer of helm_shard_exchange_bytes() (receive slots, then flags; zeroed once,
- * shared through helm_ipc_export / helm_ipc_import) and local counters
- * (zeroed once).  Every rank makes the same sequence of calls with the same
- * B, Hq, Hkv, D.  No counterpart in the reference (single-process). */
+ * the pair's record into every other rank's receive slot over NVLink (CUDA IPC
+ * mappings) as 64-bit words (value | epoch << 32, so no fence or flag is
+ * needed), waits (bounded, 2 s) for the other ranks' words of that pair and
+ * merges the records in rank order, so `out` / `out_record` hold the
+ * attention over the whole sequence on every rank, bit-identical across ranks.
+ * Buffers: per rank one receive buffer of helm_shard_exchange_bytes()
+ * (zeroed once, 16-byte aligned, shared through helm_ipc_export /
+ * helm_ipc_import) and local counters (zeroed once).  Every rank makes the
+ * same sequence of calls with the same B, Hq, Hkv, D, each call starting
+ * after the previous one on the stream has finished.  peer_flags /
+ * flags_local are unused (flags_bytes is 0).  No counterpart in the reference
+ * (single-process). */
 typedef struct {
   int32_t rank, world;
   float *peer_recv[HELM_MAX_RANKS];      /* receive slots of rank r, as mapped here */
-  uint32_t *peer_flags[HELM_MAX_RANKS];  /* flags of rank r, as mapped here */
+  uint32_t *peer_flags[HELM_MAX_RANKS];  /* unused; may be null */
   float *recv_local;                     /* == peer_recv[rank] */
-  uint32_t *flags_local;                 /* == peer_flags[rank] */
+  uint32_t *flags_local;                 /* unused; may be null */
   uint32_t *counters;                    /* local */
 } helm_shard_exchange;
 
-/* Sizes for rows = B*Hq records of D dims: receive slots, flags, local counters. */
+/* Sizes for rows = B*Hq records of D dims: receive slots, flags (0), local counters. */
 int64_t helm_shard_exchange_bytes(int32_t world, int32_t rows, int32_t D, int64_t *recv_bytes_out,
                                   int64_t *flags_bytes_out, int64_t *counters_bytes_out);
 

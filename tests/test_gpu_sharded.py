@@ -76,6 +76,12 @@ def _worker(rank, world, port, exchange, result_q):
                 group.gather_merge(rec, out=out)
             torch.cuda.synchronize(dev)
             errs.append(float((out.reshape(B, Hq, D) - full).abs().max()))
+            # every rank must hold the identical merged output (rank-order merge)
+            outs = [torch.empty_like(out) for _ in range(world)]
+            dist.all_gather(outs, out.contiguous())
+            same = all(torch.equal(o, outs[0]) for o in outs)
+            if not same:
+                errs.append(float("inf"))
         flag = int(group.error_flag.item())
         group.close()
         result_q.put((rank, max(errs), flag))
