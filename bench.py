@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
+    ap.add_argument("--workload", default="config5", choices=["config5", "config2"],
+                    help="config5: the sharded decode-attention stack (default); config2: INT8 GEMV shapes")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--exchange", default="fused", choices=["fused", "p2p", "nccl"],
@@ -60,6 +62,13 @@ def parse():
     if args.ctx is not None:
         CFG["ctx"] = args.ctx
     return args
+
+
+# DRAM traffic of one attention launch, from the ncu capture summarised in
+# profiles/attn_tc_persistent_config5.txt (small case of the same kernel): reads per algorithmic
+# byte, and the record/output writes of a batch-4, 64-head call.
+ATTN_READ_PER_ALG_BYTE = 269.749504 / 268.664832
+ATTN_WRITE_BYTES = 5.910784e6
 
 
 def peaks():
@@ -420,7 +429,12 @@ def run_helm(args, rank, local, world):
                        "num_splits": st.splits},
             "hbm_gbs": step_bytes_all / (ms_step * 1e-3) / 1e9 / world,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": achieved / hbm_peak,
+                         "traffic": (ATTN_READ_PER_ALG_BYTE * bytes_launch + ATTN_WRITE_BYTES
+                                     if (world == 1 and st.splits == 0) else None),
+                         "traffic_source": "ncu dram__bytes_read/write.sum of a 268.7 MB launch, reads scaled "
+                                           "by the units streamed (profiles/attn_tc_persistent_config5.txt)",
+                         "peak_kind": peak_kind,
                          "kernel": "attn_tc_persistent_kernel (one helm_paged_attn_decode call: counter memset + kernel)",
                          "bytes_per_launch": bytes_launch, "avg_launch_ms": attn_avg_ms},
             "breakdown_ms_per_layer": breakdown,
@@ -516,6 +530,188 @@ def run_e2e(st, stream, steps, world, dev):
             "api": "helm_b200.runtime.kv_offload._decode_batched per layer (KVCacheManager/KVAllocator state)"}
 
 
+# ----------------------------------------------------------------------------
+# config 2: INT8 weight-only GEMV (the linears feeding attention)
+# ----------------------------------------------------------------------------
+C2_SHAPES = [(12288, 4096), (4096, 12288), (6144, 4096)]   # (N, K)
+C2_ROWS = [1, 4, 8]
+C2_METRIC = "int8 weight-only linear: algorithmic HBM GB/s (config2 shapes, M in 1/4/8)"
+C2_WORKLOAD = ("config2: y = (x . Wq^T) * s, W int8 [N,K] uniform[-127,127], s fp16 U(0.001,0.02), x fp16 N(0,1); "
+               "(N,K) in (12288,4096) (4096,12288) (6144,4096); M in 1,4,8")
+
+
+def c2_bytes(M, Nn, K):
+    """Algorithmic bytes of one call: int8 weight + fp16 scale + fp16 x in + fp16 y out."""
+    return Nn * K + Nn * 2 + M * K * 2 + M * Nn * 2
+
+
+def c2_inputs(Nn, K, M, dev, copies):
+    g = torch.Generator().manual_seed(0)
+    w = [torch.randint(-127, 128, (Nn, K), generator=g, dtype=torch.int8).to(dev) for _ in range(copies)]
+    s = (torch.rand(Nn, generator=g) * 0.019 + 0.001).to(torch.float16).to(dev)
+    x = torch.randn(M, K, generator=g).to(torch.float16).to(dev)
+    return w, s, x
+
+
+def run_config2(args, rank, local, world):
+    """Device time of helm_int8_linear at every config-2 shape: a CUDA graph of one call per weight
+    copy (copies rotate through > 4x L2, so every call streams its weight from HBM), replayed;
+    CUDA events on the launching stream.  Replicas only: every rank runs the same work."""
+    from helm_b200 import _native as N
+    from helm_b200 import ops
+    from helm_b200.kernels import Int8Linear
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_pg(world, local)
+    stream = torch.cuda.current_stream(dev)
+    lib = N.lib()
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    clocks = ClockSampler(gpu_selector(dev, local))
+    clocks.start()
+    cases, tot_bytes, tot_ms = [], 0, 0.0
+    t_load0 = time.time()
+    e2e_bytes_in = e2e_bytes_out = 0
+    e2e_ms = 0.0
+    for (Nn, K) in C2_SHAPES:
+        copies = max(4, -(-4 * l2 // (Nn * K)))
+        for M in C2_ROWS:
+            w, s, x = c2_inputs(Nn, K, M, dev, copies)
+            y = torch.empty((M, Nn), dtype=torch.float16, device=dev)
+
+            def calls():
+                for wi in w:
+                    N.check("helm_int8_linear", lib.helm_int8_linear(
+                        x.data_ptr(), ops.dtype_code(x.dtype), wi.data_ptr(), s.data_ptr(), ops.dtype_code(s.dtype),
+                        None, y.data_ptr(), M, Nn, K, torch.cuda.current_stream(dev).cuda_stream))
+            for _ in range(max(args.warmup, 3)):
+                calls()
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                calls()
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            reps = max(1, args.steps // 10)
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier(world)
+            t0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = max_over_ranks(t0.elapsed_time(t1), world, dev) / (reps * copies)
+            del graph
+            nbytes = c2_bytes(M, Nn, K)
+            tot_bytes += nbytes
+            tot_ms += ms
+            # end to end through the public module: x from pinned host memory, y read back
+            mod = Int8Linear(K, Nn, bias=False, device=dev, dtype=torch.float16)
+            mod.weight = w[0]
+            mod.scale = s
+            x_h = x.cpu().pin_memory()
+            y_h = torch.empty((M, Nn), dtype=torch.float16).pin_memory()
+            n_e2e = 50
+            for _ in range(3):
+                y_h.copy_(mod(x_h.to(dev, non_blocking=True)), non_blocking=True)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n_e2e):
+                y_h.copy_(mod(x_h.to(dev, non_blocking=True)), non_blocking=True)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            e2e_ms += e0.elapsed_time(e1) / n_e2e
+            e2e_bytes_in += x_h.numel() * 2
+            e2e_bytes_out += y_h.numel() * 2
+            cases.append({"N": Nn, "K": K, "M": M, "us": round(ms * 1e3, 3), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                          "copies": copies})
+            del w, x, y, mod
+    clk = clocks.stop(t_load0, time.time())
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        agg = tot_bytes / (tot_ms * 1e-3) / 1e9
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_config2()
+        line = {
+            "metric": C2_METRIC, "value": agg * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": tot_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8 x fp16 -> fp32", "data": "synthetic",
+            "timing": "per shape: CUDA graph of one call per weight copy, replayed; CUDA events; a step = the 9 calls",
+            "config": {"workload": C2_WORKLOAD, "parallelism": f"replicas{world}",
+                       "l2": "weight copies rotate through > 4x L2 per shape"},
+            "cases": cases,
+            "roofline": {"bound": "hbm", "achieved": agg, "peak": hbm_peak, "unit": "GB/s", "frac": agg / hbm_peak,
+                         "traffic": None, "peak_kind": peak_kind, "kernel": "int8 GEMV (helm_int8_linear)",
+                         "bytes_per_launch": tot_bytes / len(cases), "avg_launch_ms": tot_ms / len(cases)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": tot_bytes / (e2e_ms * 1e-3) / 1e9 * world, "unit": "GB/s",
+                    "h2d_bytes_per_step": e2e_bytes_in, "d2h_bytes_per_step": e2e_bytes_out, "ms_per_step": e2e_ms,
+                    "api": "helm_b200.kernels.Int8Linear.forward per call, x from pinned host, y read back"},
+            "gpu_launches": len(cases) * 1,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def c2_reference_time(min_seconds=2.0):
+    """The reference's own AVX2 fp16 GEMV (helm/kernels/fp16_gemv.cpp, built into oracle/_ref) on the
+    fp16-dequantised config-2 weights, every shape and M; median seconds per call."""
+    from oracle.build_ref import load
+    from oracle.cpu_baseline import host_threads
+    mod = load()
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    out, tot_bytes, tot_s = [], 0, 0.0
+    for (Nn, K) in C2_SHAPES:
+        g = torch.Generator().manual_seed(0)
+        w = torch.randint(-127, 128, (Nn, K), generator=g, dtype=torch.int8)
+        s = (torch.rand(Nn, generator=g) * 0.019 + 0.001).to(torch.float16)
+        wf = (w.float() * s.float()[:, None]).to(torch.float16).contiguous()
+        for M in C2_ROWS:
+            x = torch.randn(M, K, generator=g).to(torch.float16)
+            mod.helm_fp16_linear(x, wf)
+            ts = []
+            t_end = time.perf_counter() + min_seconds
+            while time.perf_counter() < t_end or len(ts) < 3:
+                t0 = time.perf_counter()
+                mod.helm_fp16_linear(x, wf)
+                ts.append(time.perf_counter() - t0)
+            t = statistics.median(ts)
+            tot_bytes += c2_bytes(M, Nn, K)
+            tot_s += t
+            out.append({"N": Nn, "K": K, "M": M, "us": round(t * 1e6, 1)})
+    return tot_bytes, tot_s, out, threads
+
+
+def cpu_baseline_config2():
+    tot_bytes, tot_s, cases, threads = c2_reference_time(min_seconds=1.0)
+    return {"value": tot_bytes / tot_s / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
+            "sample": ("reference helm_fp16_linear (fp16_gemv.cpp, compiled from the reference source) on the "
+                       "fp16-dequantised weights, the 9 config-2 calls, median of >= 1 s each; value = the int8 "
+                       "path's algorithmic bytes / the reference's time for the same GEMVs"),
+            "cases": cases}
+
+
+def run_reference_config2(args, rank):
+    if rank != 0:
+        return
+    tot_bytes, tot_s, cases, threads = c2_reference_time(min_seconds=1.0)
+    v = tot_bytes / tot_s / 1e9
+    line = {"impl": "reference", "metric": C2_METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": 1, "warmup": 1, "ms_per_step": tot_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16 x fp16 -> fp32", "data": "synthetic",
+            "config": {"workload": C2_WORKLOAD, "parallelism": "host cores"}, "cases": cases,
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "sample": "helm_fp16_linear on the dequantised weights, 9 calls, median >= 1 s each"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline():
     from oracle.cpu_baseline import time_decode_attention
     c = CFG
@@ -531,6 +727,12 @@ def cpu_baseline():
 def main():
     args = parse()
     rank, local, world = dist_setup(args.gpus)
+    if args.workload == "config2":
+        if args.impl == "reference":
+            run_reference_config2(args, rank)
+        else:
+            run_config2(args, rank, local, world)
+        return
     if args.impl == "reference":
         run_reference(args, rank)
         return
