@@ -92,6 +92,7 @@ SIGNATURES = [
     ("helm_paged_attn_decode", _c.c_int, [_c.POINTER(PagedAttnParams), _p]),
     ("helm_lse_merge", _c.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p]),
     ("helm_int8_linear", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
+    ("helm_int8_linear_error", _c.c_int, [_p, _i32]),
     ("helm_kv_append", _c.c_int, [_c.POINTER(KVAppendParams), _p]),
     ("helm_copy_pages", _c.c_int, [_p, _i64, _p, _p, _i32, _i64, _c.POINTER(_i32), _p]),
     ("helm_gather_merge_state_bytes", _i64, [_i32, _i32, _i32, _c.POINTER(_i64), _c.POINTER(_i64),

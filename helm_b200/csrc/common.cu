@@ -1,7 +1,9 @@
 // Host helpers shared by the helm_b200 entry points.
 #include "common.cuh"
+#include "tma.cuh"
 
 #include <cstring>
+#include <mutex>
 
 namespace helm {
 
@@ -41,6 +43,19 @@ int num_sms() {
     cache[dev] = n > 0 ? n : 148;
   }
   return cache[dev];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
 }
 
 }  // namespace helm

@@ -1,154 +1,378 @@
 // INT8 weight-only linear: y[m, n] = (sum_k x[m, k] * w[n, k]) * s[n] + bias[n].
 //
 // The GPU counterpart of HELM's CPU decode GEMV (helm/kernels/fp16_gemv.cpp:
-// 45-100, one fp16 weight row dotted with x, fp32 accumulation, rows spread
+// 45-100: one fp16 weight row dotted with x, fp32 accumulation, rows spread
 // over threads), with the weight stored as int8 plus one scale per output
-// channel.  Decode-sized M (<= 8 per pass) runs on the CUDA cores: each warp
-// streams 4 weight rows with 16-byte loads, dequantises the int8 bytes in
-// registers (byte -> float through the 2^23 exponent trick, no I2F), and
-// accumulates with packed fp32x2 FMAs; the per-channel scale is applied once
+// channel.  Decode-sized M is HBM-bound: every weight byte is read once and
+// used M times, so the kernel is built to keep as many weight bytes in flight
+// as the SM allows and to spend as few instructions as possible per byte.
+//
+// Tensor-core formulation (mma.sync m16n8k16, fp32 accumulators): the weight
+// rows are the 16-row A operand and the rows of x are the 8-column B operand
+// (M <= 8 per n-tile, more n-tiles for larger M).  The reduction order inside
+// a 256-wide K block is permuted so that every thread reads 64 contiguous
+// weight bytes of each of its two rows (four 16-byte loads) and 128
+// contiguous bytes of its x row: thread j of a quad owns k = 64j .. 64j+63 of
+// the block, and MMA u of the block takes k = 64j + 4u + {0,1} as its
+// fragment columns (2j, 2j+1) and 64j + 4u + {2,3} as (2j+8, 2j+9).  A and B
+// use the same permutation, so the dot products are exact sums over the block.
+//
+// int8 -> fp16 is exact in two instructions per pair: the biased byte
+// b ^ 0x80 is placed in the low mantissa byte of 1024.0 (0x64xx) and 1152 is
+// subtracted.  For bf16 activations the pair goes through fp32 the same way
+// (0x4B0000xx - (2^23 + 128)) and the high halves of the exact fp32 values
+// are the bf16 values.  The per-channel scale and the bias are applied once
 // per output in the epilogue.
+//
+// Data movement: one producer warp streams the weight rows of the CTA with TMA
+// (2-D tensor map over W [N, K] int8, boxes of 128 k x 16*RT rows, 128-byte
+// swizzle) into a ring of shared-memory stages guarded by full/empty
+// mbarriers, so the bytes in flight are set by the ring size, not by
+// registers; four consumer warps each take one 128-k box of every 512-k
+// stage, convert their int8 fragments in registers and run the MMAs.  Their
+// partial tiles are summed in shared memory at the end.  A CTA owns 16*RT rows
+// over the whole K, with RT chosen so that every CTA is resident at once (the
+// HBM stream then balances the CTAs by itself).  Every mbarrier wait is
+// bounded (2 s); a wait that gives up sets HELM_DEVERR_TIMEOUT in the
+// library's INT8 error word (helm_int8_linear_error) and the CTA finishes
+// without writing its rows.
 #include "common.cuh"
+#include "tma.cuh"
+
+#include <mutex>
+#include <vector>
 
 namespace helm {
 
 namespace {
 
-constexpr int kRowsPerWarp = 4;
-constexpr int kWarps = 8;
-constexpr int kRowsPerBlock = kRowsPerWarp * kWarps;
+constexpr int kCWarps = 4;                       // consumer warps
+constexpr int kThreadsT = (kCWarps + 1) * 32;    // + one producer warp
+constexpr int kBoxK = 128;                       // k per TMA box row (128-byte swizzle)
+constexpr int kStageK = kCWarps * kBoxK;         // k per stage: one box per consumer warp
+constexpr int kStageBudget = 96 * 1024;          // shared memory for the ring
 
-__device__ __forceinline__ uint4 ld_stream(const void *p) {
+// Ring depth for RT row tiles: stages of 512 x 16*RT bytes within the budget, at most 8.
+template <int RT> constexpr int ring_stages() {
+  return (kStageBudget / (kStageK * 16 * RT)) < 8 ? (kStageBudget / (kStageK * 16 * RT)) : 8;
+}
+
+__device__ int g_int8_error;  // HELM_DEVERR_* bits of the INT8 kernels (helm_int8_linear_error)
+
+__device__ __forceinline__ uint4 ld_x(const void *p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
 
-__device__ __forceinline__ unsigned long long f2u(float2 v) {
-  return (static_cast<unsigned long long>(__float_as_uint(v.y)) << 32) | __float_as_uint(v.x);
+// Bytes (lo, hi) of `biased` (the int8 word xor 0x80808080) as an exact 16-bit pair of the
+// activation type; SEL picks the two bytes (0x4140: bytes 0,1; 0x4342: bytes 2,3).
+template <typename XT, uint32_t SEL> __device__ __forceinline__ uint32_t i8pair(uint32_t biased);
+
+template <> __device__ __forceinline__ uint32_t i8pair<__half, 0x4140u>(uint32_t u) {
+  uint32_t h = __byte_perm(u, 0x64646464u, 0x4140u), r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));  // (1024 + u) - 1152
+  return r;
 }
-__device__ __forceinline__ float2 u2f(unsigned long long u) {
-  return make_float2(__uint_as_float(static_cast<uint32_t>(u)), __uint_as_float(static_cast<uint32_t>(u >> 32)));
+template <> __device__ __forceinline__ uint32_t i8pair<__half, 0x4342u>(uint32_t u) {
+  uint32_t h = __byte_perm(u, 0x64646464u, 0x4342u), r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(0x64806480u));
+  return r;
 }
 
-// acc += a * b on both lanes of an fp32 pair.
-__device__ __forceinline__ void ffma2(unsigned long long &acc, unsigned long long a, unsigned long long b) {
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+__device__ __forceinline__ uint32_t bf16pair_from_bytes(uint32_t u, uint32_t sel_lo, uint32_t sel_hi) {
+  // fp32 (2^23 + u_byte) for both bytes, minus 2^23 + 128, exact; integers below 2^8 have zero
+  // low 16 bits in fp32, so the high halves are the bf16 values.
+  const uint32_t f0 = __byte_perm(u, 0x4B000000u, sel_lo);
+  const uint32_t f1 = __byte_perm(u, 0x4B000000u, sel_hi);
+  unsigned long long p = (static_cast<unsigned long long>(f1) << 32) | f0;
+  const unsigned long long bias = (static_cast<unsigned long long>(0x4B000080u) << 32) | 0x4B000080u;
+  asm("sub.rn.f32x2 %0, %0, %1;" : "+l"(p) : "l"(bias));
+  return __byte_perm(static_cast<uint32_t>(p), static_cast<uint32_t>(p >> 32), 0x7632u);
+}
+template <> __device__ __forceinline__ uint32_t i8pair<__nv_bfloat16, 0x4140u>(uint32_t u) {
+  return bf16pair_from_bytes(u, 0x7540u, 0x7541u);
+}
+template <> __device__ __forceinline__ uint32_t i8pair<__nv_bfloat16, 0x4342u>(uint32_t u) {
+  return bf16pair_from_bytes(u, 0x7542u, 0x7543u);
 }
 
-// Four signed bytes of `word` -> two fp32 pairs, exactly.  Each byte b is
-// biased to b+128 in [0, 255], placed in the low mantissa byte of 2^23, and
-// the float 2^23 + 128 is subtracted.
-__device__ __forceinline__ void i8x4_to_f2x2(uint32_t word, unsigned long long &p01, unsigned long long &p23) {
-  const uint32_t u = word ^ 0x80808080u;
-  const uint32_t f0 = __byte_perm(u, 0x4B000000u, 0x7540);
-  const uint32_t f1 = __byte_perm(u, 0x4B000000u, 0x7541);
-  const uint32_t f2 = __byte_perm(u, 0x4B000000u, 0x7542);
-  const uint32_t f3 = __byte_perm(u, 0x4B000000u, 0x7543);
-  const unsigned long long bias = f2u(make_float2(8388736.f, 8388736.f));
-  unsigned long long a = (static_cast<unsigned long long>(f1) << 32) | f0;
-  unsigned long long c = (static_cast<unsigned long long>(f3) << 32) | f2;
-  asm("sub.f32x2 %0, %0, %1;" : "+l"(a) : "l"(bias));
-  asm("sub.f32x2 %0, %0, %1;" : "+l"(c) : "l"(bias));
-  p01 = a;
-  p23 = c;
+template <typename XT>
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <typename XT> __device__ __forceinline__ unsigned long long x2_to_f2(uint32_t v);
-template <> __device__ __forceinline__ unsigned long long x2_to_f2<__half>(uint32_t v) {
-  return f2u(__half22float2(*reinterpret_cast<__half2 *>(&v)));
-}
-template <> __device__ __forceinline__ unsigned long long x2_to_f2<__nv_bfloat16>(uint32_t v) {
-  return (static_cast<unsigned long long>(v & 0xffff0000u) << 32) | (v << 16);
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
 }
 
-template <typename XT, int MB>
-__global__ void __launch_bounds__(256) int8_gemv_kernel(const XT *__restrict__ x, const int8_t *__restrict__ w,
-                                                        const void *__restrict__ scale, int scale_dt,
-                                                        const XT *__restrict__ bias, XT *__restrict__ y, int M,
-                                                        int N, int K) {
+// Grid (ceil(N / (16*RT)), ceil(M / (8*MT))), 160 threads.  Dynamic shared memory: the ring
+// (ST stages of 512 x 16*RT bytes, 1024-byte aligned) + kCWarps * RT * MT * 128 floats.
+template <typename XT, int RT, int MT>
+__global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                            const XT *__restrict__ x,
+                                                            const void *__restrict__ scale, int scale_dt,
+                                                            const XT *__restrict__ bias, XT *__restrict__ y, int M,
+                                                            int N, int K) {
+  constexpr int ST = ring_stages<RT>();
+  constexpr int kBoxBytes = kBoxK * 16 * RT;
+  constexpr int kStageBytes = kCWarps * kBoxBytes;
+  constexpr int P = RT * MT * 128;  // floats of one warp's partial tile
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[ST];
+  __shared__ __align__(8) uint64_t empty_bar[ST];
+  __shared__ int any_fail;
+  uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float *red = reinterpret_cast<float *>(ring + ST * kStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kRowsPerBlock + warp * kRowsPerWarp;
-  const int m0 = blockIdx.y * MB;
-  if (n0 >= N) return;
-  const int mcount = min(MB, M - m0);
+  const int n_base = blockIdx.x * 16 * RT;
+  const int m_base = blockIdx.y * 8 * MT;
+  const int nst = (K + kStageK - 1) / kStageK;
 
-  unsigned long long acc[kRowsPerWarp][MB];
-#pragma unroll
-  for (int r = 0; r < kRowsPerWarp; ++r)
-#pragma unroll
-    for (int m = 0; m < MB; ++m) acc[r][m] = 0ull;
-
-  for (int k = lane * 16; k < K; k += 32 * 16) {
-    uint4 wv[kRowsPerWarp];
-#pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r)
-      wv[r] = (n0 + r < N) ? ld_stream(w + (int64_t)(n0 + r) * K + k) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      unsigned long long xf[MB][4];
-#pragma unroll
-      for (int m = 0; m < MB; ++m) {
-        if (m < mcount) {
-          const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(x + (int64_t)(m0 + m) * K + k + 8 * half));
-          xf[m][0] = x2_to_f2<XT>(xv.x);
-          xf[m][1] = x2_to_f2<XT>(xv.y);
-          xf[m][2] = x2_to_f2<XT>(xv.z);
-          xf[m][3] = x2_to_f2<XT>(xv.w);
-        } else {
-          xf[m][0] = xf[m][1] = xf[m][2] = xf[m][3] = 0ull;
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < kRowsPerWarp; ++r) {
-        unsigned long long wf[4];
-        i8x4_to_f2x2(half ? wv[r].z : wv[r].x, wf[0], wf[1]);
-        i8x4_to_f2x2(half ? wv[r].w : wv[r].y, wf[2], wf[3]);
-#pragma unroll
-        for (int m = 0; m < MB; ++m)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) ffma2(acc[r][m], wf[j], xf[m][j]);
-      }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], kCWarps);
     }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    any_fail = 0;
+  }
+  __syncthreads();
+
+  if (warp == kCWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      bool ok = true;
+      for (int s = 0; s < nst; ++s) {
+        const int slot = s % ST;
+        if (s >= ST && !mbar_wait(&empty_bar[slot], (uint32_t)((s / ST - 1) & 1))) {
+          atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        const int k0 = s * kStageK;
+        const int boxes = min(kCWarps, (K - k0 + kBoxK - 1) / kBoxK);
+        mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(boxes * kBoxBytes));
+        for (int bx = 0; bx < boxes; ++bx)
+          tma_load_2d(ring + slot * kStageBytes + bx * kBoxBytes, &tmW, &full_bar[slot], k0 + bx * kBoxK, n_base);
+      }
+      // drain: the copies of the last stages land before this CTA can finish
+      for (int s = max(0, nst - ST); s < nst && ok; ++s)
+        if (!mbar_wait(&full_bar[s % ST], (uint32_t)((s / ST) & 1))) atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
+    }
+    return;
   }
 
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, j = lane & 3;
+  float acc[RT][MT][4];
 #pragma unroll
-  for (int r = 0; r < kRowsPerWarp; ++r) {
-    const int n = n0 + r;
+  for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
-    for (int m = 0; m < MB; ++m) {
-      const float2 p = u2f(acc[r][m]);
-      float v = p.x + p.y;
+    for (int nt = 0; nt < MT; ++nt)
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      if (lane == 0 && n < N && m < mcount) {
-        v *= load_f(scale, scale_dt, n);
-        if (bias) v += Elem<XT>::to_f(bias[n]);
-        y[(int64_t)(m0 + m) * N + n] = Elem<XT>::from_f(v);
+      for (int e = 0; e < 4; ++e) acc[rt][nt][e] = 0.f;
+
+  // x: this thread's 32 values of row m (k = box + 32j .. +31) as 4 x 16 bytes, zero past M / K
+  auto load_x = [&](int nt, int kbox, uint4 (&xv)[4]) {
+    const int m = m_base + nt * 8 + g;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int k = kbox + 32 * j + 8 * c;
+      xv[c] = (m < M && k < K) ? ld_x(x + (int64_t)m * K + k) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  constexpr int XPF = MT < 2 ? MT : 2;  // n-tiles whose x is fetched before the stage wait
+  for (int s = 0; s < nst; ++s) {
+    const int slot = s % ST;
+    const int kbox = s * kStageK + warp * kBoxK;
+    uint4 xpf[XPF][4];
+#pragma unroll
+    for (int nt = 0; nt < XPF; ++nt) load_x(nt, kbox, xpf[nt]);
+    if (!mbar_wait(&full_bar[slot], (uint32_t)((s / ST) & 1))) {
+      atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
+      any_fail = 1;
+      break;
+    }
+    if (kbox < K) {
+      const uint32_t box = smem_u32(ring + slot * kStageBytes + warp * kBoxBytes);
+      // weights: rows g and g+8 of each row tile, 32 bytes each = 16-byte chunks 2j and 2j+1 of
+      // the 128-byte row, stored at chunk ^ (row & 7) by the 128-byte swizzle
+      uint4 wv[RT][2][2];
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int r = rt * 16 + g + hr * 8;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            wv[rt][hr][c] = lds128(box + r * kBoxK + (((2 * j + c) ^ (r & 7)) << 4));
+        }
+#pragma unroll
+      for (int nt = 0; nt < MT; ++nt) {
+        uint4 xl[4];
+        if (nt < XPF) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) xl[c] = xpf[nt < XPF ? nt : 0][c];
+        } else {
+          load_x(nt, kbox, xl);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {  // word u of the thread's 32 bytes: k = box + 32j + 4u + {0..3}
+          const uint4 xa = xl[u >> 1];
+          const uint32_t b0 = (u & 1) ? xa.z : xa.x;
+          const uint32_t b1 = (u & 1) ? xa.w : xa.y;
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt) {
+            const uint32_t w0 = (&wv[rt][0][u >> 2].x)[u & 3] ^ 0x80808080u;
+            const uint32_t w1 = (&wv[rt][1][u >> 2].x)[u & 3] ^ 0x80808080u;
+            mma16816<XT>(acc[rt][nt], i8pair<XT, 0x4140u>(w0), i8pair<XT, 0x4140u>(w1),
+                         i8pair<XT, 0x4342u>(w0), i8pair<XT, 0x4342u>(w1), b0, b1);
+          }
+        }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[slot]);
+  }
+
+  // ---- sum the consumer warps' partial tiles (layout [warp][rt][nt][e][lane]) ----
+#pragma unroll
+  for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+    for (int nt = 0; nt < MT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[warp * P + ((rt * MT + nt) * 4 + e) * 32 + lane] = acc[rt][nt][e];
+  asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
+  if (any_fail) return;  // a stage never arrived: leave the rows unwritten (error word set)
+  for (int pos = threadIdx.x; pos < P; pos += kCWarps * 32) {
+    float v = 0.f;
+#pragma unroll
+    for (int wp = 0; wp < kCWarps; ++wp) v += red[wp * P + pos];
+    const int ln = pos & 31, e = (pos >> 5) & 3, tile = pos >> 7;
+    const int rt = tile / MT, nt = tile - rt * MT;
+    const int row = (ln >> 2) + ((e & 2) ? 8 : 0), col = (ln & 3) * 2 + (e & 1);
+    const int n = n_base + rt * 16 + row, m = m_base + nt * 8 + col;
+    if (n < N && m < M) {
+      v *= load_f(scale, scale_dt, n);
+      if (bias) v += Elem<XT>::to_f(bias[n]);
+      y[(int64_t)m * N + n] = Elem<XT>::from_f(v);
+    }
+  }
+}
+
+// 2-D map over W [N, K] int8: box 128 k x 16*RT rows, 128-byte swizzle, zero fill past the
+// edges.  Encoded maps are cached (a model calls the same weights every step).
+struct WMapKey {
+  const void *w;
+  int N, K, rows;
+  bool operator==(const WMapKey &o) const { return w == o.w && N == o.N && K == o.K && rows == o.rows; }
+};
+
+bool weight_map(CUtensorMap *m, const int8_t *w, int N, int K, int rows) {
+  constexpr size_t kSlots = 512;
+  static std::mutex mu;
+  static std::vector<std::pair<WMapKey, CUtensorMap>> cache;
+  static size_t next = 0;
+  const WMapKey key{w, N, K, rows};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto &e : cache)
+      if (e.first == key) {
+        *m = e.second;
+        return true;
+      }
+  }
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)N};
+  cuuint64_t gstr[1] = {(cuuint64_t)K};
+  cuuint32_t box[2] = {(cuuint32_t)kBoxK, (cuuint32_t)rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(w), gdim, gstr, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() < kSlots) {
+    cache.emplace_back(key, *m);
+  } else {
+    cache[next] = {key, *m};
+    next = (next + 1) % kSlots;
+  }
+  return true;
+}
+
+template <typename XT, int RT, int MT>
+int launch_cfg(const void *x, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
+               int K, cudaStream_t st) {
+  constexpr int ST = ring_stages<RT>();
+  const size_t smem = 1024 + (size_t)ST * kStageK * 16 * RT + sizeof(float) * kCWarps * RT * MT * 128;
+  auto kern = int8_tma_kernel<XT, RT, MT>;
+  {
+    static std::mutex mu;
+    static std::vector<int> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)done.size() <= dev) done.resize(dev + 1, 0);
+    if (!done[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_linear: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      done[dev] = 1;
+    }
+  }
+  CUtensorMap map;
+  if (!weight_map(&map, w, N, K, 16 * RT)) return fail(HELM_ERR_CUDA, "int8_linear: cuTensorMapEncodeTiled failed");
+  const dim3 grid((N + 16 * RT - 1) / (16 * RT), (M + 8 * MT - 1) / (8 * MT));
+  kern<<<grid, kThreadsT, smem, st>>>(map, static_cast<const XT *>(x), scale, sdt, static_cast<const XT *>(bias),
+                                       static_cast<XT *>(y), M, N, K);
+  return check_launch("int8_tma_kernel");
+}
+
+// Rows per CTA: the fewest row tiles (16 rows each, at most 4) for which every CTA is resident
+// at once -- 3 CTAs per SM with one tile (64 KB ring), 2 with more (96 KB ring).
+template <typename XT, int MT>
+int launch_m(const void *x, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
+             int K, cudaStream_t st) {
+  const int sms = num_sms();
+  const int tiles = (N + 15) / 16;
+  if constexpr (MT >= 4) {  // wide x tiles: one row tile per CTA (register budget)
+    return launch_cfg<XT, 1, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
+  } else {
+    if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
+    if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
+    if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
+    return launch_cfg<XT, 4, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
   }
 }
 
 template <typename XT>
 int launch(const void *x, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
            int K, cudaStream_t st) {
-  const XT *xp = static_cast<const XT *>(x);
-  const XT *bp = static_cast<const XT *>(bias);
-  XT *yp = static_cast<XT *>(y);
-  const int gx = (N + kRowsPerBlock - 1) / kRowsPerBlock;
-  if (M == 1) {
-    int8_gemv_kernel<XT, 1><<<dim3(gx, 1), 256, 0, st>>>(xp, w, scale, sdt, bp, yp, M, N, K);
-  } else if (M == 2) {
-    int8_gemv_kernel<XT, 2><<<dim3(gx, 1), 256, 0, st>>>(xp, w, scale, sdt, bp, yp, M, N, K);
-  } else if (M <= 4) {
-    int8_gemv_kernel<XT, 4><<<dim3(gx, 1), 256, 0, st>>>(xp, w, scale, sdt, bp, yp, M, N, K);
-  } else {
-    int8_gemv_kernel<XT, 8><<<dim3(gx, (M + 7) / 8), 256, 0, st>>>(xp, w, scale, sdt, bp, yp, M, N, K);
-  }
-  return check_launch("int8_gemv_kernel");
+  if (M <= 8) return launch_m<XT, 1>(x, w, scale, sdt, bias, y, M, N, K, st);
+  if (M <= 16) return launch_m<XT, 2>(x, w, scale, sdt, bias, y, M, N, K, st);
+  if (M <= 32) return launch_m<XT, 4>(x, w, scale, sdt, bias, y, M, N, K, st);
+  return launch_m<XT, 8>(x, w, scale, sdt, bias, y, M, N, K, st);
 }
 
 }  // namespace
@@ -167,7 +391,22 @@ extern "C" int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
   if (!x || !w || !w_scale || !y) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear: null pointer");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)
     return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear: x and w must be 16-byte aligned");
+  if ((int64_t)M > 65535ll * 8) return fail(HELM_ERR_UNSUPPORTED, "int8_linear: M=%d too large", M);
   cudaStream_t st = as_stream(stream);
   return x_dtype == HELM_F16 ? launch<__half>(x, w, w_scale, scale_dtype, bias, y, M, N, K, st)
                              : launch<__nv_bfloat16>(x, w, w_scale, scale_dtype, bias, y, M, N, K, st);
+}
+
+extern "C" int helm_int8_linear_error(int32_t *flag_out, int32_t reset) {
+  using namespace helm;
+  if (!flag_out) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear_error: null pointer");
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_int8_error, sizeof(int));
+  if (e == cudaSuccess && reset && v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_int8_error, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_linear_error: %s", cudaGetErrorString(e));
+  *flag_out = v;
+  return HELM_OK;
 }

@@ -190,6 +190,13 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
     return y.reshape(*lead, Nn)
 
 
+def int8_linear_error(reset: bool = True) -> int:
+    """HELM_DEVERR_* bits raised by the INT8 kernels since the last reset (synchronises)."""
+    v = ctypes.c_int32(0)
+    N.check("helm_int8_linear_error", N.lib().helm_int8_linear_error(ctypes.byref(v), 1 if reset else 0))
+    return v.value
+
+
 def make_append_params(k_new, v_new, k_base, v_base, *, page_stride, head_stride, num_pool_pages, page_size,
                        dest=None, dest_host=None, page_table=None, page_used=None, num_pages=None,
                        spare_pages=None, spare_next=None, error_flag=None) -> N.KVAppendParams:

@@ -198,12 +198,20 @@ int helm_lse_merge(const float *partials, int32_t num_partials,
  *   y[m, n] = (sum_k x[m, k] * w[n, k]) * w_scale[n] + bias[n]
  * x [M, K] (F16 or BF16), w [N, K] int8 row-major, w_scale [N] (F16, BF16 or
  * F32), bias [N] (same dtype as x) or null, y [M, N] of x_dtype.  fp32
- * accumulation.  Any M >= 1; K must be a multiple of 16.
+ * accumulation.  Any M >= 1; K must be a multiple of 16; x and w 16-byte
+ * aligned.  The weight streams through a TMA + mbarrier ring; the call encodes
+ * (and caches) a tensor map over w on its first use.
  */
 int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
                      const void *w_scale, int32_t scale_dtype,
                      const void *bias, void *y, int32_t M, int32_t N,
                      int32_t K, void *stream);
+
+/* HELM_DEVERR_* bits raised by the INT8 kernels since the last reset (a bounded
+ * wait of the weight pipeline that gave up: HELM_DEVERR_TIMEOUT; the rows of
+ * that CTA are then left unwritten).  Synchronises with the device; reset != 0
+ * clears the word.  No counterpart in the reference. */
+int helm_int8_linear_error(int32_t *flag_out, int32_t reset);
 
 /* ---- KV append ------------------------------------------------------------ */
 /*

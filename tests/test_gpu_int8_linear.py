@@ -40,6 +40,7 @@ def test_config2_shapes(shape, M, cuda):
     ref = int8_linear_ref(x.double().numpy(), w, s)
     assert y.shape == (M, N) and y.dtype == torch.float16
     assert rel_err(y, ref) <= TOL
+    assert ops.int8_linear_error() == 0
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 5, 9, 16, 17])
@@ -80,3 +81,32 @@ def test_rejects_bad_k(cuda):
     with pytest.raises(HelmError):
         ops.int8_linear(torch.zeros(1, 24, dtype=torch.float16, device=cuda), w,
                         torch.ones(8, dtype=torch.float16, device=cuda))
+
+
+@pytest.mark.parametrize("N,K", [(1024, 16384),   # few long rows: K split over a 4-CTA cluster
+                                 (2048, 8192),    # 2-CTA cluster
+                                 (20000, 4096),   # 32 rows per CTA, ragged last tile
+                                 (77, 16), (130, 48), (64, 272), (96, 4112)])  # K tails below 256
+@pytest.mark.parametrize("M", [1, 8, 9, 33, 64, 70])
+@pytest.mark.parametrize("xdtype", [torch.float16, torch.bfloat16])
+def test_split_and_tail_shapes(N, K, M, xdtype, cuda):
+    """Every work split (rows per CTA, cluster K split, K tails, M past 8/16/32/64) against the
+    float64 oracle; the tensor-core products are exact and accumulate in fp32, so the error is
+    the output rounding: max |y - ref| <= 4e-3 * max |ref|."""
+    from helm_b200 import ops
+    w, s, x = _inputs(M, N, K, seed=N * 7 + K + M, xdtype=xdtype)
+    bias = torch.randn(N, dtype=torch.float32).to(xdtype)
+    y = ops.int8_linear(x.to(cuda), torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda),
+                        bias=bias.to(cuda))
+    ref = int8_linear_ref(x.double().numpy(), w, s, bias.double().numpy())
+    assert y.shape == (M, N) and y.dtype == xdtype
+    assert rel_err(y, ref) <= 4e-3 * (2.0 if xdtype == torch.bfloat16 else 1.0)
+    assert ops.int8_linear_error() == 0
+
+
+def test_repeated_calls_identical(cuda):
+    """Deterministic: the K split and its reduction order are fixed, so two calls agree bit for bit."""
+    from helm_b200 import ops
+    w, s, x = _inputs(4, 1024, 16384, seed=5)
+    wd, sd, xd = torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda), x.to(cuda)
+    assert torch.equal(ops.int8_linear(xd, wd, sd), ops.int8_linear(xd, wd, sd))
