@@ -47,8 +47,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
-    ap.add_argument("--workload", default="config5", choices=["config5", "config2"],
-                    help="config5: the sharded decode-attention stack (default); config2: INT8 GEMV shapes")
+    ap.add_argument("--workload", default="config5", choices=["config5", "config2", "config1", "config3"],
+                    help="config5: the sharded decode-attention stack (default); config2: INT8 GEMV shapes; "
+                         "config1: the reference's single-layer mixed-residency fp32 case; config3: a "
+                         "Qwen3-8B-shaped decode step through KVOffloadManager")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--exchange", default="fused", choices=["fused", "p2p", "nccl"],
@@ -712,6 +714,307 @@ def run_reference_config2(args, rank):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------
+# config 1: the reference's own CPU case -- one layer, 4096 fp32 tokens, half of the pages on the host
+# ----------------------------------------------------------------------------
+C1 = dict(Hq=32, Hkv=8, D=128, P=64, ctx=4096, offloaded=32)
+C1_METRIC = "single-layer paged decode attention: algorithmic GB/s (config1, fp32, 32 of 64 pages host-resident)"
+C1_WORKLOAD = ("config1: batch 1, 32q/8kv heads, d128, 4096 fp32 tokens in 64-token pages, first 32 pages offloaded "
+               "to pinned host memory, scale 1/sqrt(128), seed 0")
+C1_BYTES = 2 * C1["Hkv"] * C1["ctx"] * C1["D"] * 4 + C1["Hq"] * C1["D"] * 4 * 2
+
+
+def _c1_manager(dev, seed):
+    from helm_b200.runtime import KVAllocator, KVCacheManager
+    c = C1
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(1, c["Hq"], 1, c["D"], generator=g)
+    k = torch.randn(1, c["Hkv"], c["ctx"], c["D"], generator=g)
+    v = torch.randn(1, c["Hkv"], c["ctx"], c["D"], generator=g)
+    alloc = KVAllocator(num_layers=1, num_kv_heads=c["Hkv"], head_dim=c["D"], page_size=c["P"], dtype=torch.float32)
+    mgr = KVCacheManager(alloc, gpu_high_watermark_bytes=1 << 62)
+    mgr.append_prefill(0, k.to(dev), v.to(dev))
+    return q.to(dev), alloc, mgr
+
+
+def run_config1(args, rank, local, world):
+    """perform_streaming_attention (the drop-in call) on the reference's config 1: pages 0-31 evicted
+    to pinned host memory through KVCacheManager.evict_pages, pages 32-63 resident; every call stages
+    the host pages into device slots and attends over all 64.  Also the kernel alone on 8 all-resident
+    instances (rotating through > 2x L2), from prebuilt device page tables in a CUDA graph."""
+    from helm_b200 import ops
+    from helm_b200.runtime import perform_streaming_attention
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_pg(world, local)
+    stream = torch.cuda.current_stream(dev)
+    c = C1
+    clocks = ClockSampler(gpu_selector(dev, local))
+    clocks.start()
+    t_load0 = time.time()
+    # --- the drop-in call with half of the pages on the host ---
+    q, alloc, mgr = _c1_manager(dev, 0)
+    page_bytes = 2 * c["Hkv"] * c["P"] * c["D"] * 4
+    mgr.evict_pages(c["offloaded"] * page_bytes)
+    pages = mgr.iterate_layer_pages(0)
+    n_cpu = sum(p.state == "CPU" for p in pages)
+    for _ in range(max(args.warmup, 3)):
+        perform_streaming_attention(q, pages)
+    torch.cuda.synchronize(dev)
+    steps = max(args.steps, 10)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        out = perform_streaming_attention(q, pages)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    mixed_ms = e0.elapsed_time(e1) / steps
+    # e2e: q from pinned host memory, the output read back every call
+    q_h = q.cpu().pin_memory()
+    o_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    e0.record(stream)
+    for _ in range(steps):
+        o_h.copy_(perform_streaming_attention(q_h.to(dev, non_blocking=True), pages), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / steps
+    # --- the kernel alone: 8 all-resident instances, prebuilt tables, CUDA graph ---
+    inst = []
+    for i in range(8):
+        qi, alloc_i, mgr_i = _c1_manager(dev, 100 + i)
+        store = alloc_i.store(dev)
+        pl = mgr_i.iterate_layer_pages(0)
+        pt = torch.tensor([[p.slot for p in pl]], dtype=torch.int32, device=dev)
+        pu = torch.tensor([[p.used_tokens for p in pl]], dtype=torch.int32, device=dev)
+        npg = torch.tensor([len(pl)], dtype=torch.int32, device=dev)
+        kb, vb = store.base_ptrs()
+        inst.append((qi.view(1, c["Hq"], c["D"]).contiguous(), store, pt, pu, npg, alloc_i, mgr_i))
+    outs = [torch.empty(1, c["Hq"], c["D"], device=dev) for _ in inst]
+
+    def calls():
+        for (qi, store, pt, pu, npg, _, _), o in zip(inst, outs):
+            ops.paged_decode_attention(qi, store.slab[:, 0], store.slab[:, 1], pt, pu, npg, num_kv_heads=c["Hkv"],
+                                       page_size=c["P"], page_stride=store.page_elems, head_stride=store.head_stride,
+                                       num_pool_pages=store.capacity, out=o)
+    for _ in range(3):
+        calls()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        calls()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    reps = max(args.steps // 5, 5)
+    e0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    kern_ms = e0.elapsed_time(e1) / (reps * len(inst))
+    del graph
+    clk = clocks.stop(t_load0, time.time())
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        gbs = C1_BYTES / (mixed_ms * 1e-3) / 1e9
+        kgbs = C1_BYTES / (kern_ms * 1e-3) / 1e9
+        cpu = None
+        if not args.no_cpu_baseline:
+            from oracle.cpu_baseline import time_decode_attention
+            t2, n2, threads = time_decode_attention(c["Hq"], c["Hkv"], c["D"], c["P"], c["ctx"], torch.float32,
+                                                    path=2, min_seconds=3.0, max_calls=30)
+            t3, n3, _ = time_decode_attention(c["Hq"], c["Hkv"], c["D"], c["P"], c["ctx"], torch.float32,
+                                              path=3, min_seconds=3.0, max_calls=30)
+            cpu = {"value": C1_BYTES / t2 / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                   "sample": (f"reference all-CPU path (kv_cache.py:376-380) ported, config 1, median of {n2} calls "
+                              f"({t2 * 1e3:.2f} ms); its Path-3 loop (kv_cache.py:387-442): {t3 * 1e3:.2f} ms")}
+        line = {
+            "metric": C1_METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": mixed_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "timing": "perform_streaming_attention per call (host pages staged every call), CUDA events",
+            "config": {"workload": C1_WORKLOAD, "parallelism": "single GPU",
+                       "l2": "mixed path: host pages cross PCIe every call; kernel-only: 8 instances (268 MB)"},
+            "pages_on_host": n_cpu, "h2d_bytes_per_call": n_cpu * page_bytes,
+            "kernel_only": {"ms": kern_ms, "gbs": kgbs, "frac": kgbs / hbm_peak,
+                            "how": "all 64 pages resident, 8 instances rotating, CUDA graph"},
+            "roofline": {"bound": "hbm", "achieved": kgbs, "peak": hbm_peak, "unit": "GB/s", "frac": kgbs / hbm_peak,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "paged attention (fp32 pages: attn_generic_kernel path), kernel-only timing",
+                         "bytes_per_launch": C1_BYTES, "avg_launch_ms": kern_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": C1_BYTES / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step":
+                    q_h.numel() * 4 + n_cpu * page_bytes, "d2h_bytes_per_step": o_h.numel() * 4, "ms_per_step": e2e_ms,
+                    "api": "helm_b200.runtime.perform_streaming_attention, q from pinned host, output read back"},
+            "gpu_launches": None,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(world)
+
+
+def run_reference_config1(args, rank):
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import time_decode_attention
+    c = C1
+    t2, n2, threads = time_decode_attention(c["Hq"], c["Hkv"], c["D"], c["P"], c["ctx"], torch.float32, path=2,
+                                            min_seconds=3.0, max_calls=max(args.steps, 20))
+    v = C1_BYTES / t2 / 1e9
+    line = {"impl": "reference", "metric": C1_METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": n2, "warmup": 1, "ms_per_step": t2 * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": C1_WORKLOAD, "parallelism": "host cores"},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"reference all-CPU path ported, median of {n2} calls"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# config 3: a Qwen3-8B-shaped decode step through KVOffloadManager (bf16, batch 1, 16384 tokens)
+# ----------------------------------------------------------------------------
+C3 = dict(layers=36, hidden=4096, heads=32, kv_heads=8, head_dim=128, inter=12288, vocab=151936, ctx=16384)
+C3_METRIC = "decode tok/s, Qwen3-8B-shaped model through KVOffloadManager (config3, bf16, batch 1, 16384-token paged KV)"
+C3_WORKLOAD = ("config3: random-init Qwen3-8B-shaped decoder (36 layers, hidden 4096, 32/8 heads, d128, SwiGLU "
+               "12288, vocab 151936), bf16, batch 1, 16384-token paged KV (64-token pages, cont_capacity=0)")
+
+
+def c3_step_bytes(model, ctx):
+    """Algorithmic HBM bytes of one decode step: every weight except the embedding table read once
+    (one embedding row), plus K+V of every cached token of every layer."""
+    c = C3
+    tensors = list(model.named_parameters()) + [(n, b) for n, b in model.named_buffers() if "rotary" not in n]
+    w = sum(t.numel() * t.element_size() for n, t in tensors if "embed_tokens" not in n)
+    kv = 2 * c["layers"] * c["kv_heads"] * c["head_dim"] * 2 * ctx
+    return w + c["hidden"] * 2 + kv
+
+
+def run_config3(args, rank, local, world):
+    """Decode steps of a random-init Qwen3-8B-shaped HF model whose attention forwards are patched by
+    KVOffloadManager (paged mode): prefill 16384 random tokens, then greedy decode one token per
+    step, the token fed back on the device.  `value` times K steps with CUDA events (the host-side
+    runtime included: this path is not graph-captured); `e2e` also reads every token back to the host."""
+    import transformers
+    from helm_b200.runtime import KVOffloadConfig, KVOffloadManager
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_pg(world, local)
+    stream = torch.cuda.current_stream(dev)
+    c = C3
+    cfg = transformers.Qwen3Config(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["inter"],
+                                   num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
+                                   num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], rope_theta=1e6,
+                                   max_position_embeddings=40960, rms_norm_eps=1e-6, tie_word_embeddings=False)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = transformers.Qwen3ForCausalLM(cfg).eval()
+    torch.set_default_dtype(prev)
+    # config 3 keeps the whole KV on the device (the reference's default watermark, 512 tokens per
+    # layer, is sized for consumer GPUs and would stream the rest over PCIe every step)
+    mgr = KVOffloadManager(model, KVOffloadConfig.from_model(model, page_size=64, cont_capacity=0,
+                                                             gpu_watermark_bytes=1 << 40), batch_size=1)
+    ctx = c["ctx"]
+    g = torch.Generator(device=dev).manual_seed(0)
+    ids = torch.randint(0, c["vocab"], (1, ctx), generator=g, device=dev)
+    clocks = ClockSampler(gpu_selector(dev, local))
+    clocks.start()
+    t_load0 = time.time()
+    with torch.no_grad():
+        mask = torch.full((ctx, ctx), torch.finfo(torch.bfloat16).min, device=dev, dtype=torch.bfloat16).triu_(1)
+        logits = model(input_ids=ids, attention_mask=mask[None, None], position_ids=torch.arange(ctx, device=dev)[None],
+                       use_cache=False, logits_to_keep=1).logits
+        del mask
+        tok = logits[:, -1:].argmax(-1)
+        pos = ctx
+
+        def step(tok, pos):
+            m = torch.zeros((1, 1, 1, pos + 1), device=dev, dtype=torch.bfloat16)
+            lg = model(input_ids=tok, attention_mask=m, position_ids=torch.tensor([[pos]], device=dev),
+                       use_cache=False, logits_to_keep=1).logits
+            return lg[:, -1:].argmax(-1)
+        for _ in range(max(args.warmup, 3)):
+            tok = step(tok, pos)
+            pos += 1
+        torch.cuda.synchronize(dev)
+        steps = min(max(args.steps, 10), 100)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            tok = step(tok, pos)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+        ctx_mid = pos - steps // 2
+        # e2e: the token read back to the host every step (what a serving loop does)
+        e0.record(stream)
+        for _ in range(steps):
+            tok = step(tok, pos)
+            pos += 1
+            tok_host = int(tok.item())
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = e0.elapsed_time(e1) / steps
+        # the same model with INT8 weight-only linears (patch_int8_linears), same cache
+        bf16_bytes = c3_step_bytes(model, ctx_mid)
+        from helm_b200.kernels import patch_int8_linears
+        n_int8 = patch_int8_linears(model)
+        torch.cuda.empty_cache()
+        for _ in range(3):
+            tok = step(tok, pos)
+            pos += 1
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(steps):
+            tok = step(tok, pos)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        int8_ms = e0.elapsed_time(e1) / steps
+        int8_bytes = c3_step_bytes(model, pos - steps // 2)
+    clk = clocks.stop(t_load0, time.time())
+    err = int(mgr.batch.error_flag.item()) if getattr(mgr, "batch", None) is not None else 0
+    rep = mgr.report()
+    mgr.restore()
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        tok_s = 1.0 / (ms * 1e-3)
+        ach = bf16_bytes / (ms * 1e-3) / 1e9
+        line = {
+            "metric": C3_METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random token ids)",
+            "timing": "eager model.forward per token (host runtime included), CUDA events",
+            "config": {"workload": C3_WORKLOAD, "model": "Qwen3-8B-shaped (random init)", "global_batch": 1,
+                       "seq_len": ctx, "parallelism": "single GPU", "l2": "weights 15 GB + KV per step >> L2"},
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm_peak, "unit": "GB/s", "frac": ach / hbm_peak,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "whole decode step (weights + KV of every layer read once)",
+                         "bytes_per_step": bf16_bytes},
+            "int8_linears": {"replaced": n_int8, "ms_per_step": int8_ms, "tok_s": 1.0 / (int8_ms * 1e-3),
+                             "algorithmic_gbs": int8_bytes / (int8_ms * 1e-3) / 1e9},
+            "cpu_baseline": None,
+            "e2e": {"value": 1.0 / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 8, "ms_per_step": e2e_ms,
+                    "api": "model.forward with KVOffloadManager patches; the token read back every step"},
+            "gpu_launches": None, "clocks": clk, "device_error_flag": err, "kv_report": rep,
+        }
+        print(json.dumps(line, default=str), flush=True)
+    del model
+    barrier(world)
+
+
+def run_reference_config3(args, rank):
+    if rank != 0:
+        return
+    print(json.dumps({"impl": "reference", "unavailable": "config 3 is a full 8B-parameter model decode; the "
+                      "reference's CPU path is infeasible at this size on the host cores (its per-layer CPU "
+                      "attention is timed by --workload config1 and config5)"}), flush=True)
+
+
 def cpu_baseline():
     from oracle.cpu_baseline import time_decode_attention
     c = CFG
@@ -732,6 +1035,18 @@ def main():
             run_reference_config2(args, rank)
         else:
             run_config2(args, rank, local, world)
+        return
+    if args.workload == "config1":
+        if args.impl == "reference":
+            run_reference_config1(args, rank)
+        else:
+            run_config1(args, rank, local, world)
+        return
+    if args.workload == "config3":
+        if args.impl == "reference":
+            run_reference_config3(args, rank)
+        else:
+            run_config3(args, rank, local, world)
         return
     if args.impl == "reference":
         run_reference(args, rank)
