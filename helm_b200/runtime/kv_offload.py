@@ -124,6 +124,18 @@ def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_g
     dev = q.device
     alloc = kvcms[0].allocator
     store = alloc.store(dev)
+    if batch.graph is not None:
+        # CUDA-graph decode (runtime/graph.py): the append picks its page on the device and the
+        # host mirrors it after the step, so nothing here reads or changes host state
+        from .graph import device_append
+        device_append(batch, l, k, v, store)
+        Hq, D = q.shape[1], q.shape[-1]
+        q3 = q.reshape(B, Hq, D)
+        if not q3.is_contiguous():
+            q3 = q3.contiguous()
+        out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
+        _attend_batch(batch, l, q3, scale, store, False, out=out, out_record=None)
+        return out.reshape(B, Hq, 1, D)
     append = shard is None or shard.rank == shard.world - 1
     if append:
         _append_batch(batch, l, k, v, all_gpu, store, dev)

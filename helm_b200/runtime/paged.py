@@ -182,6 +182,7 @@ class DecodeBatch:
         self.error_flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.dest = np.zeros((self.B, 3), dtype=np.int32)
         self.cont = None          # ContiguousBatch when the contiguous fast path is active
+        self.graph = None         # DecodeGraph while a decode step is being captured or warmed up
         self._rec = None
         for i, m in enumerate(self.kvcms):
             m._batch = (self, i)
