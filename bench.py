@@ -915,7 +915,8 @@ def run_config3(args, rank, local, world):
     # config 3 keeps the whole KV on the device (the reference's default watermark, 512 tokens per
     # layer, is sized for consumer GPUs and would stream the rest over PCIe every step)
     mgr = KVOffloadManager(model, KVOffloadConfig.from_model(model, page_size=64, cont_capacity=0,
-                                                             gpu_watermark_bytes=1 << 40), batch_size=1)
+                                                             gpu_watermark_bytes=1 << 40), batch_size=1,
+                           fused_norms=True)
     ctx = c["ctx"]
     g = torch.Generator(device=dev).manual_seed(0)
     ids = torch.randint(0, c["vocab"], (1, ctx), generator=g, device=dev)
@@ -1004,9 +1005,9 @@ def run_config3(args, rank, local, world):
             "metric": C3_METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random token ids)",
-            "timing": ("DecodeGraph: the whole decode step (model.forward with the KVOffloadManager patches) "
-                       "captured in one CUDA graph and replayed per token, host bookkeeping mirrored after "
-                       "each replay; CUDA events"),
+            "timing": ("DecodeGraph: the whole decode step (model.forward with the KVOffloadManager patches, "
+                       "fused decode prologue and fused RMSNorm) captured in one CUDA graph and replayed per "
+                       "token, host bookkeeping mirrored after each replay; CUDA events"),
             "eager": {"ms_per_step": eager_ms, "tok_s": 1.0 / (eager_ms * 1e-3),
                       "how": "the same model.forward called eagerly per token"},
             "config": {"workload": C3_WORKLOAD, "model": "Qwen3-8B-shaped (random init)", "global_batch": 1,

@@ -74,6 +74,17 @@ class KVAppendParams(ctypes.Structure):
     ]
 
 
+class DecodePrologueParams(ctypes.Structure):
+    _fields_ = [
+        ("append", KVAppendParams),
+        ("q_in", _p), ("q_out", _p), ("Hq", _i32),
+        ("q_stride", _i64), ("k_stride", _i64), ("v_stride", _i64),
+        ("q_norm_w", _p), ("k_norm_w", _p), ("norm_dtype", _i32), ("eps", ctypes.c_float),
+        ("cos", _p), ("sin", _p), ("cs_dtype", _i32), ("cs_stride", _i64),
+        ("do_append", _i32),
+    ]
+
+
 class GatherMergeParams(ctypes.Structure):
     _fields_ = [
         ("rank", _i32), ("world", _i32), ("rows", _i32), ("D", _i32),
@@ -94,6 +105,8 @@ SIGNATURES = [
     ("helm_int8_linear", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
     ("helm_int8_linear_error", _c.c_int, [_p, _i32]),
     ("helm_kv_append", _c.c_int, [_c.POINTER(KVAppendParams), _p]),
+    ("helm_decode_prologue", _c.c_int, [_c.POINTER(DecodePrologueParams), _p]),
+    ("helm_rmsnorm", _c.c_int, [_p, _i32, _i64, _p, _i32, _p, _i64, _i64, _i32, ctypes.c_float, _p]),
     ("helm_copy_pages", _c.c_int, [_p, _i64, _p, _p, _i32, _i64, _c.POINTER(_i32), _p]),
     ("helm_gather_merge_state_bytes", _i64, [_i32, _i32, _i32, _c.POINTER(_i64), _c.POINTER(_i64),
                                               _c.POINTER(_i64)]),

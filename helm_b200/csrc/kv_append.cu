@@ -27,65 +27,69 @@ struct AppendArgs {
   int32_t hdest[kHostDestRows][3];     // host-directed rows, by value
 };
 
+// Destination of sequence b's new token: (page id, slot), with the page table updated; pid = -1
+// (and an error bit) when the destination is invalid.  Run by one thread.
+__device__ void resolve_dest(const AppendArgs &a, int b, int local, int &pid_out, int &slot_out) {
+  int pid = -1, slot = -1;
+  int32_t *pt = a.page_table ? a.page_table + (int64_t)b * a.pt_stride : nullptr;
+  int32_t *pu = a.page_used ? a.page_used + (int64_t)b * a.pt_stride : nullptr;
+  if (a.dest || a.use_hdest) {
+    const int32_t *row = a.use_hdest ? a.hdest[local] : a.dest + 3 * b;
+    pid = row[0];
+    const int li = row[1];
+    slot = row[2];
+    const bool ok = pid >= 0 && pid < a.num_pool_pages && slot >= 0 && slot < a.P;
+    if (!ok) {
+      flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
+      pid = -1;
+    } else if (pt) {
+      if (li < 0 || li >= a.pt_stride) {
+        flag_error(a.error_flag, HELM_DEVERR_NUM_PAGES);
+        pid = -1;
+      } else {
+        pt[li] = pid;
+        pu[li] = slot + 1;
+        if (a.num_pages[b] < li + 1) a.num_pages[b] = li + 1;
+      }
+    }
+  } else {
+    const int np = a.num_pages[b];
+    const bool np_ok = np >= 0 && np <= a.pt_stride;
+    const int u = (np_ok && np > 0) ? pu[np - 1] : a.P;
+    if (!np_ok) {
+      flag_error(a.error_flag, HELM_DEVERR_NUM_PAGES);
+    } else if (u < a.P) {
+      pid = pt[np - 1];
+      slot = u;
+      pu[np - 1] = u + 1;
+    } else {
+      const int j = a.spare_next ? a.spare_next[b] : a.spare_stride;
+      if (j >= a.spare_stride || np >= a.pt_stride) {
+        flag_error(a.error_flag, HELM_DEVERR_APPEND_FULL);
+      } else {
+        pid = a.spare_pages[(int64_t)b * a.spare_stride + j];
+        a.spare_next[b] = j + 1;
+        slot = 0;
+        pt[np] = pid;
+        pu[np] = 1;
+        a.num_pages[b] = np + 1;
+      }
+    }
+    if (pid >= a.num_pool_pages || (pid < 0 && slot >= 0)) {
+      flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
+      pid = -1;
+    }
+  }
+  pid_out = pid;
+  slot_out = slot;
+}
+
 // One CTA per sequence: thread 0 resolves the destination (page id, slot),
 // then the CTA copies Hkv*D elements of K and of V.
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   __shared__ int s_pid, s_slot;
   const int b = a.b0 + blockIdx.x;
-  if (threadIdx.x == 0) {
-    int pid = -1, slot = -1;
-    int32_t *pt = a.page_table ? a.page_table + (int64_t)b * a.pt_stride : nullptr;
-    int32_t *pu = a.page_used ? a.page_used + (int64_t)b * a.pt_stride : nullptr;
-    if (a.dest || a.use_hdest) {
-      const int32_t *row = a.use_hdest ? a.hdest[blockIdx.x] : a.dest + 3 * b;
-      pid = row[0];
-      const int li = row[1];
-      slot = row[2];
-      const bool ok = pid >= 0 && pid < a.num_pool_pages && slot >= 0 && slot < a.P;
-      if (!ok) {
-        flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
-        pid = -1;
-      } else if (pt) {
-        if (li < 0 || li >= a.pt_stride) {
-          flag_error(a.error_flag, HELM_DEVERR_NUM_PAGES);
-          pid = -1;
-        } else {
-          pt[li] = pid;
-          pu[li] = slot + 1;
-          if (a.num_pages[b] < li + 1) a.num_pages[b] = li + 1;
-        }
-      }
-    } else {
-      const int np = a.num_pages[b];
-      const bool np_ok = np >= 0 && np <= a.pt_stride;
-      const int u = (np_ok && np > 0) ? pu[np - 1] : a.P;
-      if (!np_ok) {
-        flag_error(a.error_flag, HELM_DEVERR_NUM_PAGES);
-      } else if (u < a.P) {
-        pid = pt[np - 1];
-        slot = u;
-        pu[np - 1] = u + 1;
-      } else {
-        const int j = a.spare_next ? a.spare_next[b] : a.spare_stride;
-        if (j >= a.spare_stride || np >= a.pt_stride) {
-          flag_error(a.error_flag, HELM_DEVERR_APPEND_FULL);
-        } else {
-          pid = a.spare_pages[(int64_t)b * a.spare_stride + j];
-          a.spare_next[b] = j + 1;
-          slot = 0;
-          pt[np] = pid;
-          pu[np] = 1;
-          a.num_pages[b] = np + 1;
-        }
-      }
-      if (pid >= a.num_pool_pages || (pid < 0 && slot >= 0)) {
-        flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
-        pid = -1;
-      }
-    }
-    s_pid = pid;
-    s_slot = slot;
-  }
+  if (threadIdx.x == 0) resolve_dest(a, b, blockIdx.x, s_pid, s_slot);
   __syncthreads();
   const int pid = s_pid, slot = s_slot;
   if (pid < 0) return;
@@ -99,17 +103,139 @@ __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode prologue: per-head RMSNorm of q and k (Qwen3 q_norm / k_norm), rotary
+// embedding of q and k (x*cos + rotate_half(x)*sin, rotate_half(x) =
+// (-x[D/2:], x[:D/2])), q written out, k and v appended to the pool.  One CTA
+// per sequence, one warp per head; lane l owns the rotary pairs
+// (d, d + D/2) for d = l, l + 32, ...
+// ---------------------------------------------------------------------------
+struct PrologueArgs {
+  const void *q_in;
+  void *q_out;
+  int32_t Hq;
+  int64_t q_stride, k_stride, v_stride;  // elements between sequences of q_in, k_new, v_new
+  const void *q_norm_w, *k_norm_w;
+  int32_t norm_dtype;
+  float eps;
+  const void *cos, *sin;
+  int32_t cs_dtype;
+  int64_t cs_stride;
+  int32_t do_append;
+};
+
+constexpr int kMaxHalfPerLane = 4;  // D <= 256
+
+__device__ __forceinline__ void norm_rope_head(const void *src, int src_dt, int64_t src_off, const void *w,
+                                               int w_dt, float eps, const void *cs_cos, const void *cs_sin,
+                                               int cs_dt, int64_t cs_off, int D, int lane,
+                                               float (&lo)[kMaxHalfPerLane], float (&hi)[kMaxHalfPerLane]) {
+  const int half = D >> 1;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxHalfPerLane; ++i) {
+    const int d = lane + 32 * i;
+    lo[i] = hi[i] = 0.f;
+    if (d < half) {
+      lo[i] = load_f(src, src_dt, src_off + d);
+      hi[i] = load_f(src, src_dt, src_off + d + half);
+      ss = fmaf(lo[i], lo[i], fmaf(hi[i], hi[i], ss));
+    }
+  }
+  if (w) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float r = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < kMaxHalfPerLane; ++i) {
+      const int d = lane + 32 * i;
+      if (d < half) {
+        lo[i] = lo[i] * r * load_f(w, w_dt, d);
+        hi[i] = hi[i] * r * load_f(w, w_dt, d + half);
+      }
+    }
+  }
+  if (cs_cos) {
+#pragma unroll
+    for (int i = 0; i < kMaxHalfPerLane; ++i) {
+      const int d = lane + 32 * i;
+      if (d < half) {
+        const float c0 = load_f(cs_cos, cs_dt, cs_off + d), c1 = load_f(cs_cos, cs_dt, cs_off + d + half);
+        const float s0 = load_f(cs_sin, cs_dt, cs_off + d), s1 = load_f(cs_sin, cs_dt, cs_off + d + half);
+        const float x0 = lo[i], x1 = hi[i];
+        lo[i] = x0 * c0 - x1 * s0;  // rotate_half: first half takes -x[d + D/2]
+        hi[i] = x1 * c1 + x0 * s1;  // second half takes x[d]
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) decode_prologue_kernel(AppendArgs a, PrologueArgs pr) {
+  __shared__ int s_pid, s_slot;
+  const int b = a.b0 + blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  if (threadIdx.x == 0) {
+    if (pr.do_append) {
+      resolve_dest(a, b, blockIdx.x, s_pid, s_slot);
+    } else {
+      s_pid = -1;
+      s_slot = -1;
+    }
+  }
+  __syncthreads();
+  const int pid = s_pid, slot = s_slot;
+  const int D = a.D, half = D >> 1;
+  const int tasks = pr.Hq + (pr.do_append && pid >= 0 ? 2 * a.Hkv : 0);
+  const int64_t cs_off = (int64_t)b * pr.cs_stride;
+  for (int t = warp; t < tasks; t += nwarps) {
+    float lo[kMaxHalfPerLane], hi[kMaxHalfPerLane];
+    if (t < pr.Hq) {  // query head: norm + rope -> q_out
+      norm_rope_head(pr.q_in, a.src_dtype, (int64_t)b * pr.q_stride + (int64_t)t * D, pr.q_norm_w, pr.norm_dtype,
+                     pr.eps, pr.cos, pr.sin, pr.cs_dtype, cs_off, D, lane, lo, hi);
+      const int64_t o = ((int64_t)b * pr.Hq + t) * D;
+#pragma unroll
+      for (int i = 0; i < kMaxHalfPerLane; ++i) {
+        const int d = lane + 32 * i;
+        if (d < half) {
+          store_f(pr.q_out, a.src_dtype, o + d, lo[i]);
+          store_f(pr.q_out, a.src_dtype, o + d + half, hi[i]);
+        }
+      }
+    } else if (t < pr.Hq + a.Hkv) {  // key head: norm + rope -> pool
+      const int h = t - pr.Hq;
+      norm_rope_head(a.k_new, a.src_dtype, (int64_t)b * pr.k_stride + (int64_t)h * D, pr.k_norm_w, pr.norm_dtype,
+                     pr.eps, pr.cos, pr.sin, pr.cs_dtype, cs_off, D, lane, lo, hi);
+      const int64_t dst = (int64_t)pid * a.page_stride + (int64_t)h * a.head_stride + (int64_t)slot * D;
+#pragma unroll
+      for (int i = 0; i < kMaxHalfPerLane; ++i) {
+        const int d = lane + 32 * i;
+        if (d < half) {
+          store_f(a.k_base, a.kv_dtype, dst + d, lo[i]);
+          store_f(a.k_base, a.kv_dtype, dst + d + half, hi[i]);
+        }
+      }
+    } else {  // value head: copy -> pool
+      const int h = t - pr.Hq - a.Hkv;
+      const int64_t src = (int64_t)b * pr.v_stride + (int64_t)h * D;
+      const int64_t dst = (int64_t)pid * a.page_stride + (int64_t)h * a.head_stride + (int64_t)slot * D;
+      for (int d = lane; d < D; d += 32) store_f(a.v_base, a.kv_dtype, dst + d, load_f(a.v_new, a.src_dtype, src + d));
+    }
+  }
+}
+
 }  // namespace helm
 
-extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
-  using namespace helm;
+namespace helm {
+namespace {
+
+int check_append(const helm_kv_append_params *p, bool need_data) {
   if (!p) return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: params is null");
   if (p->B < 0 || p->Hkv <= 0 || p->D <= 0 || p->P <= 0)
     return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: bad sizes B=%d Hkv=%d D=%d P=%d", p->B, p->Hkv, p->D, p->P);
   for (int dt : {p->src_dtype, p->kv_dtype})
     if (dt != HELM_F32 && dt != HELM_F16 && dt != HELM_BF16)
       return fail(HELM_ERR_UNSUPPORTED, "kv_append: dtype %d", dt);
-  if (p->B == 0) return HELM_OK;
+  if (p->B == 0 || !need_data) return HELM_OK;
   if (!p->k_new || !p->v_new || !p->k_base || !p->v_base)
     return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: null data pointer");
   const bool directed = p->dest || p->dest_host;
@@ -117,6 +243,10 @@ extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
     return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: device-directed mode needs page table and spare pages");
   if (directed && p->page_table && (!p->page_used || !p->num_pages))
     return fail(HELM_ERR_INVALID_ARGUMENT, "kv_append: page_table given without page_used/num_pages");
+  return HELM_OK;
+}
+
+AppendArgs append_args(const helm_kv_append_params *p) {
   AppendArgs a{};
   a.k_new = p->k_new;
   a.v_new = p->v_new;
@@ -140,10 +270,16 @@ extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
   a.spare_next = p->spare_next;
   a.spare_stride = p->spare_stride;
   a.error_flag = p->error_flag;
-  cudaStream_t st = as_stream(stream);
+  return a;
+}
+
+// Launches `launch(a, blocks)` once, or once per kHostDestRows sequences with the host-directed
+// rows carried by value.
+template <typename F>
+int launch_rows(const helm_kv_append_params *p, AppendArgs a, F launch, const char *what) {
   if (!p->dest_host) {
-    kv_append_kernel<<<p->B, 256, 0, st>>>(a);
-    return check_launch("kv_append_kernel");
+    launch(a, p->B);
+    return check_launch(what);
   }
   a.use_hdest = 1;
   for (int b0 = 0; b0 < p->B; b0 += kHostDestRows) {
@@ -151,9 +287,63 @@ extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
     a.b0 = b0;
     for (int i = 0; i < nb; ++i)
       for (int j = 0; j < 3; ++j) a.hdest[i][j] = p->dest_host[3 * (b0 + i) + j];
-    kv_append_kernel<<<nb, 256, 0, st>>>(a);
-    int rc = check_launch("kv_append_kernel");
+    launch(a, nb);
+    int rc = check_launch(what);
     if (rc != HELM_OK) return rc;
   }
   return HELM_OK;
+}
+
+}  // namespace
+}  // namespace helm
+
+extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
+  using namespace helm;
+  int rc = check_append(p, true);
+  if (rc != HELM_OK || p->B == 0) return rc;
+  cudaStream_t st = as_stream(stream);
+  return launch_rows(p, append_args(p), [&](const AppendArgs &a, int blocks) {
+    kv_append_kernel<<<blocks, 256, 0, st>>>(a);
+  }, "kv_append_kernel");
+}
+
+extern "C" int helm_decode_prologue(const helm_decode_prologue_params *p, void *stream) {
+  using namespace helm;
+  if (!p) return fail(HELM_ERR_INVALID_ARGUMENT, "decode_prologue: params is null");
+  const helm_kv_append_params *ap = &p->append;
+  int rc = check_append(ap, p->do_append != 0);
+  if (rc != HELM_OK) return rc;
+  if (ap->B == 0) return HELM_OK;
+  if (p->Hq <= 0 || p->Hq % ap->Hkv != 0)
+    return fail(HELM_ERR_INVALID_ARGUMENT, "decode_prologue: Hq=%d not a positive multiple of Hkv=%d", p->Hq, ap->Hkv);
+  if (ap->D % 2 != 0 || ap->D > 2 * 32 * kMaxHalfPerLane)
+    return fail(HELM_ERR_UNSUPPORTED, "decode_prologue: head dim %d (even, <= 256)", ap->D);
+  if (!p->q_in || !p->q_out) return fail(HELM_ERR_INVALID_ARGUMENT, "decode_prologue: null q pointer");
+  if ((p->cos == nullptr) != (p->sin == nullptr))
+    return fail(HELM_ERR_INVALID_ARGUMENT, "decode_prologue: cos and sin go together");
+  if ((p->q_norm_w == nullptr) != (p->k_norm_w == nullptr))
+    return fail(HELM_ERR_INVALID_ARGUMENT, "decode_prologue: q_norm and k_norm weights go together");
+  for (int dt : {p->norm_dtype, p->cs_dtype})
+    if (dt != HELM_F32 && dt != HELM_F16 && dt != HELM_BF16)
+      return fail(HELM_ERR_UNSUPPORTED, "decode_prologue: dtype %d", dt);
+  PrologueArgs pr{};
+  pr.q_in = p->q_in;
+  pr.q_out = p->q_out;
+  pr.Hq = p->Hq;
+  pr.q_stride = p->q_stride;
+  pr.k_stride = p->k_stride;
+  pr.v_stride = p->v_stride;
+  pr.q_norm_w = p->q_norm_w;
+  pr.k_norm_w = p->k_norm_w;
+  pr.norm_dtype = p->norm_dtype;
+  pr.eps = p->eps;
+  pr.cos = p->cos;
+  pr.sin = p->sin;
+  pr.cs_dtype = p->cs_dtype;
+  pr.cs_stride = p->cs_stride;
+  pr.do_append = p->do_append;
+  cudaStream_t st = as_stream(stream);
+  return launch_rows(ap, append_args(ap), [&](const AppendArgs &a, int blocks) {
+    decode_prologue_kernel<<<blocks, 256, 0, st>>>(a, pr);
+  }, "decode_prologue_kernel");
 }

@@ -230,6 +230,53 @@ def kv_append(k_new: torch.Tensor, v_new: torch.Tensor, k_base: torch.Tensor, v_
     N.check("helm_kv_append", N.lib().helm_kv_append(ctypes.byref(p), _stream(dev)))
 
 
+def decode_prologue(q_in: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, q_out: torch.Tensor, k_base,
+                    v_base, *, q_norm_w=None, k_norm_w=None, eps: float = 1e-6, cos=None, sin=None,
+                    do_append: bool = True, **append_kw) -> None:
+    """helm_decode_prologue: q_in [B, Hq, D], k_new / v_new [B, Hkv, D] raw projections (rows may be
+    strided, heads contiguous); q_out [B, Hq, D] contiguous; cos / sin [B, D] (rows may be strided);
+    append_kw: the destination arguments of make_append_params."""
+    dev = _need_cuda("decode_prologue", q_in, k_new, v_new, q_out)
+    B, Hq, D = q_in.shape
+    for name, t in (("q_in", q_in), ("k_new", k_new), ("v_new", v_new)):
+        if t.dim() != 3 or t.stride(2) != 1 or t.stride(1) != D:
+            raise ValueError(f"decode_prologue: {name} must be [B, H, D] with contiguous heads")
+    if not q_out.is_contiguous() or tuple(q_out.shape) != (B, Hq, D) or q_out.dtype != q_in.dtype:
+        raise ValueError("decode_prologue: q_out must be a contiguous [B, Hq, D] tensor of q's dtype")
+    if k_new.dtype != q_in.dtype or v_new.dtype != q_in.dtype:
+        raise ValueError("decode_prologue: q, k and v must share a dtype")
+    p = N.DecodePrologueParams()
+    p.append = make_append_params(k_new, v_new, k_base, v_base, **append_kw)
+    p.q_in, p.q_out, p.Hq = q_in.data_ptr(), q_out.data_ptr(), Hq
+    p.q_stride, p.k_stride, p.v_stride = q_in.stride(0), k_new.stride(0), v_new.stride(0)
+    p.q_norm_w, p.k_norm_w = _ptr(q_norm_w), _ptr(k_norm_w)
+    p.norm_dtype = dtype_code(q_norm_w.dtype) if q_norm_w is not None else N.F32
+    p.eps = float(eps)
+    if cos is not None:
+        if cos.stride(-1) != 1 or sin.stride(-1) != 1 or cos.shape[-1] != D or cos.stride(0) != sin.stride(0):
+            raise ValueError("decode_prologue: cos / sin must be [B, D] rows with unit inner stride")
+        p.cos, p.sin, p.cs_dtype, p.cs_stride = cos.data_ptr(), sin.data_ptr(), dtype_code(cos.dtype), cos.stride(0)
+    else:
+        p.cs_dtype = N.F32
+    p.do_append = 1 if do_append else 0
+    N.check("helm_decode_prologue", N.lib().helm_decode_prologue(ctypes.byref(p), _stream(dev)))
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """helm_rmsnorm over the last dimension of x (rows may be strided; the last dim contiguous)."""
+    dev = _need_cuda("rmsnorm", x, weight)
+    dim = x.shape[-1]
+    x2 = x.reshape(-1, dim) if x.dim() != 2 else x
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    y = out if out is not None else torch.empty(x.shape, dtype=x.dtype, device=dev)
+    y2 = y.view(-1, dim)
+    N.check("helm_rmsnorm", N.lib().helm_rmsnorm(x2.data_ptr(), dtype_code(x.dtype), x2.stride(0), weight.data_ptr(),
+                                                 dtype_code(weight.dtype), y2.data_ptr(), y2.stride(0), x2.shape[0],
+                                                 dim, float(eps), _stream(dev)))
+    return y
+
+
 def copy_pages(dst: torch.Tensor, dst_first: int, src: torch.Tensor, src_ids, page_bytes: int,
                stream: Optional[int] = None) -> int:
     """Copies pages src[src_ids[i]] -> dst[dst_first + i] (runs merged); returns the copy count."""

@@ -38,7 +38,7 @@ from .. import ops
 class DecodeGraph:
     SPARES = 2   # spare pages per (layer, sequence); one is consumed at most per step
 
-    def __init__(self, mgr, model, headroom_tokens: int = 4096):
+    def __init__(self, mgr, model, headroom_tokens: int = 1024):
         batch = mgr.batch
         if batch is None or batch.cont is not None or mgr.kvcms[0].use_contiguous:
             raise RuntimeError("DecodeGraph needs KVOffloadManager in paged mode (cont_capacity=0) on a CUDA device")
@@ -58,11 +58,8 @@ class DecodeGraph:
         self.alloc = mgr.allocator
         self.store = self.alloc.store(self.dev)
         P = self.alloc.page_size
-        # table width for the pages reachable before the next recapture
-        need = max(len(m.layers[l].pages) for m in kvcms for l in range(self.L))
         self.headroom = max(P, headroom_tokens)
-        batch._grow(need + self.headroom // P + self.SPARES + 1)
-        self.width = batch.width
+        self._make_room()
         for l in range(self.L):
             for b in range(self.B):
                 if not batch.in_sync(l, b):
@@ -79,6 +76,19 @@ class DecodeGraph:
         self.ids = torch.zeros((self.B, 1), dtype=torch.long, device=self.dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.logits = None
+
+    def _make_room(self) -> None:
+        """Grows the page tables and the device slab for the tokens decodable before the next
+        capture.  A captured graph holds the tables' and the slab's addresses, so neither may be
+        reallocated while it lives: step() recaptures when either has moved or is about to run out."""
+        P = self.alloc.page_size
+        need = max(len(m.layers[l].pages) for m in self.batch.kvcms for l in range(self.L))
+        self.batch._grow(need + self.headroom // P + self.SPARES + 1)
+        self.width = self.batch.width
+        st = self.store
+        st.reserve(st.next_slot + self.L * self.B * (self.headroom // P + self.SPARES + 1))
+        self._slab_ptr = st.slab.data_ptr()
+        self._slot_limit = st.capacity
 
     # ---- spare pages ----------------------------------------------------------------------
     def _refill(self, seqs) -> None:
@@ -141,8 +151,11 @@ class DecodeGraph:
         The returned tensor is reused by the next step."""
         if tuple(input_ids.shape) != (self.B, 1):
             raise ValueError(f"DecodeGraph.step: input_ids must be [{self.B}, 1]")
-        if self.graph is not None and max(len(m.layers[0].pages) for m in self.batch.kvcms) + 2 > self.width:
-            self._recapture()   # the page tables must grow: a captured graph holds their addresses
+        if self.graph is not None and (
+                max(len(m.layers[0].pages) for m in self.batch.kvcms) + 2 > self.width
+                or self.store.slab.data_ptr() != self._slab_ptr
+                or self.store.next_slot + self.L * self.B * self.SPARES > self._slot_limit):
+            self._recapture()   # tables or slab grew (or are about to): the graph holds their addresses
         self.ids.copy_(input_ids, non_blocking=True)
         if self.graph is None:
             # first step: run it eagerly in device-directed mode (warms up every library the graph
@@ -164,10 +177,7 @@ class DecodeGraph:
         torch.cuda.synchronize(self.dev)
         self.graph = None
         self.logits = None
-        P = self.alloc.page_size
-        need = max(len(m.layers[l].pages) for m in self.batch.kvcms for l in range(self.L))
-        self.batch._grow(need + self.headroom // P + self.SPARES + 1)
-        self.width = self.batch.width
+        self._make_room()
 
     def close(self) -> None:
         """Returns the unused spare pages to the allocator; decode continues eagerly."""
@@ -181,19 +191,24 @@ class DecodeGraph:
                 self.spare_pages[l][b] = []
 
 
-def device_append(batch, l: int, k, v, store) -> None:
+def device_append(batch, l: int, k, v, store, prologue=None, q_out=None) -> None:
     """The graph-mode append of layer l: one token per sequence, destination chosen on the device
-    (tail page, or the next spare page when the tail is full), page table updated by the kernel."""
+    (tail page, or the next spare page when the tail is full), page table updated by the kernel.
+    With a prologue, the same launch also normalises / rotates q (into q_out) and k."""
     g = batch.graph
     B = batch.B
+    k_base, v_base = store.base_ptrs()
+    dest_kw = dict(page_stride=store.page_elems, head_stride=store.head_stride, num_pool_pages=store.capacity,
+                   page_size=store.P, page_table=batch.table[l], page_used=batch.used[l],
+                   num_pages=batch.npages[l], spare_pages=g.spare_ids[l], spare_next=g.spare_next[l],
+                   error_flag=batch.error_flag)
+    if prologue is not None:
+        prologue.run(q_out, k_base, v_base, True, **dest_kw)
+        return
     k3 = k.reshape(B, k.shape[1], k.shape[-1])
     v3 = v.reshape(B, v.shape[1], v.shape[-1])
     if not k3.is_contiguous():
         k3 = k3.contiguous()
     if not v3.is_contiguous():
         v3 = v3.contiguous()
-    k_base, v_base = store.base_ptrs()
-    ops.kv_append(k3, v3, k_base, v_base, page_stride=store.page_elems, head_stride=store.head_stride,
-                  num_pool_pages=store.capacity, page_size=store.P, page_table=batch.table[l],
-                  page_used=batch.used[l], num_pages=batch.npages[l], spare_pages=g.spare_ids[l],
-                  spare_next=g.spare_next[l], error_flag=batch.error_flag)
+    ops.kv_append(k3, v3, k_base, v_base, **dest_kw)

@@ -65,6 +65,53 @@ class KVOffloadConfig:
 # Batched decode (kv_offload.py:82-167)
 # ---------------------------------------------------------------------------------------------
 
+class _Prologue:
+    """The decode step's raw q/k/v projections ([B, 1, H, D]) and what turns them into the
+    attention inputs: the per-head RMSNorm modules (Qwen3's q_norm / k_norm, or None) and the
+    rotary tables (cos, sin [B, 1, D]).  On the paged batch path one helm_decode_prologue launch
+    applies them and appends K/V; elsewhere materialize() applies the model's own functions."""
+
+    def __init__(self, q, k, v, cos, sin, rope_fn, q_norm=None, k_norm=None):
+        self.q, self.k, self.v = q, k, v
+        self.cos, self.sin, self.rope_fn = cos, sin, rope_fn
+        self.q_norm, self.k_norm = q_norm, k_norm
+
+    def materialize(self):
+        """(q [B, Hq, 1, D], k, v [B, Hkv, 1, D]) as the unfused forward computes them."""
+        q = (self.q_norm(self.q) if self.q_norm is not None else self.q).transpose(1, 2)
+        k = (self.k_norm(self.k) if self.k_norm is not None else self.k).transpose(1, 2)
+        v = self.v.transpose(1, 2)
+        q, k = self.rope_fn(q, k, self.cos, self.sin)
+        return q, k, v
+
+    def fusable(self) -> bool:
+        q, k, v, cos = self.q, self.k, self.v, self.cos
+        ok = (q.dim() == 4 and q.shape[1] == 1 and q.dtype in (torch.float16, torch.bfloat16)
+              and k.dtype == q.dtype and v.dtype == q.dtype and cos.dim() == 3 and cos.shape[1] == 1
+              and cos.shape[0] in (1, q.shape[0]) and tuple(self.sin.shape) == tuple(cos.shape))
+        if self.q_norm is not None:
+            ok = ok and hasattr(self.q_norm, "variance_epsilon") and hasattr(self.k_norm, "variance_epsilon")
+        return ok
+
+    def run(self, q_out, k_base, v_base, do_append: bool, **append_kw) -> None:
+        B, _, Hq, D = self.q.shape
+        Hkv = self.k.shape[2]
+        cos = self.cos.reshape(self.cos.shape[0], D)
+        sin = self.sin.reshape(self.sin.shape[0], D)
+        if cos.stride(-1) != 1 or sin.stride(-1) != 1:
+            cos, sin = cos.contiguous(), sin.contiguous()
+        if cos.shape[0] != B:      # one position shared by the batch: broadcast rows (stride 0)
+            cos, sin = cos.expand(B, D), sin.expand(B, D)
+        elif cos.stride(0) != sin.stride(0):
+            cos, sin = cos.contiguous(), sin.contiguous()
+        qn = self.q_norm
+        ops.decode_prologue(self.q.view(B, Hq, D), self.k.view(B, Hkv, D), self.v.view(B, Hkv, D), q_out,
+                            k_base, v_base, q_norm_w=None if qn is None else qn.weight,
+                            k_norm_w=None if qn is None else self.k_norm.weight,
+                            eps=1e-6 if qn is None else qn.variance_epsilon, cos=cos, sin=sin,
+                            do_append=do_append, **append_kw)
+
+
 def _batch_of(kvcms):
     b0 = getattr(kvcms[0], "_batch", None)
     if b0 is None:
@@ -78,7 +125,7 @@ def _batch_of(kvcms):
     return batch
 
 
-def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float, *, shard=None):
+def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float, *, shard=None, prologue=None):
     """Decode step shared by all architecture forward patches; returns [bsz, Hq, 1, D].
 
     Path selection follows the reference: (1) contiguous buffers while the sequence fits,
@@ -87,17 +134,28 @@ def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float, *, shard=None)
 
     shard (a KVShardGroup, multi-GPU only): the managers hold this rank's share of every
     sequence's pages; only the last rank appends the new token, and the per-rank records are
-    exchanged and merged so that every rank returns the full attention output."""
-    bsz = q.shape[0]
-    if q.device.type != "cuda":
+    exchanged and merged so that every rank returns the full attention output.
+
+    prologue (a _Prologue, instead of q/k/v): the raw projections plus their norms and rotary
+    tables; the paged batch path fuses them into the append launch (helm_decode_prologue)."""
+    x = q if q is not None else prologue.q
+    bsz = x.shape[0]
+    if x.device.type != "cuda":
         raise RuntimeError("helm_b200 decode attention runs on CUDA devices only")
     batch = _batch_of(kvcms)
+    fuse = prologue is not None and prologue.fusable()
+    if prologue is not None and not fuse:
+        q, k, v = prologue.materialize()
+        prologue = None
     if shard is not None and shard.world > 1:
         if batch is None or kvcms[0].use_contiguous:
             raise RuntimeError("sharded decode needs a registered batch in paged mode (cont_capacity=0)")
         all_gpu = all(kvcms[i].all_gpu_resident(layer_idx) for i in range(bsz))
-        return _decode_paged_batch(batch, layer_idx, q, k, v, scale, all_gpu, shard=shard)
+        return _decode_paged_batch(batch, layer_idx, q, k, v, scale, all_gpu, shard=shard, prologue=prologue)
 
+    if prologue is not None and (kvcms[0].use_contiguous or batch is None):
+        q, k, v = prologue.materialize()
+        prologue = None
     if kvcms[0].use_contiguous:
         if kvcms[0].cont_seq_len < kvcms[0].cont_capacity:
             return _decode_contiguous(kvcms, q, k, v, layer_idx, scale, batch)
@@ -108,7 +166,7 @@ def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float, *, shard=None)
 
     all_gpu = all(kvcms[i].all_gpu_resident(layer_idx) for i in range(bsz))
     if batch is not None:
-        return _decode_paged_batch(batch, layer_idx, q, k, v, scale, all_gpu)
+        return _decode_paged_batch(batch, layer_idx, q, k, v, scale, all_gpu, prologue=prologue)
 
     outs = []
     for i in range(bsz):
@@ -118,38 +176,43 @@ def _decode_batched(kvcms, q, k, v, layer_idx: int, scale: float, *, shard=None)
     return torch.cat(outs, dim=0)
 
 
-def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_gpu: bool, shard=None):
+def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_gpu: bool, shard=None,
+                        prologue=None):
     kvcms = batch.kvcms
     B = batch.B
-    dev = q.device
+    x = q if q is not None else prologue.q
+    dev = x.device
     alloc = kvcms[0].allocator
     store = alloc.store(dev)
-    if batch.graph is not None:
-        # CUDA-graph decode (runtime/graph.py): the append picks its page on the device and the
-        # host mirrors it after the step, so nothing here reads or changes host state
-        from .graph import device_append
-        device_append(batch, l, k, v, store)
+    if prologue is not None:
+        Hq, D = prologue.q.shape[2], prologue.q.shape[-1]
+        q3 = torch.empty((B, Hq, D), dtype=x.dtype, device=dev)
+    else:
         Hq, D = q.shape[1], q.shape[-1]
         q3 = q.reshape(B, Hq, D)
         if not q3.is_contiguous():
             q3 = q3.contiguous()
-        out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
+    if batch.graph is not None:
+        # CUDA-graph decode (runtime/graph.py): the append picks its page on the device and the
+        # host mirrors it after the step, so nothing here reads or changes host state
+        from .graph import device_append
+        device_append(batch, l, k, v, store, prologue=prologue, q_out=q3)
+        out = torch.empty((B, Hq, D), dtype=x.dtype, device=dev)
         _attend_batch(batch, l, q3, scale, store, False, out=out, out_record=None)
         return out.reshape(B, Hq, 1, D)
     append = shard is None or shard.rank == shard.world - 1
     if append:
-        _append_batch(batch, l, k, v, all_gpu, store, dev)
+        _append_batch(batch, l, k, v, all_gpu, store, dev, prologue=prologue, q_out=q3)
     else:
+        if prologue is not None:   # q only: this rank holds no tail page
+            prologue.run(q3, *store.base_ptrs(), do_append=False, page_stride=store.page_elems,
+                         head_stride=store.head_stride, num_pool_pages=store.capacity, page_size=store.P)
         for b, m in enumerate(kvcms):
             layer = m.layers.get(l)
             if layer is not None and not batch.in_sync(l, b) and not layer._n_off:
                 batch.sync_row(l, b)
     mixed = any(m.layers[l]._n_off for m in kvcms if l in m.layers)
-    Hq, D = q.shape[1], q.shape[-1]
-    q3 = q.reshape(B, Hq, D)
-    if not q3.is_contiguous():
-        q3 = q3.contiguous()
-    out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
+    out = torch.empty((B, Hq, D), dtype=x.dtype, device=dev)
     if shard is not None and shard.fused and not getattr(shard, "_fused_unsupported", False):
         try:
             _attend_batch(batch, l, q3, scale, store, mixed, out=out, out_record=None,
@@ -168,7 +231,7 @@ def _decode_paged_batch(batch: DecodeBatch, l: int, q, k, v, scale: float, all_g
     return out.reshape(B, Hq, 1, D)
 
 
-def _append_batch(batch: DecodeBatch, l: int, k, v, all_gpu: bool, store, dev):
+def _append_batch(batch: DecodeBatch, l: int, k, v, all_gpu: bool, store, dev, prologue=None, q_out=None):
     """Host bookkeeping of append_decode for every sequence + one kernel writing the tokens and
     their device page-table entries; rows changed structurally are re-uploaded."""
     kvcms = batch.kvcms
@@ -183,17 +246,20 @@ def _append_batch(batch: DecodeBatch, l: int, k, v, all_gpu: bool, store, dev):
         max_li = max(max_li, li)
         reserved.append(page)
     batch._grow(max_li + 1)
-    k3 = k.reshape(B, k.shape[1], k.shape[-1])
-    v3 = v.reshape(B, v.shape[1], v.shape[-1])
-    if not k3.is_contiguous():
-        k3 = k3.contiguous()
-    if not v3.is_contiguous():
-        v3 = v3.contiguous()
     k_base, v_base = store.base_ptrs()
-    ops.kv_append(k3, v3, k_base, v_base, page_stride=store.page_elems, head_stride=store.head_stride,
-                  num_pool_pages=store.capacity, page_size=store.P, dest_host=dest,
-                  page_table=batch.table[l], page_used=batch.used[l], num_pages=batch.npages[l],
-                  error_flag=batch.error_flag)
+    dest_kw = dict(page_stride=store.page_elems, head_stride=store.head_stride, num_pool_pages=store.capacity,
+                   page_size=store.P, dest_host=dest, page_table=batch.table[l], page_used=batch.used[l],
+                   num_pages=batch.npages[l], error_flag=batch.error_flag)
+    if prologue is not None:
+        prologue.run(q_out, k_base, v_base, True, **dest_kw)
+    else:
+        k3 = k.reshape(B, k.shape[1], k.shape[-1])
+        v3 = v.reshape(B, v.shape[1], v.shape[-1])
+        if not k3.is_contiguous():
+            k3 = k3.contiguous()
+        if not v3.is_contiguous():
+            v3 = v3.contiguous()
+        ops.kv_append(k3, v3, k_base, v_base, **dest_kw)
     in_sync = [batch.in_sync(l, b) for b in range(B)]
     for b, m in enumerate(kvcms):
         m._commit_decode_slot(l, reserved[b], all_gpu)
@@ -397,18 +463,21 @@ def _make_qwen2_forward(kvcms, shard=None):
         from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
         bsz, q_len, _ = hidden_states.shape
         hidden_shape = (bsz, q_len, -1, attn_self.head_dim)
-        q = attn_self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-        k = attn_self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-        v = attn_self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
         cos, sin = position_embeddings
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
         scale = 1.0 / math.sqrt(attn_self.head_dim)
-        groups = q.shape[1] // k.shape[1]
-        if q_len > 1:
+        if q_len == 1:
+            pro = _Prologue(attn_self.q_proj(hidden_states).view(hidden_shape),
+                            attn_self.k_proj(hidden_states).view(hidden_shape),
+                            attn_self.v_proj(hidden_states).view(hidden_shape), cos, sin, apply_rotary_pos_emb)
+            out = _decode_batched(kvcms, None, None, None, attn_self.layer_idx, scale, shard=shard, prologue=pro)
+        else:
+            q = attn_self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            k = attn_self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            v = attn_self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
+            groups = q.shape[1] // k.shape[1]
             out = _prefill(attn_self, kvcms, q, k, v, attention_mask, scale,
                            k.repeat_interleave(groups, dim=1), v.repeat_interleave(groups, dim=1), shard)
-        else:
-            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale, shard=shard)
         out = out.transpose(1, 2).contiguous().reshape(bsz, q_len, -1)
         return attn_self.o_proj(out), None
     return forward
@@ -420,18 +489,22 @@ def _make_qwen3_forward(kvcms, shard=None):
         from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb, repeat_kv
         bsz, q_len, _ = hidden_states.shape
         hidden_shape = (bsz, q_len, -1, attn_self.head_dim)
-        q = attn_self.q_norm(attn_self.q_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
-        k = attn_self.k_norm(attn_self.k_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
-        v = attn_self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
         cos, sin = position_embeddings
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
         scale = 1.0 / math.sqrt(attn_self.head_dim)
-        if q_len > 1:
+        if q_len == 1:
+            pro = _Prologue(attn_self.q_proj(hidden_states).view(hidden_shape),
+                            attn_self.k_proj(hidden_states).view(hidden_shape),
+                            attn_self.v_proj(hidden_states).view(hidden_shape), cos, sin, apply_rotary_pos_emb,
+                            q_norm=attn_self.q_norm, k_norm=attn_self.k_norm)
+            out = _decode_batched(kvcms, None, None, None, attn_self.layer_idx, scale, shard=shard, prologue=pro)
+        else:
+            q = attn_self.q_norm(attn_self.q_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
+            k = attn_self.k_norm(attn_self.k_proj(hidden_states).view(hidden_shape)).transpose(1, 2)
+            v = attn_self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
             out = _prefill(attn_self, kvcms, q, k, v, attention_mask, scale,
                            repeat_kv(k, attn_self.num_key_value_groups), repeat_kv(v, attn_self.num_key_value_groups),
                            shard)
-        else:
-            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale, shard=shard)
         out = out.transpose(1, 2).contiguous().reshape(bsz, q_len, -1)
         return attn_self.o_proj(out), None
     return forward
@@ -443,20 +516,35 @@ def _make_llama_forward(kvcms, shard=None):
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
         bsz, q_len, _ = hidden_states.shape
         hidden_shape = (bsz, q_len, -1, attn_self.head_dim)
-        q = attn_self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-        k = attn_self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
-        v = attn_self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
         cos, sin = position_embeddings
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
         scale = 1.0 / math.sqrt(attn_self.head_dim)
-        groups = q.shape[1] // k.shape[1]
-        if q_len > 1:
+        if q_len == 1:
+            pro = _Prologue(attn_self.q_proj(hidden_states).view(hidden_shape),
+                            attn_self.k_proj(hidden_states).view(hidden_shape),
+                            attn_self.v_proj(hidden_states).view(hidden_shape), cos, sin, apply_rotary_pos_emb)
+            out = _decode_batched(kvcms, None, None, None, attn_self.layer_idx, scale, shard=shard, prologue=pro)
+        else:
+            q = attn_self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            k = attn_self.k_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            v = attn_self.v_proj(hidden_states).view(hidden_shape).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
+            groups = q.shape[1] // k.shape[1]
             out = _prefill(attn_self, kvcms, q, k, v, attention_mask, scale,
                            k.repeat_interleave(groups, dim=1), v.repeat_interleave(groups, dim=1), shard)
-        else:
-            out = _decode_batched(kvcms, q, k, v, attn_self.layer_idx, scale, shard=shard)
         out = out.transpose(1, 2).contiguous().reshape(bsz, q_len, -1)
         return attn_self.o_proj(out), None
+    return forward
+
+
+def _make_rmsnorm_forward(orig):
+    """RMSNorm forward as one helm_rmsnorm launch (16-bit CUDA inputs; anything else runs the
+    module's own forward).  Same arithmetic as the HF modules: fp32 statistics, the normalised
+    value cast to the input dtype, then scaled by the weight."""
+    def forward(norm_self, hidden_states):
+        if (hidden_states.device.type == "cuda" and hidden_states.dtype in (torch.float16, torch.bfloat16)
+                and norm_self.weight.dtype == hidden_states.dtype and hasattr(norm_self, "variance_epsilon")):
+            return ops.rmsnorm(hidden_states, norm_self.weight, norm_self.variance_epsilon)
+        return orig(norm_self, hidden_states)
     return forward
 
 
@@ -469,10 +557,16 @@ class KVOffloadManager:
     One KVCacheManager per batch item, all sharing one KVAllocator; the batch's page tables
     live on the device (DecodeBatch)."""
 
-    def __init__(self, model, config: KVOffloadConfig, batch_size: int = 1, shard_group=None):
+    def __init__(self, model, config: KVOffloadConfig, batch_size: int = 1, shard_group=None,
+                 fused_norms: bool = False):
         """shard_group (a KVShardGroup; extension, multi-GPU only): store this rank's share of every
         sequence's KV pages and merge the ranks' attention records on each decode step.  Requires
-        config.cont_capacity == 0 (paged mode)."""
+        config.cont_capacity == 0 (paged mode).
+
+        fused_norms (extension): also patch the architecture's RMSNorm module (Qwen3RMSNorm /
+        Qwen2RMSNorm / LlamaRMSNorm) to run as one helm_rmsnorm launch for 16-bit CUDA inputs
+        instead of five elementwise kernels; restore() undoes it too."""
+        self.fused_norms = fused_norms
         self.config = config
         self.batch_size = batch_size
         self.shard_group = shard_group
@@ -548,3 +642,8 @@ class KVOffloadManager:
             raise ValueError(arch)
         self._patched[arch] = (cls, cls.forward)
         cls.forward = new_fwd
+        if self.fused_norms:
+            norm_cls = {"qwen2": "Qwen2RMSNorm", "qwen3": "Qwen3RMSNorm", "llama": "LlamaRMSNorm"}[arch]
+            ncls = getattr(m, norm_cls)
+            self._patched[arch + "_norm"] = (ncls, ncls.forward)
+            ncls.forward = _make_rmsnorm_forward(ncls.forward)

@@ -258,6 +258,45 @@ typedef struct {
 
 int helm_kv_append(const helm_kv_append_params *p, void *stream);
 
+/* ---- Decode prologue (fused) ---------------------------------------------- */
+/*
+ * The attention forward's decode prologue in one launch (kv_offload.py:244-249
+ * + append_decode, kv_cache.py:87-113): per-head RMSNorm of q and k with the
+ * q_norm / k_norm weights (Qwen3; null weights = none), the rotary embedding
+ * x*cos + rotate_half(x)*sin of q and k (null cos/sin = none), q written to
+ * q_out [B, Hq, D] (contiguous, append.src_dtype), and -- with do_append -- k
+ * and v written into the pool exactly as helm_kv_append places them (host- or
+ * device-directed).  q_in / append.k_new / append.v_new are the raw
+ * projections [B, H, D] with row strides q_stride / k_stride / v_stride
+ * elements; cos / sin [B, D] with row stride cs_stride.  fp32 arithmetic.
+ */
+typedef struct {
+  helm_kv_append_params append;
+  const void *q_in;
+  void *q_out;
+  int32_t Hq;
+  int64_t q_stride, k_stride, v_stride;
+  const void *q_norm_w, *k_norm_w;
+  int32_t norm_dtype;
+  float eps;
+  const void *cos, *sin;
+  int32_t cs_dtype;
+  int64_t cs_stride;
+  int32_t do_append;
+} helm_decode_prologue_params;
+
+int helm_decode_prologue(const helm_decode_prologue_params *p, void *stream);
+
+/* ---- RMSNorm (fused) ------------------------------------------------------ */
+/*
+ * y[r] = w * cast(x[r] * rsqrt(mean(x[r]^2) + eps)) for rows r < rows of dim
+ * elements (row strides in elements), x / y of x_dtype (F32/F16/BF16), w of
+ * w_dtype: the decoders' RMSNorm modules (Qwen3RMSNorm etc., used around the
+ * patched attention) in one launch.  No counterpart in the reference's kernels.
+ */
+int helm_rmsnorm(const void *x, int32_t x_dtype, int64_t x_stride, const void *w, int32_t w_dtype,
+                 void *y, int64_t y_stride, int64_t rows, int32_t dim, float eps, void *stream);
+
 /* ---- KV sequence sharding: cross-GPU record exchange + merge ------------- */
 /*
  * No reference counterpart (HELM has no multi-GPU path): with each sequence's

@@ -33,8 +33,8 @@ def _eager_step(model, tok, pos):
 
 
 @torch.no_grad()
-@pytest.mark.parametrize("B", [1, 2])
-def test_graph_decode_matches_eager(B):
+@pytest.mark.parametrize("B,fused_norms", [(1, False), (2, False), (2, True)])
+def test_graph_decode_matches_eager(B, fused_norms):
     from helm_b200.runtime import KVOffloadConfig, KVOffloadManager
     from helm_b200.runtime.graph import DecodeGraph
     model = _tiny()
@@ -54,16 +54,21 @@ def test_graph_decode_matches_eager(B):
     mgr.restore()
 
     # graph run from the same prefill
-    mgr = KVOffloadManager(model, cfg, batch_size=B)
+    mgr = KVOffloadManager(model, cfg, batch_size=B, fused_norms=fused_norms)
     try:
         tok = _prefill(model, ids)[:, -1:].argmax(-1)
         g = DecodeGraph(mgr, model)
+        agree = 0
         for t in range(steps):
-            lg = g.step(tok)
+            lg = g.step(tok if t == 0 else ref_tokens[t - 1])     # teacher-forced on the eager tokens
             err = float((lg.float() - ref_logits[t]).abs().max())
             assert err <= 0.05 * max(1.0, float(ref_logits[t].abs().max())), f"step {t}: {err}"
-            tok = lg[:, -1:].argmax(-1)
-            assert torch.equal(tok, ref_tokens[t]), f"step {t}: tokens differ"
+            same = torch.equal(lg[:, -1:].argmax(-1), ref_tokens[t])
+            agree += same
+            if not fused_norms:   # same kernels as the eager run: the same greedy tokens
+                assert same, f"step {t}: tokens differ"
+        assert agree >= 0.9 * steps
+        tok = ref_tokens[-1]
         torch.cuda.synchronize()
         assert int(mgr.batch.error_flag.item()) == 0
         # host bookkeeping = device tables
@@ -94,5 +99,43 @@ def test_graph_decode_rejects_unsupported():
     try:
         with pytest.raises(RuntimeError):
             DecodeGraph(mgr, model)
+    finally:
+        mgr.restore()
+
+
+@torch.no_grad()
+def test_graph_decode_survives_slab_growth():
+    """The device slab is reallocated between two steps (as a growth for other pages would): the
+    next step recaptures against the new slab, and the decode stays equal to the eager one."""
+    from helm_b200.runtime import KVOffloadConfig, KVOffloadManager
+    from helm_b200.runtime.graph import DecodeGraph
+    model = _tiny()
+    B, S, steps = 2, 60, 30
+    ids = torch.randint(0, 320, (B, S), device=DEV, generator=torch.Generator(device=DEV).manual_seed(3))
+    cfg = KVOffloadConfig.from_model(model, page_size=64, cont_capacity=0, gpu_watermark_bytes=1 << 40)
+    mgr = KVOffloadManager(model, cfg, batch_size=B)
+    tok = _prefill(model, ids)[:, -1:].argmax(-1)
+    ref = []
+    for t in range(steps):
+        lg = _eager_step(model, tok, S + t)
+        ref.append(lg.float())
+        tok = lg[:, -1:].argmax(-1)
+    mgr.restore()
+    mgr = KVOffloadManager(model, cfg, batch_size=B)
+    try:
+        tok = _prefill(model, ids)[:, -1:].argmax(-1)
+        g = DecodeGraph(mgr, model)
+        store = mgr.allocator.store(DEV)
+        for t in range(steps):
+            if t == 10:
+                old = store.slab.data_ptr()
+                store.reserve(store.capacity + 4096)
+                assert store.slab.data_ptr() != old
+            lg = g.step(tok)
+            assert torch.isfinite(lg.float()).all(), f"step {t}"
+            assert float((lg.float() - ref[t]).abs().max()) <= 0.05 * max(1.0, float(ref[t].abs().max()))
+            tok = lg[:, -1:].argmax(-1)
+        assert int(mgr.batch.error_flag.item()) == 0
+        g.close()
     finally:
         mgr.restore()

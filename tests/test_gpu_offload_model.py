@@ -66,7 +66,7 @@ def _check(ours, ref, what):
     assert agree >= 0.9, f"{what}: argmax agreement {agree:.2f}"
 
 
-@pytest.mark.parametrize("mode", ["paged", "contiguous", "offload"])
+@pytest.mark.parametrize("mode", ["paged", "contiguous", "offload", "paged_fused_norms"])
 def test_qwen3_decode_paths_match_unpatched(mode):
     from helm_b200.runtime import KVOffloadConfig, KVOffloadManager
     model = _tiny("qwen3")
@@ -76,7 +76,7 @@ def test_qwen3_decode_paths_match_unpatched(mode):
     ref = _reference_logits(model, ids)[:, S - 1:]
     cfg = KVOffloadConfig.from_model(model, page_size=64, cont_capacity=4096 if mode == "contiguous" else 0,
                                      gpu_watermark_bytes=(2 * 2 * 64 * 128 * 2 * 2) if mode == "offload" else 10 ** 12)
-    mgr = KVOffloadManager(model, cfg, batch_size=B)
+    mgr = KVOffloadManager(model, cfg, batch_size=B, fused_norms=mode == "paged_fused_norms")
     try:
         ours = _pipeline_logits(model, ids, S)
         _check(ours, ref, mode)
