@@ -35,7 +35,9 @@
 // HBM stream then balances the CTAs by itself).  Every mbarrier wait is
 // bounded (2 s); a wait that gives up sets HELM_DEVERR_TIMEOUT in the
 // library's INT8 error word (helm_int8_linear_error) and the CTA finishes
-// without writing its rows.
+// without writing its rows.  Launched with programmatic dependent launch: the
+// producer starts on the weights while the previous kernel on the stream drains;
+// the consumers wait for that kernel (griddepcontrol.wait) before reading x.
 #include "common.cuh"
 #include "tma.cuh"
 
@@ -50,20 +52,24 @@ constexpr int kCWarps = 4;                       // consumer warps
 constexpr int kThreadsT = (kCWarps + 1) * 32;    // + one producer warp
 constexpr int kBoxK = 128;                       // k per TMA box row (128-byte swizzle)
 constexpr int kStageK = kCWarps * kBoxK;         // k per stage: one box per consumer warp
-constexpr int kStageBudget = 96 * 1024;          // shared memory for the ring
+constexpr int kMaxStages = 16;
 
-// Ring depth for RT row tiles: stages of 512 x 16*RT bytes within the budget, at most 8.
-template <int RT> constexpr int ring_stages() {
-  return (kStageBudget / (kStageK * 16 * RT)) < 8 ? (kStageBudget / (kStageK * 16 * RT)) : 8;
+// Ring depth: the shared memory left per CTA when ceil(CTAs / SMs) CTAs share an SM (at most 3;
+// the whole grid is resident at once), within 2..kMaxStages stages.  Few CTAs get deep rings,
+// which is what keeps a short-N, long-K weight (few rows per SM) streaming at the HBM rate.
+inline int ring_stages(int ctas, int sms, int stage_bytes, int other_bytes) {
+  int per = (ctas + sms - 1) / sms;
+  if (per < 1) per = 1;
+  if (per > 3) per = 3;
+  int budget = (226 * 1024) / per - other_bytes - 2048;
+  if (budget > 200 * 1024) budget = 200 * 1024;
+  int st = budget / stage_bytes;
+  if (st > kMaxStages) st = kMaxStages;
+  return st < 2 ? 2 : st;
 }
 
 __device__ int g_int8_error;  // HELM_DEVERR_* bits of the INT8 kernels (helm_int8_linear_error)
 
-__device__ __forceinline__ uint4 ld_x(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
 
 // Bytes (lo, hi) of `biased` (the int8 word xor 0x80808080) as an exact 16-bit pair of the
 // activation type; SEL picks the two bytes (0x4140: bytes 0,1; 0x4342: bytes 2,3).
@@ -125,29 +131,37 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   return v;
 }
 
-// Grid (ceil(N / (16*RT)), ceil(M / (8*MT))), 160 threads.  Dynamic shared memory: the ring
-// (ST stages of 512 x 16*RT bytes, 1024-byte aligned) + kCWarps * RT * MT * 128 floats.
+// Grid (ceil(N / (16*RT)), ceil(M / (8*MT))), 160 threads.  Dynamic shared memory: the ring of
+// ST stages (each, 1024-byte aligned: 4 weight boxes of 128 k x 16*RT rows, then 4 x boxes of
+// 128 k x XR rows at 128-byte alignment) + kCWarps * RT * MT * 128 floats for the final sum.
 template <typename XT, int RT, int MT>
 __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_constant__ CUtensorMap tmW,
-                                                            const XT *__restrict__ x,
+                                                            const __grid_constant__ CUtensorMap tmX,
                                                             const void *__restrict__ scale, int scale_dt,
                                                             const XT *__restrict__ bias, XT *__restrict__ y, int M,
-                                                            int N, int K) {
-  constexpr int ST = ring_stages<RT>();
-  constexpr int kBoxBytes = kBoxK * 16 * RT;
-  constexpr int kStageBytes = kCWarps * kBoxBytes;
+                                                            int N, int K, int ST, int XR, int xbox_bytes) {
+  constexpr int kWBoxBytes = kBoxK * 16 * RT;
   constexpr int P = RT * MT * 128;  // floats of one warp's partial tile
+  const int stage_bytes = (kCWarps * (kWBoxBytes + xbox_bytes) + 1023) & ~1023;
+  const uint32_t xtx = (uint32_t)(kBoxK * XR * sizeof(XT));  // bytes one x box brings
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[ST];
-  __shared__ __align__(8) uint64_t empty_bar[ST];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
   __shared__ int any_fail;
   uint8_t *ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float *red = reinterpret_cast<float *>(ring + ST * kStageBytes);
+  float *red = reinterpret_cast<float *>(ring + (size_t)ST * stage_bytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_base = blockIdx.x * 16 * RT;
   const int m_base = blockIdx.y * 8 * MT;
   const int nst = (K + kStageK - 1) / kStageK;
+  auto wbox = [&](int slot, int bx) { return ring + (size_t)slot * stage_bytes + bx * kWBoxBytes; };
+  auto xbox = [&](int slot, int bx) {
+    return ring + (size_t)slot * stage_bytes + kCWarps * kWBoxBytes + bx * xbox_bytes;
+  };
 
+  // Programmatic dependent launch: the next kernel on the stream may start its own prologue now;
+  // it still waits (griddepcontrol.wait) for this grid to finish before reading what we write.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) {
       mbar_init(&full_bar[i], 1);
@@ -162,18 +176,33 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
     // ---------------- producer ----------------
     if (lane == 0) {
       bool ok = true;
-      for (int s = 0; s < nst; ++s) {
+      auto boxes_of = [&](int s) { return min(kCWarps, (K - s * kStageK + kBoxK - 1) / kBoxK); };
+      // The weights of the first stages go out before the previous kernel has finished (they
+      // are never written by a preceding kernel of a decode step); x only after it has.
+      const int pre = min(ST, nst);
+      for (int s = 0; s < pre; ++s) {
+        const int boxes = boxes_of(s);
+        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(boxes * (kWBoxBytes + xtx)));
+        for (int bx = 0; bx < boxes; ++bx)
+          tma_load_2d(wbox(s, bx), &tmW, &full_bar[s], s * kStageK + bx * kBoxK, n_base);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int s = 0; s < pre; ++s)
+        for (int bx = 0; bx < boxes_of(s); ++bx)
+          tma_load_2d(xbox(s, bx), &tmX, &full_bar[s], s * kStageK + bx * kBoxK, m_base);
+      for (int s = pre; s < nst; ++s) {
         const int slot = s % ST;
-        if (s >= ST && !mbar_wait(&empty_bar[slot], (uint32_t)((s / ST - 1) & 1))) {
+        if (!mbar_wait(&empty_bar[slot], (uint32_t)((s / ST - 1) & 1))) {
           atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
           ok = false;
           break;
         }
-        const int k0 = s * kStageK;
-        const int boxes = min(kCWarps, (K - k0 + kBoxK - 1) / kBoxK);
-        mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(boxes * kBoxBytes));
-        for (int bx = 0; bx < boxes; ++bx)
-          tma_load_2d(ring + slot * kStageBytes + bx * kBoxBytes, &tmW, &full_bar[slot], k0 + bx * kBoxK, n_base);
+        const int boxes = boxes_of(s);
+        mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(boxes * (kWBoxBytes + xtx)));
+        for (int bx = 0; bx < boxes; ++bx) {
+          tma_load_2d(wbox(slot, bx), &tmW, &full_bar[slot], s * kStageK + bx * kBoxK, n_base);
+          tma_load_2d(xbox(slot, bx), &tmX, &full_bar[slot], s * kStageK + bx * kBoxK, m_base);
+        }
       }
       // drain: the copies of the last stages land before this CTA can finish
       for (int s = max(0, nst - ST); s < nst && ok; ++s)
@@ -192,29 +221,17 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[rt][nt][e] = 0.f;
 
-  // x: this thread's 32 values of row m (k = box + 32j .. +31) as 4 x 16 bytes, zero past M / K
-  auto load_x = [&](int nt, int kbox, uint4 (&xv)[4]) {
-    const int m = m_base + nt * 8 + g;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int k = kbox + 32 * j + 8 * c;
-      xv[c] = (m < M && k < K) ? ld_x(x + (int64_t)m * K + k) : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-  constexpr int XPF = MT < 2 ? MT : 2;  // n-tiles whose x is fetched before the stage wait
   for (int s = 0; s < nst; ++s) {
     const int slot = s % ST;
     const int kbox = s * kStageK + warp * kBoxK;
-    uint4 xpf[XPF][4];
-#pragma unroll
-    for (int nt = 0; nt < XPF; ++nt) load_x(nt, kbox, xpf[nt]);
     if (!mbar_wait(&full_bar[slot], (uint32_t)((s / ST) & 1))) {
       atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
       any_fail = 1;
       break;
     }
     if (kbox < K) {
-      const uint32_t box = smem_u32(ring + slot * kStageBytes + warp * kBoxBytes);
+      const uint32_t box = smem_u32(wbox(slot, warp));
+      const uint32_t xb = smem_u32(xbox(slot, warp));
       // weights: rows g and g+8 of each row tile, 32 bytes each = 16-byte chunks 2j and 2j+1 of
       // the 128-byte row, stored at chunk ^ (row & 7) by the 128-byte swizzle
       uint4 wv[RT][2][2];
@@ -229,13 +246,12 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
         }
 #pragma unroll
       for (int nt = 0; nt < MT; ++nt) {
+        // x: row nt*8 + g of the box (rows past XR are zero), k = 32j .. 32j+31 of the box
+        const int r = nt * 8 + g;
         uint4 xl[4];
-        if (nt < XPF) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) xl[c] = xpf[nt < XPF ? nt : 0][c];
-        } else {
-          load_x(nt, kbox, xl);
-        }
+        for (int c = 0; c < 4; ++c)
+          xl[c] = r < XR ? lds128(xb + r * (kBoxK * (int)sizeof(XT)) + 64 * j + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {  // word u of the thread's 32 bytes: k = box + 32j + 4u + {0..3}
           const uint4 xa = xl[u >> 1];
@@ -264,6 +280,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
       for (int e = 0; e < 4; ++e) red[warp * P + ((rt * MT + nt) * 4 + e) * 32 + lane] = acc[rt][nt][e];
   asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
   if (any_fail) return;  // a stage never arrived: leave the rows unwritten (error word set)
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // y may still be read by the previous kernel
   for (int pos = threadIdx.x; pos < P; pos += kCWarps * 32) {
     float v = 0.f;
 #pragma unroll
@@ -322,57 +339,117 @@ bool weight_map(CUtensorMap *m, const int8_t *w, int N, int K, int rows) {
   return true;
 }
 
+// 2-D map over x [M, K] (16-bit): box 128 k x XR rows, no swizzle, zero fill past the edges.
+// Activations move between calls, so these maps are re-encoded when the pointer is new (small
+// cache keyed by everything the map encodes).
+bool act_map(CUtensorMap *m, const void *x, int xdt, int M, int K, int rows) {
+  struct Key {
+    const void *x;
+    int dt, M, K, rows;
+  };
+  constexpr size_t kSlots = 64;
+  static std::mutex mu;
+  static std::vector<std::pair<Key, CUtensorMap>> cache;
+  static size_t next = 0;
+  const Key key{x, xdt, M, K, rows};
+  auto same = [&](const Key &a) { return a.x == key.x && a.dt == key.dt && a.M == key.M && a.K == key.K && a.rows == key.rows; };
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto &e : cache)
+      if (same(e.first)) {
+        *m = e.second;
+        return true;
+      }
+  }
+  auto enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  cuuint64_t gstr[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBoxK, (cuuint32_t)rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, xdt == HELM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void *>(x), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() < kSlots) {
+    cache.emplace_back(key, *m);
+  } else {
+    cache[next] = {key, *m};
+    next = (next + 1) % kSlots;
+  }
+  return true;
+}
+
 template <typename XT, int RT, int MT>
-int launch_cfg(const void *x, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
-               int K, cudaStream_t st) {
-  constexpr int ST = ring_stages<RT>();
-  const size_t smem = 1024 + (size_t)ST * kStageK * 16 * RT + sizeof(float) * kCWarps * RT * MT * 128;
+int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y,
+               int M, int N, int K, cudaStream_t st) {
+  const int XR = M < 8 * MT ? M : 8 * MT;                          // x rows per box
+  const int xbox_bytes = ((kBoxK * XR * (int)sizeof(XT)) + 127) & ~127;   // 128-byte aligned x boxes
+  const int stage_bytes = (kCWarps * (kBoxK * 16 * RT + xbox_bytes) + 1023) & ~1023;
+  const int red_bytes = (int)sizeof(float) * kCWarps * RT * MT * 128;
+  const int ctas = ((N + 16 * RT - 1) / (16 * RT)) * ((M + 8 * MT - 1) / (8 * MT));
+  const int ST = ring_stages(ctas, num_sms(), stage_bytes, red_bytes);
+  const size_t smem = 1024 + (size_t)ST * stage_bytes + red_bytes;
   auto kern = int8_tma_kernel<XT, RT, MT>;
   {
     static std::mutex mu;
-    static std::vector<int> done;
+    static std::vector<std::pair<int, size_t>> done;  // (device, bytes allowed)
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(mu);
-    if ((int)done.size() <= dev) done.resize(dev + 1, 0);
-    if (!done[dev]) {
+    size_t have = 0;
+    for (const auto &d : done)
+      if (d.first == dev) have = d.second;
+    if (have < smem) {
       const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_linear: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      done[dev] = 1;
+      done.emplace_back(dev, smem);
     }
   }
-  CUtensorMap map;
-  if (!weight_map(&map, w, N, K, 16 * RT)) return fail(HELM_ERR_CUDA, "int8_linear: cuTensorMapEncodeTiled failed");
-  const dim3 grid((N + 16 * RT - 1) / (16 * RT), (M + 8 * MT - 1) / (8 * MT));
-  kern<<<grid, kThreadsT, smem, st>>>(map, static_cast<const XT *>(x), scale, sdt, static_cast<const XT *>(bias),
-                                       static_cast<XT *>(y), M, N, K);
+  CUtensorMap wmap, xmap;
+  if (!weight_map(&wmap, w, N, K, 16 * RT) || !act_map(&xmap, x, xdt, M, K, XR))
+    return fail(HELM_ERR_CUDA, "int8_linear: cuTensorMapEncodeTiled failed");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((N + 16 * RT - 1) / (16 * RT), (M + 8 * MT - 1) / (8 * MT));
+  cfg.blockDim = dim3(kThreadsT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, xmap, scale, sdt, static_cast<const XT *>(bias),
+                                           static_cast<XT *>(y), M, N, K, ST, XR, xbox_bytes);
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_linear: launch: %s", cudaGetErrorString(e));
   return check_launch("int8_tma_kernel");
 }
 
 // Rows per CTA: the fewest row tiles (16 rows each, at most 4) for which every CTA is resident
 // at once -- 3 CTAs per SM with one tile (64 KB ring), 2 with more (96 KB ring).
 template <typename XT, int MT>
-int launch_m(const void *x, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
+int launch_m(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
              int K, cudaStream_t st) {
   const int sms = num_sms();
   const int tiles = (N + 15) / 16;
   if constexpr (MT >= 4) {  // wide x tiles: one row tile per CTA (register budget)
-    return launch_cfg<XT, 1, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
+    return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
   } else {
-    if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
-    if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
-    if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
-    return launch_cfg<XT, 4, MT>(x, w, scale, sdt, bias, y, M, N, K, st);
+    if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+    if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+    if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+    return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
   }
 }
 
 template <typename XT>
-int launch(const void *x, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
+int launch(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
            int K, cudaStream_t st) {
-  if (M <= 8) return launch_m<XT, 1>(x, w, scale, sdt, bias, y, M, N, K, st);
-  if (M <= 16) return launch_m<XT, 2>(x, w, scale, sdt, bias, y, M, N, K, st);
-  if (M <= 32) return launch_m<XT, 4>(x, w, scale, sdt, bias, y, M, N, K, st);
-  return launch_m<XT, 8>(x, w, scale, sdt, bias, y, M, N, K, st);
+  if (M <= 8) return launch_m<XT, 1>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+  if (M <= 16) return launch_m<XT, 2>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+  if (M <= 32) return launch_m<XT, 4>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+  return launch_m<XT, 8>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
 }
 
 }  // namespace
@@ -393,8 +470,8 @@ extern "C" int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
     return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear: x and w must be 16-byte aligned");
   if ((int64_t)M > 65535ll * 8) return fail(HELM_ERR_UNSUPPORTED, "int8_linear: M=%d too large", M);
   cudaStream_t st = as_stream(stream);
-  return x_dtype == HELM_F16 ? launch<__half>(x, w, w_scale, scale_dtype, bias, y, M, N, K, st)
-                             : launch<__nv_bfloat16>(x, w, w_scale, scale_dtype, bias, y, M, N, K, st);
+  return x_dtype == HELM_F16 ? launch<__half>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, N, K, st)
+                             : launch<__nv_bfloat16>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, N, K, st);
 }
 
 extern "C" int helm_int8_linear_error(int32_t *flag_out, int32_t reset) {
