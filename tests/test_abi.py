@@ -78,3 +78,36 @@ def test_errors_are_reported_without_a_gpu():
     assert code == N.ERR_UNSUPPORTED
     with pytest.raises(N.HelmError):
         N.check("helm_int8_linear", code)
+
+
+STRUCTS = [("helm_shard_exchange", "ShardExchange"), ("helm_paged_attn_params", "PagedAttnParams"),
+           ("helm_kv_append_params", "KVAppendParams"), ("helm_decode_prologue_params", "DecodePrologueParams"),
+           ("helm_gather_merge_params", "GatherMergeParams")]
+
+
+def test_ctypes_layouts_match_the_compiled_header(tmp_path):
+    """sizeof and every field offset of each ABI struct, as a C compiler lays them out from
+    include/helm_b200.h, equal the ctypes mirrors the Python host side passes."""
+    import shutil
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void) {"]
+    for cname, pyname in STRUCTS:
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in getattr(N, pyname)._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c11", str(src), "-o", str(exe)], check=True, capture_output=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        s, f, v = line.split()
+        got[(s, f)] = int(v)
+    for cname, pyname in STRUCTS:
+        cls = getattr(N, pyname)
+        assert got[(cname, "size")] == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert got[(cname, fname)] == getattr(cls, fname).offset, f"{cname}.{fname}"
