@@ -47,10 +47,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
-    ap.add_argument("--workload", default="config5", choices=["config5", "config2", "config1", "config3"],
+    ap.add_argument("--workload", default="config5", choices=["config5", "config2", "config1", "config3", "config4"],
                     help="config5: the sharded decode-attention stack (default); config2: INT8 GEMV shapes; "
                          "config1: the reference's single-layer mixed-residency fp32 case; config3: a "
-                         "Qwen3-8B-shaped decode step through KVOffloadManager")
+                         "Qwen3-8B-shaped decode step through KVOffloadManager; config4: a Qwen3-14B-shaped "
+                         "INT8 decode step with half the KV on the host")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--exchange", default="fused", choices=["fused", "p2p", "nccl"],
@@ -1037,6 +1038,149 @@ def run_reference_config3(args, rank):
                       "attention is timed by --workload config1 and config5)"}), flush=True)
 
 
+# ----------------------------------------------------------------------------
+# config 4: Qwen3-14B-shaped, INT8 linears, batch 8, 32768 tokens per sequence, half the KV on the host
+# ----------------------------------------------------------------------------
+C4 = dict(layers=40, hidden=5120, heads=40, kv_heads=8, head_dim=128, inter=17408, vocab=151936, ctx=32768, batch=8)
+C4_METRIC = ("decode tok/s, Qwen3-14B-shaped INT8 model through KVOffloadManager (config4, batch 8, 32768-token "
+             "paged KV per sequence, oldest 50% of the pages in pinned host memory)")
+
+
+def run_config4(args, rank, local, world):
+    """Decode steps of a random-init Qwen3-14B-shaped model with INT8 weight-only linears
+    (patch_int8_linears) through KVOffloadManager: every sequence holds 32768 cached tokens, filled
+    with seeded K/V through KVCacheManager.append_prefill under a GPU watermark of half the KV, so
+    the reference's eviction policy moves the oldest half of every sequence's pages to pinned host
+    memory; each decode step then stages those host pages back through the device (the reference's
+    mixed-residency path), layer by layer.  With N > 1 the pages are sharded by sequence position
+    over the ranks (KVShardGroup) and every rank holds 1/N of them."""
+    import transformers
+    from helm_b200.kernels import patch_int8_linears
+    from helm_b200.runtime import KVOffloadConfig, KVOffloadManager
+    from helm_b200.runtime.sharded import KVShardGroup, shard_bounds
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    init_pg(world, local)
+    stream = torch.cuda.current_stream(dev)
+    c = C4
+    B, L, ctx = c["batch"], c["layers"], c["ctx"]
+    cfg = transformers.Qwen3Config(vocab_size=c["vocab"], hidden_size=c["hidden"], intermediate_size=c["inter"],
+                                   num_hidden_layers=L, num_attention_heads=c["heads"],
+                                   num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], rope_theta=1e6,
+                                   max_position_embeddings=40960, rms_norm_eps=1e-6, tie_word_embeddings=False)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(0)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = transformers.Qwen3ForCausalLM(cfg).eval()
+    torch.set_default_dtype(prev)
+    n_int8 = patch_int8_linears(model)
+    torch.cuda.empty_cache()
+    P, Hkv, D = 64, c["kv_heads"], c["head_dim"]
+    page_bytes = 2 * Hkv * P * D * 2
+    plo, phi = shard_bounds(ctx // P, rank, world)
+    local_pages = phi - plo
+    kv_bytes = L * B * local_pages * page_bytes
+    group = KVShardGroup(B * c["heads"], D, dev) if world > 1 else None
+    mgr = KVOffloadManager(model, KVOffloadConfig.from_model(model, page_size=P, cont_capacity=0,
+                                                             gpu_watermark_bytes=kv_bytes // 2),
+                           batch_size=B, shard_group=group, fused_norms=True)
+    alloc = mgr.allocator
+    alloc.reserve_capacity(dev, L * B * (local_pages // 2 + 8) + B * local_pages + 1024)
+    alloc.reserve_capacity(torch.device("cpu"), L * B * (local_pages // 2 + 8))
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    t_fill = time.time()
+    with torch.no_grad():
+        for l in range(L):
+            for b in range(B):
+                K = torch.randn((1, Hkv, local_pages * P, D), generator=g, device=dev, dtype=torch.bfloat16)
+                V = torch.randn((1, Hkv, local_pages * P, D), generator=g, device=dev, dtype=torch.bfloat16)
+                mgr.kvcms[b].append_prefill(l, K, V)
+        del K, V
+        torch.cuda.synchronize(dev)
+        t_fill = time.time() - t_fill
+        rep0 = mgr.report()
+        host_pages = rep0["active_cpu_pages"]
+        clocks = ClockSampler(gpu_selector(dev, local))
+        clocks.start()
+        t_load0 = time.time()
+        gt = torch.Generator(device=dev).manual_seed(7)
+
+        def step(pos):
+            ids = torch.randint(0, c["vocab"], (B, 1), generator=gt, device=dev)
+            m = torch.zeros((B, 1, 1, pos + 1), device=dev, dtype=torch.bfloat16)
+            return model(input_ids=ids, attention_mask=m, position_ids=torch.full((B, 1), pos, device=dev),
+                         use_cache=False, logits_to_keep=1).logits
+        pos = ctx
+        for _ in range(max(1, min(args.warmup, 2))):
+            step(pos)
+            pos += 1
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        steps = max(2, min(args.steps, 5))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            lg = step(pos)
+            pos += 1
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+        # e2e: the next tokens read back to the host every step
+        e0.record(stream)
+        for _ in range(steps):
+            lg = step(pos)
+            pos += 1
+            tok_host = lg[:, -1].argmax(-1).cpu()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, dev) / steps
+    clk = clocks.stop(t_load0, time.time())
+    err = int(mgr.batch.error_flag.item())
+    rep = mgr.report()
+    mgr.restore()
+    if group is not None:
+        group.close()
+    if rank == 0:
+        hbm_peak, peak_kind = peaks()
+        w_bytes = sum(t.numel() * t.element_size() for n, t in list(model.named_parameters()) +
+                      list(model.named_buffers()) if "embed_tokens" not in n and "rotary" not in n)
+        host_bytes = host_pages * page_bytes          # streamed from the host every step
+        dev_kv = (L * B * local_pages - host_pages) * page_bytes
+        hbm_bytes = w_bytes + dev_kv + 2 * host_bytes   # staged pages are written, then read, on the device
+        line = {
+            "metric": C4_METRIC, "value": B / (ms * 1e-3) * 1.0, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 activations, int8 weights", "data": "synthetic (random-init "
+            "weights, seeded K/V, random token ids)",
+            "timing": "eager model.forward per token (mixed residency: host pages staged every layer), CUDA events",
+            "config": {"workload": "config4: random-init Qwen3-14B-shaped decoder (40 layers, hidden 5120, 40/8 "
+                                   "heads, d128, SwiGLU 17408), INT8 weight-only linears, batch 8, 32768-token paged "
+                                   "KV per sequence, oldest 50% of pages in pinned host memory",
+                       "model": "Qwen3-14B-shaped (random init)", "global_batch": B, "seq_len": ctx,
+                       "parallelism": f"kv-seq-shard{world}", "l2": "weights 14 GB + KV >> L2"},
+            "int8_linears": n_int8, "fill_seconds": round(t_fill, 1),
+            "pages_on_host": host_pages, "host_bytes_per_step": host_bytes,
+            "pcie_gbs": host_bytes / (ms * 1e-3) / 1e9,
+            "roofline": {"bound": "host link (PCIe) for the offloaded half; HBM for the rest",
+                         "achieved": hbm_bytes / (ms * 1e-3) / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": hbm_bytes / (ms * 1e-3) / 1e9 / hbm_peak, "traffic": None, "peak_kind": peak_kind,
+                         "bytes_per_step": hbm_bytes},
+            "cpu_baseline": None,
+            "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8 * B + host_bytes,
+                    "d2h_bytes_per_step": 8 * B, "ms_per_step": e2e_ms,
+                    "api": "model.forward with KVOffloadManager patches (INT8 linears); tokens read back each step"},
+            "gpu_launches": None, "clocks": clk, "device_error_flag": err, "kv_report": rep,
+        }
+        print(json.dumps(line, default=str), flush=True)
+    del model
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def cpu_baseline():
     from oracle.cpu_baseline import time_decode_attention
     c = CFG
@@ -1069,6 +1213,14 @@ def main():
             run_reference_config3(args, rank)
         else:
             run_config3(args, rank, local, world)
+        return
+    if args.workload == "config4":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "config 4 is a full 14B-parameter model "
+                                  "decode with 43 GB of KV; the reference's CPU path is infeasible at this size"}))
+        else:
+            run_config4(args, rank, local, world)
         return
     if args.impl == "reference":
         run_reference(args, rank)

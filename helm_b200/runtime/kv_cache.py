@@ -21,6 +21,8 @@ different by design:
 """
 from __future__ import annotations
 
+import heapq
+import itertools
 import math
 from typing import List, Optional
 
@@ -99,26 +101,26 @@ def _candidate(page) -> bool:
 
 
 class LayerKVCache:
-    """Per-layer page list (kv_cache.py:19-28), plus the layer's eviction candidates and a count
-    of non-GPU pages, both maintained as pages are appended and moved."""
+    """Per-layer page list (kv_cache.py:19-28), plus a count of non-GPU pages maintained as pages
+    are appended and moved."""
 
     def __init__(self, layer_id: int):
         self.layer_id = layer_id
         self.pages: List[KVPage] = []
         self.tail_page: Optional[KVPage] = None
         self.total_tokens: int = 0
-        self._evictable: List[KVPage] = []
         self._n_off: int = 0      # pages with state != 'GPU' and used_tokens > 0
         self._version: int = 0    # bumped on changes the device page table must resync
 
-    def append_page(self, page: KVPage):
+    def append_page(self, page: KVPage) -> Optional[KVPage]:
+        """Appends `page` as the new tail; returns the old tail if it just became an eviction
+        candidate (full, GPU-resident, no longer the tail)."""
         old = self.tail_page
-        if old is not None and _candidate(old):
-            self._evictable.append(old)
         if page.state != "GPU" and page.used_tokens > 0:
             self._n_off += 1
         self.pages.append(page)
         self.tail_page = page
+        return old if old is not None and _candidate(old) else None
 
 
 class KVCacheManager:
@@ -138,23 +140,36 @@ class KVCacheManager:
         # Set by KVOffloadManager: (DecodeBatch, row) when this sequence is one row of a batch
         # whose page tables live on the device.
         self._batch = None
-        self._n_evictable = 0  # sum of len(layer._evictable) over layers
+        # Eviction candidates in the reference's eviction order: a heap keyed by (start_token,
+        # layer order in self.layers, page position) -- exactly the order of its stable sort by
+        # start_token over the layer-by-layer, page-by-page scan (kv_cache.py:121-159) -- so an
+        # eviction costs O(log n) instead of a rescan and sort of every page per call.
+        self._heap: list = []
+        self._rank: dict = {}            # layer id -> position among self.layers' keys
+        self._tie = itertools.count()
+        self._n_evictable = 0            # live entries of the heap
 
     def _page_bytes(self) -> int:
         a = self.allocator
         elem = torch.tensor([], dtype=a.dtype).element_size()
         return a.num_kv_heads * a.page_size * a.head_dim * elem * 2
 
+    def _layer(self, layer_id: int) -> LayerKVCache:
+        layer = self.layers.get(layer_id)
+        if layer is None:
+            layer = self.layers[layer_id] = LayerKVCache(layer_id)
+            self._rank.setdefault(layer_id, len(self._rank))
+        return layer
+
     def initialize_layer_caches(self, num_layers: int):
         for i in range(num_layers):
-            self.layers[i] = LayerKVCache(layer_id=i)
+            self.layers[i] = LayerKVCache(layer_id=i)   # a replaced key keeps its dict position
+            self._rank.setdefault(i, len(self._rank))
 
     # ---- appends (kv_cache.py:55-113) ------------------------------------------------
     def append_prefill(self, layer_id: int, K_prefill: torch.Tensor, V_prefill: torch.Tensor):
         """Append prefill KV in page-sized chunks; residency enforced after every page."""
-        if layer_id not in self.layers:
-            self.layers[layer_id] = LayerKVCache(layer_id)
-        layer = self.layers[layer_id]
+        layer = self._layer(layer_id)
         seq_len = K_prefill.size(2)
         page_size = self.allocator.page_size
         device = K_prefill.device
@@ -185,9 +200,7 @@ class KVCacheManager:
     # The two halves of append_decode, so that a batched caller can write the token of every
     # sequence with one kernel launch between them.
     def _reserve_decode_slot(self, layer_id: int, device):
-        if layer_id not in self.layers:
-            self.layers[layer_id] = LayerKVCache(layer_id)
-        layer = self.layers[layer_id]
+        layer = self._layer(layer_id)
         new_page = False
         if layer.tail_page is None or layer.tail_page.used_tokens == layer.tail_page.capacity_tokens:
             page = self.allocator.allocate(device)
@@ -209,9 +222,11 @@ class KVCacheManager:
             self._enforce_residency_policy()
 
     def _append_page(self, layer: LayerKVCache, page: KVPage) -> None:
-        n0 = len(layer._evictable)
-        layer.append_page(page)
-        self._n_evictable += len(layer._evictable) - n0
+        cand = layer.append_page(page)
+        if cand is not None:
+            rank = self._rank.get(layer.layer_id, len(self._rank))
+            heapq.heappush(self._heap, (cand.start_token, rank, len(layer.pages) - 2, next(self._tie), layer, cand))
+            self._n_evictable += 1
 
     def iterate_layer_pages(self, layer_id: int):
         if layer_id not in self.layers:
@@ -220,47 +235,35 @@ class KVCacheManager:
 
     # ---- eviction (kv_cache.py:121-172) ------------------------------------------------
     def _candidates(self):
-        """(layer, page) pairs the reference scan would collect, in its order."""
-        out = []
-        for layer in self.layers.values():
-            keep = []
-            for page in layer._evictable:
-                if page is not layer.tail_page and _candidate(page):
-                    keep.append(page)
-                    out.append((layer, page))
-            layer._evictable = keep
-        return out
+        """(layer, page) pairs the reference scan would collect, in its eviction order."""
+        return [(e[4], e[5]) for e in sorted(self._heap) if self._live(e)]
+
+    @staticmethod
+    def _live(entry) -> bool:
+        _, _, pos, _, layer, page = entry
+        return pos < len(layer.pages) and layer.pages[pos] is page and page is not layer.tail_page and _candidate(page)
 
     def evict_pages(self, bytes_to_evict: int):
-        """Global oldest-page-first eviction to the CPU."""
+        """Global oldest-page-first eviction to the CPU; the byte budget is checked before each page."""
         if bytes_to_evict <= 0:
             return
-        gpu_pages = self._candidates()
-        gpu_pages.sort(key=lambda t: t[1].start_token)
         evicted_bytes = 0
-        moved = set()
-        for layer, page in gpu_pages:
-            if evicted_bytes >= bytes_to_evict:
-                break
+        heap = self._heap
+        while heap and evicted_bytes < bytes_to_evict:
+            entry = heapq.heappop(heap)
+            self._n_evictable -= 1
+            if not self._live(entry):
+                continue
+            _, _, idx, _, layer, page = entry
             original_start_token = page.start_token
             new_page = self.allocator.move_page(page, torch.device("cpu"))
             assert new_page.start_token == original_start_token, "Page invariant broken during migration"
-            idx = layer.pages.index(page)
             layer.pages[idx] = new_page
-            if layer.tail_page is page:
-                layer.tail_page = new_page
             if new_page.state != "GPU" and new_page.used_tokens > 0:
                 layer._n_off += 1
             layer._version += 1
-            moved.add(id(page))
             # full page capacity, as the reference counts it from the new page's tensors
             evicted_bytes += self._page_bytes()
-        n = 0
-        for layer in self.layers.values():
-            if moved and layer._evictable:
-                layer._evictable = [p for p in layer._evictable if id(p) not in moved]
-            n += len(layer._evictable)
-        self._n_evictable = n
 
     def _gpu_evictable_bytes(self) -> int:
         return self._n_evictable * self._page_bytes()
@@ -288,10 +291,11 @@ class KVCacheManager:
             layer.pages.clear()
             layer.tail_page = None
             layer.total_tokens = 0
-            layer._evictable = []
             layer._n_off = 0
             layer._version += 1
         self.layers.clear()
+        self._heap = []
+        self._rank = {}
         self._n_evictable = 0
 
     def all_gpu_resident(self, layer_id: int) -> bool:

@@ -66,10 +66,8 @@ class PageStore:
     def _alloc(self, n: int) -> torch.Tensor:
         shape = (n, 2, self.Hkv, self.P, self.D)
         if self.device.type == "cpu":
-            t = torch.empty(shape, dtype=self.dtype)
-            if torch.cuda.is_available():
-                t = t.pin_memory()
-            return t
+            # pinned from the start (no pageable copy first: host slabs can be tens of GB)
+            return torch.empty(shape, dtype=self.dtype, pin_memory=torch.cuda.is_available())
         return torch.empty(shape, dtype=self.dtype, device=self.device)
 
     def reserve(self, capacity: int) -> None:
