@@ -346,9 +346,12 @@ int helm_ipc_close(void *base);
  * Replaces the per-page H2D prefetch of perform_streaming_attention
  * (helm/runtime/kv_cache.py:412-423): copies `count` pages of page_bytes
  * bytes each from src_base + src_ids[i]*page_bytes (pinned host or device
- * memory) to dst_base + (dst_first + i)*page_bytes with cudaMemcpyAsync on
- * `stream`, merging runs of consecutive ids into one copy.  src_ids is a HOST
- * array.  Returns the number of cudaMemcpyAsync calls issued in *copies_out.
+ * memory) to dst_base + (dst_first + i)*page_bytes on `stream`.  When the ids
+ * form many runs, the source is pinned host memory the device can address and
+ * the destination is device memory, one gather kernel copies every page
+ * (16-byte loads over the host link); otherwise runs of consecutive ids are
+ * copied with one cudaMemcpyAsync each.  src_ids is a HOST array.  Returns the
+ * number of launches / copies issued in *copies_out.
  */
 int helm_copy_pages(void *dst_base, int64_t dst_first, const void *src_base,
                     const int32_t *src_ids, int32_t count, int64_t page_bytes,
