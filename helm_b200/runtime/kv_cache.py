@@ -162,9 +162,17 @@ class KVCacheManager:
         return layer
 
     def initialize_layer_caches(self, num_layers: int):
+        replaced = False
         for i in range(num_layers):
+            replaced |= i in self.layers
             self.layers[i] = LayerKVCache(layer_id=i)   # a replaced key keeps its dict position
             self._rank.setdefault(i, len(self._rank))
+        if replaced:
+            # pages of a replaced layer belong to no layer any more: the reference's scan never
+            # sees them again, so they leave the candidates (and the evictable byte count)
+            self._heap = [e for e in self._heap if self._live(e)]
+            heapq.heapify(self._heap)
+            self._n_evictable = len(self._heap)
 
     # ---- appends (kv_cache.py:55-113) ------------------------------------------------
     def append_prefill(self, layer_id: int, K_prefill: torch.Tensor, V_prefill: torch.Tensor):
@@ -238,10 +246,12 @@ class KVCacheManager:
         """(layer, page) pairs the reference scan would collect, in its eviction order."""
         return [(e[4], e[5]) for e in sorted(self._heap) if self._live(e)]
 
-    @staticmethod
-    def _live(entry) -> bool:
+    def _live(self, entry) -> bool:
+        """The entry is still a candidate: its layer is current, the page still sits at its
+        position and is full, GPU-resident and not the tail."""
         _, _, pos, _, layer, page = entry
-        return pos < len(layer.pages) and layer.pages[pos] is page and page is not layer.tail_page and _candidate(page)
+        return (self.layers.get(layer.layer_id) is layer and pos < len(layer.pages) and layer.pages[pos] is page
+                and page is not layer.tail_page and _candidate(page))
 
     def evict_pages(self, bytes_to_evict: int):
         """Global oldest-page-first eviction to the CPU; the byte budget is checked before each page."""
