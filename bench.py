@@ -1,20 +1,27 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 decode hot path (BASELINE config 5).
+"""Benchmark of the B200 decode hot path.
 
-Workload: long-context split-KV decode attention over a Qwen3-32B-shaped layer
-stack -- 64 layers, 64 query / 8 KV heads, head_dim 128, bf16, batch 4,
-131072 cached tokens per sequence in 64-token pages, KV sharded by sequence
-over the N GPUs (one process per GPU).  One step = one decode step of the
-stack: for every layer, append the new token's K/V (on the rank holding the
-sequence tail), run paged decode attention over the rank's shard, and --
-for N > 1 -- all-gather the per-head (m, l, o) records over NCCL and merge
-them.  Synthetic data (seeded normal K/V, random page placement); the KV
-working set (137 GB / N) is far larger than L2, so no flush is needed.
+Default workload (the metric's long-context decode): a Qwen3-32B-shaped
+attention stack -- 64 layers, 64 query / 8 KV heads, head_dim 128, bf16, batch 4, 131072 cached
+tokens per sequence in 64-token pages, KV sharded by sequence over the N GPUs (one process per
+GPU).  One step = one decode step of the stack: for every layer, append the new token's K/V (on
+the rank holding the sequence tail, device-directed) and run the persistent paged-attention
+kernel over the rank's shard; for N > 1 the kernel itself exchanges the per-head (m, l, o)
+records with the other ranks over NVLink and merges them.  Synthetic data (seeded normal K/V
+through KVCacheManager.append_prefill); the KV working set (137 GB / N) is far larger than L2, so
+no flush is needed.  The step is captured in a CUDA graph; `e2e` reruns it through the runtime's
+_decode_batched with pinned-host inputs and outputs.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl helm|reference]
+                  [--workload config5|config1|config2|config3|config4]
 
-Rank 0 prints one JSON line.  `--impl reference` times the reference's own
-CPU attention algorithm (oracle/cpu_baseline.py) on the host cores instead.
+Other workloads (single JSON line each): config1 -- the reference's mixed-residency fp32 case
+through perform_streaming_attention; config2 -- the INT8 GEMV shapes; config3 -- a Qwen3-8B-shaped
+decode step through KVOffloadManager (CUDA graph); config4 -- a Qwen3-14B-shaped INT8 decode step
+with half of the KV in pinned host memory.
+
+Rank 0 prints one JSON line.  `--impl reference` times the reference's own CPU algorithm on the
+host cores instead (oracle/cpu_baseline.py; the compiled reference GEMV for config2).
 """
 from __future__ import annotations
 
