@@ -324,6 +324,8 @@ def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store, out_record=
                                page_stride=store.page_elems, head_stride=store.head_stride,
                                num_pool_pages=store.capacity, scale=scale, max_pages=width, out=out,
                                out_record=out_record, error_flag=batch.error_flag, exchange=exchange)
+    if host_slots:
+        staging_for(store).consumed()
     return out
 
 

@@ -3,9 +3,9 @@
 * attend_page_list(): attention of a query over an arbitrary list of KVPages
   (what perform_streaming_attention receives).  Pages held by a device
   PageStore are read in place; pages in a host store are first copied into
-  staging slots of the device store with helm_copy_pages (runs of consecutive
-  slots become one cudaMemcpyAsync); pages given as loose tensors are gathered
-  into a temporary pool.
+  a double-buffered range of staging slots of the device store on a side
+  stream (helm_copy_pages; Staging below); pages given as loose tensors are
+  gathered into a temporary pool.
 * DecodeBatch: the int32 page tables [layers, B, width] of a batch of
   KVCacheManagers (one row per sequence), kept on the device and updated
   incrementally: a decode append writes its token and its table entry in the
@@ -29,35 +29,88 @@ def _is_cuda(device) -> bool:
 
 
 class Staging:
-    """A contiguous range of slots of a device PageStore reserved for host pages in flight."""
+    """Host pages in flight to the device: two ranges of slots of a device PageStore (a double
+    buffer, alternating per call), filled on a dedicated side stream with helm_copy_pages.
+
+    Ordering is by events only -- no host synchronisation:
+    * a copy into a range waits for the last consumer of that range (the event recorded by
+      consumed()) and for the host store's pending D2H copies (pages just evicted), not for the
+      rest of the consumer stream, so it can run ahead of kernels still queued there;
+    * the consumer stream waits for the copy's completion event before stage() returns.
+    The reference keeps one copy stream per device for the same purpose (kv_cache.py:315,413-414)."""
 
     def __init__(self, store: PageStore):
         self.store = store
-        self.start = -1
-        self.n = 0
+        self.ranges = [[-1, 0], [-1, 0]]     # (first slot, slots) of each half
+        self.turn = 0
+        self.stream = None
+        self.ready = [None, None]
+        self.done = [None, None]             # consumer-side events: the half's last reader finished
+
+    def _reserve(self, r: int, n: int) -> bool:
+        """Makes half r hold >= n slots; True when the slab had to grow (a reallocation copy on
+        the consumer stream that the side stream must then wait for)."""
+        start, have = self.ranges[r]
+        if n <= have:
+            return False
+        st = self.store
+        if have:
+            for s in range(start, start + have):
+                st.release(s)
+        grew = False
+        if st.next_slot + n > st.capacity:
+            st.reserve(max(st.capacity * 2, st.next_slot + n))
+            grew = True
+        self.ranges[r] = [st.next_slot, n]
+        st.next_slot += n
+        return grew
 
     def reserve(self, n: int) -> int:
-        if n > self.n:
-            st = self.store
-            if self.n:
-                for s in range(self.start, self.start + self.n):
-                    st.release(s)
-            # a fresh contiguous range at the end of the slab
-            if st.next_slot + n > st.capacity:
-                st.reserve(max(st.capacity * 2, st.next_slot + n))
-            self.start = st.next_slot
-            st.next_slot += n
-            self.n = n
-        return self.start
+        """First slot of the next half, sized for n pages (no copy)."""
+        r = self.turn
+        self._reserve(r, n)
+        return self.ranges[r][0]
 
     def stage(self, host_store: PageStore, host_slots: List[int]) -> int:
-        """Copies host pages into the first len(host_slots) staging slots; returns the first slot."""
-        start = self.reserve(len(host_slots))
-        if host_slots:
-            if host_store.slab.shape[1:] != self.store.slab.shape[1:] or host_store.dtype != self.store.dtype:
-                raise ValueError("staging: host and device page geometry differ")
-            ops.copy_pages(self.store.slab, start, host_store.slab, host_slots, self.store.page_bytes)
+        """Copies host pages into the next half's first len(host_slots) slots on the side stream and
+        makes the current stream wait for them; returns the first slot.  Call consumed() after
+        enqueueing the kernel that reads them."""
+        r = self.turn
+        self.turn ^= 1
+        grew = self._reserve(r, len(host_slots))
+        start = self.ranges[r][0]
+        if not host_slots:
+            return start
+        if host_store.slab.shape[1:] != self.store.slab.shape[1:] or host_store.dtype != self.store.dtype:
+            raise ValueError("staging: host and device page geometry differ")
+        dev = self.store.device
+        cur = torch.cuda.current_stream(dev)
+        if self.stream is None:
+            self.stream = torch.cuda.Stream(device=dev)
+            self.ready = [torch.cuda.Event(), torch.cuda.Event()]
+        side = self.stream
+        if grew:
+            side.wait_stream(cur)             # the slab was reallocated (copied) on this stream
+        elif self.done[r] is not None:
+            side.wait_event(self.done[r])     # the half's previous reader has finished
+        pend = host_store.pending_event
+        if pend is not None:
+            side.wait_event(pend)             # pages evicted just now: their D2H copies
+        ops.copy_pages(self.store.slab, start, host_store.slab, host_slots, self.store.page_bytes,
+                       stream=side.cuda_stream)
+        self.ready[r].record(side)
+        cur.wait_event(self.ready[r])
+        self._last = r
         return start
+
+    def consumed(self) -> None:
+        """Records, on the current stream, that the half filled by the last stage() may be reused."""
+        r = getattr(self, "_last", None)
+        if r is None:
+            return
+        ev = self.done[r] if self.done[r] is not None else torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.store.device))
+        self.done[r] = ev
 
 
 _STAGING = {}
@@ -133,6 +186,8 @@ def attend_page_list(query: torch.Tensor, pages: list, scale: float) -> torch.Te
         usedt = torch.tensor([used] * B, dtype=torch.int32).to(dev, non_blocking=False)
         npg = torch.full((B,), n, dtype=torch.int32, device=dev)
         _launch(q3, dev_store, table, usedt, npg, scale, out, n)
+        if host_slots:
+            staging_for(dev_store).consumed()
         return out.reshape(B, Hq, 1, D)
 
     # Loose tensors (or mixed stores): gather the used tokens into a temporary pool.
