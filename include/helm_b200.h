@@ -200,7 +200,12 @@ int helm_lse_merge(const float *partials, int32_t num_partials,
  * F32), bias [N] (same dtype as x) or null, y [M, N] of x_dtype.  fp32
  * accumulation.  Any M >= 1; K must be a multiple of 16; x and w 16-byte
  * aligned.  The weight streams through a TMA + mbarrier ring; the call encodes
- * (and caches) a tensor map over w on its first use.
+ * (and caches) a tensor map over w on its first use.  The kernel is launched
+ * with programmatic dependent launch: it starts reading w while the previous
+ * kernel on the stream may still be running (x is read only after that kernel
+ * has finished), so w must not be written by the kernel launched immediately
+ * before this call on the same stream -- weights written on the device need an
+ * event or any other launch in between.
  */
 int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
                      const void *w_scale, int32_t scale_dtype,
