@@ -1,7 +1,7 @@
 """Generates the golden fixtures in tests/golden/ from the HELM reference itself.
 
-Run in a checkout where the reference is importable (HELM_REFERENCE_ROOT,
-default /root/reference):  python tests/golden/make_golden.py
+Run where the reference checkout is importable (its root in HELM_REFERENCE_ROOT, else the
+default below):  python tests/golden/make_golden.py
 
 Fixtures written (all small; the GPU host never needs the reference):
   attention_cases.npz   -- outputs, for the seeded cases of cases.py, of the
