@@ -25,10 +25,11 @@ def test_rope_and_norm_formula_match_transformers(monkeypatch):
     ours = _ref(x, w, 1e-6, cos, sin)
     # the HF module computes its statistics in fp32 even for float64 inputs: agreement to fp32
     assert torch.allclose(ours, q_hf[:, :, 0].detach(), rtol=1e-5, atol=1e-5)
-    # and the tables equal the model's own rotary embedding at those positions
+    # and the tables equal the model's own rotary embedding at those positions (it forms the angles
+    # position * inv_freq in fp32: about 1e-7 relative, 2e-3 absolute at position 16000)
     cfg = m.Qwen3Config(hidden_size=256, num_attention_heads=2, num_key_value_heads=1, head_dim=D, rope_theta=1e6,
                         max_position_embeddings=40960)
     rot = m.Qwen3RotaryEmbedding(cfg)
     c_hf, s_hf = rot(x, torch.tensor([pos]).T)
-    assert torch.allclose(cos, c_hf[:, 0].double(), atol=1e-6)
-    assert torch.allclose(sin, s_hf[:, 0].double(), atol=1e-6)
+    assert torch.allclose(cos, c_hf[:, 0].double(), atol=3e-3)
+    assert torch.allclose(sin, s_hf[:, 0].double(), atol=3e-3)
