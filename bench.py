@@ -60,6 +60,8 @@ def parse():
                          "Qwen3-8B-shaped decode step through KVOffloadManager; config4: a Qwen3-14B-shaped "
                          "INT8 decode step with half the KV on the host")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub-records", action="store_true",
+                    help="config5 at N=1: skip the config-2 and config-1 sub-records of the line")
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--exchange", default="fused", choices=["fused", "p2p", "nccl"],
                     help="cross-GPU record exchange for N > 1")
@@ -222,10 +224,23 @@ def run_reference(args, rank):
 # ----------------------------------------------------------------------------
 # helm arm
 # ----------------------------------------------------------------------------
+CHUNK_PAGES = 64   # K/V are generated per chunk of 64 pages of one (layer, sequence)
+
+
+def kv_chunk(l, b, c, Hkv, D, P, dev):
+    """K and V [1, Hkv, CHUNK_PAGES*P, D] bf16 of chunk c (global pages c*64 .. c*64+63) of layer l,
+    sequence b: seeded by (l, b, c) alone, so any rank -- and the checker -- rebuilds any chunk."""
+    g = torch.Generator(device=dev).manual_seed(((l * 4096 + b) * 65536 + c) * 2 + 1)
+    K = torch.randn((1, Hkv, CHUNK_PAGES * P, D), generator=g, device=dev, dtype=torch.bfloat16)
+    V = torch.randn((1, Hkv, CHUNK_PAGES * P, D), generator=g, device=dev, dtype=torch.bfloat16)
+    return K, V
+
+
 class Stack:
     """The sharded attention stack on one rank, held by the drop-in runtime: a KVAllocator whose
     device slab holds every page, one KVCacheManager per sequence (prefilled through
-    append_prefill) and the batch's device page tables (DecodeBatch)."""
+    append_prefill) and the batch's device page tables (DecodeBatch).  K/V come from kv_chunk (the
+    rank's share of every sequence); q and the appended tokens are the same on every rank."""
 
     def __init__(self, rank, world, dev, spare_pages, exchange="fused"):
         from helm_b200 import ops
@@ -247,14 +262,17 @@ class Stack:
         self.alloc.reserve_capacity(dev, self.L * self.B * (self.npg + self.spare) + 4 * self.L * self.B + 64)
         self.kvcms = [KVCacheManager(self.alloc, gpu_high_watermark_bytes=1 << 62) for _ in range(self.B)]
         self.batch = DecodeBatch(self.kvcms, self.L, dev, width=self.npg + self.spare + 8)
-        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        self.plo, self.phi = plo, phi
         for l in range(self.L):
             for b in range(self.B):
-                K = torch.randn((1, self.Hkv, self.local_ctx, self.D), generator=g, device=dev, dtype=torch.bfloat16)
-                V = torch.randn((1, self.Hkv, self.local_ctx, self.D), generator=g, device=dev, dtype=torch.bfloat16)
-                self.kvcms[b].append_prefill(l, K, V)
+                for c in range(plo // CHUNK_PAGES, (phi + CHUNK_PAGES - 1) // CHUNK_PAGES):
+                    K, V = kv_chunk(l, b, c, self.Hkv, self.D, self.P, dev)
+                    t0 = max(plo - c * CHUNK_PAGES, 0) * self.P
+                    t1 = (min(phi, (c + 1) * CHUNK_PAGES) - c * CHUNK_PAGES) * self.P
+                    self.kvcms[b].append_prefill(l, K[:, :, t0:t1], V[:, :, t0:t1])
                 self.batch.sync_row(l, b)
         del K, V
+        g = torch.Generator(device=dev).manual_seed(1234)   # q and new tokens: identical on every rank
         self.store = self.alloc.store(dev)
         self.n_pool = self.store.capacity
         # spare pages for the device-directed appends of the graph-captured step (tail rank)
@@ -389,6 +407,9 @@ def run_helm(args, rank, local, world):
     ms = t0.elapsed_time(t1)
     ms_max = max_over_ranks(ms, world, dev)
     ms_step = ms_max / args.steps
+    # correctness of what was timed: eager warm-up steps + the warm replay + the timed replays each
+    # appended one token per (layer, sequence)
+    check = check_stack(st, stream, world, dev, appended=args.warmup + 1 + args.steps)
 
     # Attention-call durations for the roofline: back-to-back calls over every layer, each
     # bracketed by CUDA events on the launching stream (no other work in between).
@@ -416,7 +437,7 @@ def run_helm(args, rank, local, world):
 
     if rank == 0:
         hbm_peak, peak_kind = peaks()
-        tokens_per_seq = st.local_ctx + args.warmup + 1 + args.steps
+        tokens_per_seq = st.local_ctx + ((args.warmup + 1 + args.steps) if st.tail else 0)
         bytes_launch = st.attn_bytes(tokens_per_seq)
         achieved = bytes_launch / (attn_avg_ms * 1e-3) / 1e9
         step_bytes_all = bytes_launch * st.L * world
@@ -445,21 +466,95 @@ def run_helm(args, rank, local, world):
                          "traffic_source": "ncu dram__bytes_read/write.sum of a 268.7 MB launch, reads scaled "
                                            "by the units streamed (profiles/attn_tc_persistent_config5.txt)",
                          "peak_kind": peak_kind,
-                         "kernel": "attn_tc_persistent_kernel (one helm_paged_attn_decode call: counter memset + kernel)",
+                         "kernel": "attn_tc_persistent_kernel (one helm_paged_attn_decode call = one launch)",
                          "bytes_per_launch": bytes_launch, "avg_launch_ms": attn_avg_ms},
             "breakdown_ms_per_layer": breakdown,
+            "check": check,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": st.launches_per_step * args.steps,
             "clocks": clk,
             "device_error_flag": err,
         }
-        print(json.dumps(line), flush=True)
     barrier(world)
     if st.shard is not None:
         st.shard.close()
+    if world == 1 and not args.no_sub_records:
+        # configs 2 and 1 (the INT8 GEMV shapes and the reference's fp32 single-layer case), timed in
+        # the same run after the config-5 pool is released, nested in the one line as sub-records
+        del st
+        torch.cuda.empty_cache()
+        subs = {}
+        for name, fn in (("config2", config2_line), ("config1", config1_line)):
+            subs[name] = fn(args, rank, world, dev)
+        if rank == 0:
+            line["sub_records"] = subs
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def check_stack(st, stream, world, dev, appended):
+    """Correctness of the sharded stack, outside the timed region.  Every rank makes one more
+    attention call of the last layer (exchange included) into an fp32 output; the outputs of all
+    ranks must be bit-identical, and rank 0 recomputes 2 sequences x 2 kv heads of it in float64
+    on the host from the seeds: every cached token (kv_chunk of every global page) plus the
+    `appended` decode tokens (the step appends the same k_new / v_new each time), softmax
+    attention as in the reference's all-CPU path (kv_cache.py:376-380).  Returns the check record
+    on rank 0."""
+    from helm_b200 import _native as N
+    l = st.L - 1
+    out32 = torch.empty((st.B, st.Hq, st.D), dtype=torch.float32, device=dev)
+    p = N.PagedAttnParams()
+    ctypes.memmove(ctypes.byref(p), ctypes.byref(st.attn_params[l]), ctypes.sizeof(p))
+    p.out = out32.data_ptr()
+    p.out_dtype = N.F32
+    p.out_record = None
+    if world > 1 and not st.fused:
+        p.out = None
+        p.out_record = st.rec[l].data_ptr()
+    N.check("helm_paged_attn_decode", st.lib.helm_paged_attn_decode(ctypes.byref(p), stream.cuda_stream))
+    if world > 1 and not st.fused:
+        st.shard.gather_merge(st.rec[l], out=out32.view(st.B * st.Hq, st.D))
+    torch.cuda.synchronize(dev)
+    identical = True
+    if world > 1:
+        import torch.distributed as dist
+        got = [torch.empty_like(out32) for _ in range(world)]
+        dist.all_gather(got, out32)
+        identical = all(torch.equal(got[0], t) for t in got[1:])
+    if st.rank != 0:
+        return None
+    gq = st.Hq // st.Hkv
+    scale = 1.0 / math.sqrt(st.D)
+    n_chunks = (CFG["ctx"] // st.P + CHUNK_PAGES - 1) // CHUNK_PAGES
+    max_err, max_ref = 0.0, 0.0
+    seqs, heads = sorted({0, st.B - 1}), sorted({0, st.Hkv - 1})
+    for b in seqs:
+        ks = {g: [] for g in heads}
+        vs = {g: [] for g in heads}
+        for c in range(n_chunks):
+            K, V = kv_chunk(l, b, c, st.Hkv, st.D, st.P, dev)
+            n_tok = min(CHUNK_PAGES * st.P, CFG["ctx"] - c * CHUNK_PAGES * st.P)
+            for g in heads:
+                ks[g].append(K[0, g, :n_tok].cpu())
+                vs[g].append(V[0, g, :n_tok].cpu())
+        for g in heads:
+            k_all = torch.cat(ks[g] + [st.k_new[l, b, g].cpu()[None]] * appended).double()
+            v_all = torch.cat(vs[g] + [st.v_new[l, b, g].cpu()[None]] * appended).double()
+            q = st.q[l, b, g * gq:(g + 1) * gq].cpu().double()
+            w = torch.softmax((q @ k_all.T) * scale, dim=-1)
+            ref = w @ v_all
+            got = out32[b, g * gq:(g + 1) * gq].cpu().double()
+            max_err = max(max_err, float((got - ref).abs().max()))
+            max_ref = max(max_ref, float(ref.abs().max()))
+    rel = max_err / max_ref if max_ref > 0 else max_err
+    return {"rel_err": rel, "max_abs_err": max_err, "max_ref": max_ref, "bar": 2e-3, "ok": rel <= 2e-3,
+            "ranks_bit_identical": identical,
+            "sample": (f"last layer, sequences {seqs} x kv heads {heads} ({len(seqs) * len(heads) * gq} query "
+                       f"heads), all {CFG['ctx'] + appended} cached tokens, fp32 kernel output vs float64 "
+                       f"softmax attention on the host")}
 
 
 def component_breakdown(st, stream, world, dev, reps=3):
@@ -564,16 +659,28 @@ def c2_inputs(Nn, K, M, dev, copies):
 
 
 def run_config2(args, rank, local, world):
-    """Device time of helm_int8_linear at every config-2 shape: a CUDA graph of one call per weight
-    copy (copies rotate through > 4x L2, so every call streams its weight from HBM), replayed;
-    CUDA events on the launching stream.  Replicas only: every rank runs the same work."""
-    from helm_b200 import _native as N
-    from helm_b200 import ops
-    from helm_b200.kernels import Int8Linear
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     init_pg(world, local)
+    line = config2_line(args, rank, world, dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    barrier(world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def config2_line(args, rank, world, dev):
+    """Device time of helm_int8_linear at every config-2 shape: a CUDA graph of one call per weight
+    copy (copies rotate through > 4x L2, so every call streams its weight from HBM), replayed;
+    CUDA events on the launching stream.  Replicas only: every rank runs the same work.  Returns
+    the JSON record (rank 0; None elsewhere)."""
+    from helm_b200 import _native as N
+    from helm_b200 import ops
+    from helm_b200.kernels import Int8Linear
     stream = torch.cuda.current_stream(dev)
+    local = dev.index
     lib = N.lib()
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     clocks = ClockSampler(gpu_selector(dev, local))
@@ -661,11 +768,8 @@ def run_config2(args, rank, local, world):
             "gpu_launches": len(cases) * 1,
             "clocks": clk,
         }
-        print(json.dumps(line), flush=True)
-    barrier(world)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
+        return line
+    return None
 
 
 def c2_reference_time(min_seconds=2.0):
@@ -746,16 +850,25 @@ def _c1_manager(dev, seed):
 
 
 def run_config1(args, rank, local, world):
-    """perform_streaming_attention (the drop-in call) on the reference's config 1: pages 0-31 evicted
-    to pinned host memory through KVCacheManager.evict_pages, pages 32-63 resident; every call stages
-    the host pages into device slots and attends over all 64.  Also the kernel alone on 8 all-resident
-    instances (rotating through > 2x L2), from prebuilt device page tables in a CUDA graph."""
-    from helm_b200 import ops
-    from helm_b200.runtime import perform_streaming_attention
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     init_pg(world, local)
+    line = config1_line(args, rank, world, dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    barrier(world)
+
+
+def config1_line(args, rank, world, dev):
+    """perform_streaming_attention (the drop-in call) on the reference's config 1: pages 0-31 evicted
+    to pinned host memory through KVCacheManager.evict_pages, pages 32-63 resident; every call stages
+    the host pages into device slots and attends over all 64.  Also the kernel alone on 8 all-resident
+    instances (rotating through > 2x L2), from prebuilt device page tables in a CUDA graph.  Returns
+    the JSON record (rank 0; None elsewhere)."""
+    from helm_b200 import ops
+    from helm_b200.runtime import perform_streaming_attention
     stream = torch.cuda.current_stream(dev)
+    local = dev.index
     c = C1
     clocks = ClockSampler(gpu_selector(dev, local))
     clocks.start()
@@ -856,8 +969,8 @@ def run_config1(args, rank, local, world):
             "gpu_launches": None,
             "clocks": clk,
         }
-        print(json.dumps(line), flush=True)
-    barrier(world)
+        return line
+    return None
 
 
 def run_reference_config1(args, rank):

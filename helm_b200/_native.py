@@ -14,7 +14,10 @@ import pathlib
 LIB_PATH = pathlib.Path(os.environ.get(
     "HELM_B200_LIB", pathlib.Path(__file__).resolve().parent / "lib" / "libhelm_b200.so"))
 
-ABI_VERSION = 2
+ABI_VERSION = 3
+
+# bytes at the start of an attention workspace reserved for the call token and arrival counters
+WORKSPACE_HEADER_BYTES = 256
 
 # helm_dtype
 F32, F16, BF16, I8 = 0, 1, 2, 3
@@ -39,6 +42,7 @@ class ShardExchange(ctypes.Structure):
         ("rank", _i32), ("world", _i32),
         ("peer_recv", _p * MAX_RANKS), ("peer_flags", _p * MAX_RANKS),
         ("recv_local", _p), ("flags_local", _p), ("counters", _p),
+        ("wait_ns", ctypes.c_uint64),
     ]
 
 
@@ -92,6 +96,7 @@ class GatherMergeParams(ctypes.Structure):
         ("peer_recv", _p * MAX_RANKS), ("peer_flags", _p * MAX_RANKS),
         ("recv_local", _p), ("flags_local", _p), ("counters", _p),
         ("out", _p), ("out_dtype", _i32), ("out_record", _p), ("error_flag", _p),
+        ("wait_ns", ctypes.c_uint64),
     ]
 
 
@@ -108,6 +113,7 @@ SIGNATURES = [
     ("helm_decode_prologue", _c.c_int, [_c.POINTER(DecodePrologueParams), _p]),
     ("helm_rmsnorm", _c.c_int, [_p, _i32, _i64, _p, _i32, _p, _i64, _i64, _i32, ctypes.c_float, _p]),
     ("helm_copy_pages", _c.c_int, [_p, _i64, _p, _p, _i32, _i64, _c.POINTER(_i32), _p]),
+    ("helm_move_pages", _c.c_int, [_p, _p, _p, _p, _i32, _i64, _i64, _i64, _c.POINTER(_i32), _p]),
     ("helm_gather_merge_state_bytes", _i64, [_i32, _i32, _i32, _c.POINTER(_i64), _c.POINTER(_i64),
                                               _c.POINTER(_i64)]),
     ("helm_gather_merge", _c.c_int, [_c.POINTER(GatherMergeParams), _p]),

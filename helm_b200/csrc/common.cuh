@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdarg>
+#include <utility>
 
 #include "../../include/helm_b200.h"
 
@@ -85,5 +86,32 @@ __device__ __forceinline__ void flag_error(int32_t *flag, int bits) {
 }
 
 constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with launch_pdl() may start
+// while the previous kernel on the stream is still running: it must call
+// pdl_wait() before reading anything an earlier kernel writes (and before
+// writing anything an earlier kernel may still read).  pdl_trigger() lets the
+// next kernel on the stream start its own prologue early.  Both are no-ops in a
+// kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace helm

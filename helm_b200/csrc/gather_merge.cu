@@ -40,6 +40,7 @@ struct GatherArgs {
   int out_dtype;
   float *out_record;
   int32_t *error_flag;
+  uint64_t wait_ns;
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(kThreads) gather_merge_kernel(GatherArgs a) {
           ok = true;
           break;
         }
-        if (now_ns() - t0 > kWaitNs) break;
+        if (now_ns() - t0 > a.wait_ns) break;
       }
     }
     if (!ok) {
@@ -201,6 +202,7 @@ extern "C" int helm_gather_merge(const helm_gather_merge_params *p, void *stream
   a.out_dtype = p->out_dtype;
   a.out_record = p->out_record;
   a.error_flag = p->error_flag;
+  a.wait_ns = p->wait_ns ? p->wait_ns : kWaitNs;
   gather_merge_kernel<<<a.nblocks, kThreads, 0, as_stream(stream)>>>(a);
   return check_launch("gather_merge_kernel");
 }

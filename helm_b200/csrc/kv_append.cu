@@ -89,6 +89,9 @@ __device__ void resolve_dest(const AppendArgs &a, int b, int local, int &pid_out
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   __shared__ int s_pid, s_slot;
   const int b = a.b0 + blockIdx.x;
+  // Programmatic dependent launch: only the launch overlaps the previous kernel.
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) resolve_dest(a, b, blockIdx.x, s_pid, s_slot);
   __syncthreads();
   const int pid = s_pid, slot = s_slot;
@@ -174,6 +177,8 @@ __global__ void __launch_bounds__(256) decode_prologue_kernel(AppendArgs a, Prol
   __shared__ int s_pid, s_slot;
   const int b = a.b0 + blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) {
     if (pr.do_append) {
       resolve_dest(a, b, blockIdx.x, s_pid, s_slot);
@@ -303,7 +308,7 @@ extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
   if (rc != HELM_OK || p->B == 0) return rc;
   cudaStream_t st = as_stream(stream);
   return launch_rows(p, append_args(p), [&](const AppendArgs &a, int blocks) {
-    kv_append_kernel<<<blocks, 256, 0, st>>>(a);
+    launch_pdl(kv_append_kernel, dim3(blocks), dim3(256), 0, st, a);
   }, "kv_append_kernel");
 }
 
@@ -344,6 +349,6 @@ extern "C" int helm_decode_prologue(const helm_decode_prologue_params *p, void *
   pr.do_append = p->do_append;
   cudaStream_t st = as_stream(stream);
   return launch_rows(ap, append_args(ap), [&](const AppendArgs &a, int blocks) {
-    decode_prologue_kernel<<<blocks, 256, 0, st>>>(a, pr);
+    launch_pdl(decode_prologue_kernel, dim3(blocks), dim3(256), 0, st, a, pr);
   }, "decode_prologue_kernel");
 }

@@ -599,7 +599,9 @@ constexpr int kMaxPending = 64;  // deferred merges per CTA
 struct PersistArgs {
   float *rec_o;        // [C + pairs][gq][D]: CTA c's unnormalised o for pair p at slot c + p
   float *rec_ml;       // [C + pairs][gq][2]: its (m, l)
-  uint32_t *counter;   // [pairs], zero at launch
+  uint64_t *counter;   // [pairs]: (call token << 32) | arrivals; a word with another token counts 0
+  uint32_t *token;     // workspace header: token of the last completed call
+  uint64_t *done;      // workspace header: (token << 32) | CTAs finished
   int C;               // grid size
   // Fused cross-GPU exchange (xworld > 1).  Receive slots of every rank: [2][G][B*Hq][D+2] words
   // of 64 bits, each one value (o[0..D), m, l) in the low half and the call's epoch in the high
@@ -608,9 +610,23 @@ struct PersistArgs {
   uint64_t *xrecv[HELM_MAX_RANKS];
   uint64_t *xrecv_local;
   uint32_t *xsent;                  // [pairs]: exchanges done per pair (epoch of the next is +1)
+  uint64_t xwait_ns;                // bound of each wait for peers' words
 };
 
 constexpr uint64_t kExchangeWaitNs = 2000000000ull;
+
+// Adds one arrival to a token-tagged counter word and returns the arrivals after it; a word that
+// carries another call's token (stale, or never written) counts as zero.
+__device__ __forceinline__ uint32_t tagged_arrive(uint64_t *word, uint32_t tok) {
+  unsigned long long old = *reinterpret_cast<volatile unsigned long long *>(word);
+  for (;;) {
+    const uint32_t cnt = (uint32_t)(old >> 32) == tok ? (uint32_t)old : 0u;
+    const unsigned long long nw = ((unsigned long long)tok << 32) | (cnt + 1u);
+    const unsigned long long prev = atomicCAS(reinterpret_cast<unsigned long long *>(word), old, nw);
+    if (prev == old) return cnt + 1u;
+    old = prev;
+  }
+}
 
 __device__ __forceinline__ uint64_t ll_word(float v, uint32_t epoch) {
   return ((uint64_t)epoch << 32) | __float_as_uint(v);
@@ -636,7 +652,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     attn_tc_persistent_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                               AttnArgs a, PersistArgs pa) {
   constexpr int HN = NT * 8;        // padded heads per kv head
-  constexpr int EPT = HN;           // merge elements per consumer thread: HN * D / 128
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kStages];
   __shared__ __align__(8) uint64_t empty_bar[kStages];
@@ -652,6 +667,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __shared__ float mg_M[HN], mg_L[HN], mg_A[HN];
   __shared__ int pending[kMaxPending];
   __shared__ int npending;
+  __shared__ uint32_t call_tok;
   __shared__ uint32_t xs_epoch;
   __shared__ int xs_dead;  // a wait of this CTA ran out: later exchanges do not wait again
   __shared__ uint64_t *xs_peer[HELM_MAX_RANKS];  // pa.xrecv (dynamic indexing of a kernel parameter array
@@ -662,7 +678,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int gq = a.gq, B = a.B, Hkv = a.Hkv;
-  const int rl = D + 2;
 
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -674,7 +689,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int r = 0; r < HELM_MAX_RANKS; ++r) xs_peer[r] = pa.xrecv[r];
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmK)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmV)) : "memory");
   }
+  // Launched with programmatic dependent launch: everything above overlapped the previous
+  // kernel; page tables, q, the workspace and the outputs are touched only after it finished.
+  pdl_trigger();
+  pdl_wait();
+  if (tid == 0) call_tok = *reinterpret_cast<volatile uint32_t *>(pa.token) + 1u;
   // Units per sequence and their prefix sums (warp 0: chunked scan).
   if (warp == 0) {
     const int per = (B + 31) / 32;
@@ -941,7 +963,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               if (!timed) {
                 t0 = global_ns();
                 timed = true;
-              } else if (global_ns() - t0 > kExchangeWaitNs) {
+              } else if (global_ns() - t0 > pa.xwait_ns) {
                 ok = false;
                 break;
               }
@@ -1133,8 +1155,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int b = pair / Hkv, g = pair - b * Hkv;
           const int64_t up = seq_prefix[b] + (int64_t)g * seq_pages[b];
           const int c0 = owner_cta(up, U, C), c1 = owner_cta(up + seq_pages[b] - 1, U, C);
-          const uint32_t old = atomicAdd(&pa.counter[pair], 1u);
-          if (old + 1 == (uint32_t)(c1 - c0 + 1)) pending[npending++] = pair;
+          if (tagged_arrive(&pa.counter[pair], call_tok) == (uint32_t)(c1 - c0 + 1)) pending[npending++] = pair;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       } else if (nvalid > 0 && nvalid < 16) {
@@ -1242,6 +1263,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
+  // The last CTA to finish publishes this call's token: the next call (which starts reading the
+  // workspace only after this grid has finished) then treats every counter word of this call
+  // as stale, so no counter ever needs zeroing.
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (tagged_arrive(pa.done, call_tok) == gridDim.x) *reinterpret_cast<volatile uint32_t *>(pa.token) = call_tok;
+  }
 }
 
 }  // namespace tc
@@ -1413,6 +1442,9 @@ Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
   if (Cp < 1) Cp = 1;
   // a CTA covers at most units_max/C + 1 units, hence at most that many + 1 pairs
   const bool pending_ok = pairs_all <= tc::kMaxPending || units_max / Cp + 2 <= tc::kMaxPending;
+  // Workspace layout: the header (call token at byte 0, finished-CTA word at byte 8), then the
+  // CTA records (persistent path) or the split records (split path).
+  constexpr int64_t H = HELM_WORKSPACE_HEADER_BYTES;
   if (p->num_splits == 0 && eligible && p->B <= tc::kMaxSeqs && pending_ok && units_max < (1ll << 31) &&
       !env_flag("HELM_B200_NO_PERSISTENT")) {
     pl.persistent = true;
@@ -1421,13 +1453,13 @@ Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
     const int gq = p->Hq / p->Hkv;
     const int64_t slots = pl.C + (int64_t)pairs;
     pl.rec_bytes = slots * gq * p->D * (int64_t)sizeof(float);                 // o
-    pl.ml_off = (pl.rec_bytes + 255) / 256 * 256;
+    pl.ml_off = H + (pl.rec_bytes + 255) / 256 * 256;
     pl.counter_off = (pl.ml_off + slots * gq * 2 * (int64_t)sizeof(float) + 255) / 256 * 256;
-    pl.bytes = pl.counter_off + (int64_t)pairs * sizeof(uint32_t);
+    pl.bytes = pl.counter_off + (int64_t)pairs * sizeof(uint64_t);
     return pl;
   }
   pl.S = resolve_splits(p);
-  pl.bytes = pl.S > 1 ? (int64_t)pl.S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
+  pl.bytes = pl.S > 1 ? H + (int64_t)pl.S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
   return pl;
 }
 
@@ -1492,7 +1524,9 @@ template <typename T, int NT>
 int launch_tc_persistent(const CUtensorMap &mk, const CUtensorMap &mv, const AttnArgs &a,
                          const tc::PersistArgs &pa, cudaStream_t st) {
   ensure_smem_attr(tc::attn_tc_persistent_kernel<T, NT>, tc::kSmemBytes);
-  tc::attn_tc_persistent_kernel<T, NT><<<pa.C, tc::kThreads, tc::kSmemBytes, st>>>(mk, mv, a, pa);
+  const cudaError_t e = launch_pdl(tc::attn_tc_persistent_kernel<T, NT>, dim3(pa.C), dim3(tc::kThreads),
+                                   tc::kSmemBytes, st, mk, mv, a, pa);
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: launch: %s", cudaGetErrorString(e));
   return check_launch("attn_tc_persistent_kernel");
 }
 
@@ -1552,8 +1586,9 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
   a.scale_log2 = p->scale * kLog2e;
   a.num_splits = S;
   a.error_flag = p->error_flag;
+  float *const records = p->workspace ? p->workspace + HELM_WORKSPACE_HEADER_BYTES / sizeof(float) : nullptr;
   if (S > 1) {
-    a.rec = p->workspace;
+    a.rec = records;
   } else {
     a.out = p->out;
     a.out_record = p->out_record;
@@ -1570,10 +1605,14 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
     const bool two = a.gq > 8;
     if (pl.persistent) {
       tc::PersistArgs pa{};
-      pa.rec_o = p->workspace;
-      pa.rec_ml = reinterpret_cast<float *>(reinterpret_cast<char *>(p->workspace) + pl.ml_off);
-      pa.counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(p->workspace) + pl.counter_off);
+      char *ws = reinterpret_cast<char *>(p->workspace);
+      pa.rec_o = records;
+      pa.rec_ml = reinterpret_cast<float *>(ws + pl.ml_off);
+      pa.counter = reinterpret_cast<uint64_t *>(ws + pl.counter_off);
+      pa.token = reinterpret_cast<uint32_t *>(ws);
+      pa.done = reinterpret_cast<uint64_t *>(ws + 8);
       pa.C = pl.C;
+      pa.xwait_ns = tc::kExchangeWaitNs;
       pa.xrank = 0;
       pa.xworld = 0;
       if (p->exchange && p->exchange->world > 1) {
@@ -1583,9 +1622,8 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
         for (int r = 0; r < x->world; ++r) pa.xrecv[r] = reinterpret_cast<uint64_t *>(x->peer_recv[r]);
         pa.xrecv_local = reinterpret_cast<uint64_t *>(x->recv_local);
         pa.xsent = x->counters;
+        if (x->wait_ns) pa.xwait_ns = x->wait_ns;
       }
-      cudaError_t e = cudaMemsetAsync(pa.counter, 0, (size_t)p->B * p->Hkv * sizeof(uint32_t), st);
-      if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: cudaMemsetAsync: %s", cudaGetErrorString(e));
       a.rec = nullptr;
       a.out = p->out;
       a.out_record = p->out_record;
@@ -1608,7 +1646,7 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
     }
   }
   if (rc != HELM_OK || S == 1) return rc;
-  lse_merge_kernel<<<rows, 128, 0, st>>>(p->workspace, S, (int64_t)rows * (p->D + 2), rows, p->D, p->out,
+  lse_merge_kernel<<<rows, 128, 0, st>>>(records, S, (int64_t)rows * (p->D + 2), rows, p->D, p->out,
                                          p->out_dtype, p->out_record);
   return check_launch("lse_merge_kernel");
 }
@@ -1667,7 +1705,7 @@ extern "C" int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, v
   int rc = validate(p);
   if (rc != HELM_OK) return rc;
   if (p->B == 0 || p->Hq == 0) return HELM_OK;
-  const int64_t cap = HELM_NOALLOC_SCRATCH_BYTES;
+  const int64_t cap = HELM_NOALLOC_SCRATCH_BYTES - HELM_WORKSPACE_HEADER_BYTES;  // bytes for records
   const int64_t per_split = (int64_t)p->B * p->Hq * (p->D + 2) * (int64_t)sizeof(float);
   int S = resolve_splits(p);
   if (S > 1 && (int64_t)S * per_split > cap) {
@@ -1686,7 +1724,7 @@ extern "C" int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, v
   if (S > 1) {
     rc = noalloc_scratch(&q.workspace);
     if (rc != HELM_OK) return rc;
-    q.workspace_bytes = cap;
+    q.workspace_bytes = HELM_NOALLOC_SCRATCH_BYTES;
   }
   return helm_paged_attn_decode(&q, stream);
 }

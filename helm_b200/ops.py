@@ -282,6 +282,12 @@ def copy_pages(dst: torch.Tensor, dst_first: int, src: torch.Tensor, src_ids, pa
     """Copies pages src[src_ids[i]] -> dst[dst_first + i] (runs merged); returns the copy count."""
     import numpy as np
     ids = np.ascontiguousarray(np.asarray(src_ids, dtype=np.int32))
+    if len(ids):
+        if int(ids.min()) < 0 or int(ids.max()) >= src.shape[0]:
+            raise ValueError(f"copy_pages: source page ids must lie in [0, {src.shape[0]})")
+        if dst_first < 0 or dst_first + len(ids) > dst.shape[0]:
+            raise ValueError(f"copy_pages: destination pages [{dst_first}, {dst_first + len(ids)}) outside "
+                             f"[0, {dst.shape[0]})")
     dev = dst.device if dst.device.type == "cuda" else src.device
     st = _stream(dev) if stream is None else stream
     n = ctypes.c_int32(0)
@@ -289,4 +295,25 @@ def copy_pages(dst: torch.Tensor, dst_first: int, src: torch.Tensor, src_ids, pa
                                    ids.ctypes.data_as(ctypes.c_void_p), len(ids), int(page_bytes),
                                    ctypes.byref(n), st)
     N.check("helm_copy_pages", code)
+    return n.value
+
+
+def move_pages(dst: torch.Tensor, dst_ids, src: torch.Tensor, src_ids, page_bytes: int,
+               stream: Optional[int] = None) -> int:
+    """helm_move_pages: src[src_ids[i]] -> dst[dst_ids[i]] for slabs whose first dimension is the page
+    (ids checked against both slabs' page counts); returns the launch / copy count."""
+    import numpy as np
+    s_ids = np.ascontiguousarray(np.asarray(src_ids, dtype=np.int32))
+    d_ids = np.ascontiguousarray(np.asarray(dst_ids, dtype=np.int32))
+    if s_ids.shape != d_ids.shape:
+        raise ValueError("move_pages: src_ids and dst_ids differ in length")
+    dev = src.device if src.device.type == "cuda" else dst.device
+    if dev.type != "cuda":
+        raise ValueError("helm_b200.move_pages: one slab must be on a CUDA device")
+    st = _stream(dev) if stream is None else stream
+    n = ctypes.c_int32(0)
+    code = N.lib().helm_move_pages(dst.data_ptr(), d_ids.ctypes.data_as(ctypes.c_void_p), src.data_ptr(),
+                                   s_ids.ctypes.data_as(ctypes.c_void_p), len(s_ids), int(page_bytes),
+                                   int(dst.shape[0]), int(src.shape[0]), ctypes.byref(n), st)
+    N.check("helm_move_pages", code)
     return n.value

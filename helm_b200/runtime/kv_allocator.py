@@ -63,6 +63,13 @@ class KVAllocator:
             self._stores[key] = st
         return st
 
+    def flush_migrations(self) -> None:
+        """Issues every queued eviction copy (batched helm_move_pages launches on the transfer
+        streams); nothing waits for them here."""
+        for st in self._stores.values():
+            if st.pending_moves:
+                st.flush_moves()
+
     def reserve_capacity(self, device, pages: int) -> None:
         """Pre-sizes the slab of `device` for `pages` slots (avoids growth copies later).
         No bookkeeping changes: page ids and pool counters are untouched."""
@@ -131,15 +138,18 @@ class KVAllocator:
             return page
         new_page = self.allocate(target_device)
         used = page.used_tokens
+        queued = False
         if used > 0:
-            copy_page_tokens(page, new_page, used)
+            queued = copy_page_tokens(page, new_page, used)
         new_page.layer_id = page.layer_id
         new_page.start_token = page.start_token
         new_page.used_tokens = used
         new_page.device = target_device
 
         if _is_cuda(page.device) and not _is_cuda(target_device):
-            page.detach_storage(release=True)
+            # a queued copy still has to read the source slot: its store quarantines the slot when
+            # the copy is issued, instead of freeing it now
+            page.detach_storage(release=not queued)
             page.k_tensor = torch.empty(0, dtype=self.dtype)
             page.v_tensor = torch.empty(0, dtype=self.dtype)
             page.state = "DEAD"
@@ -167,24 +177,26 @@ class KVAllocator:
         }
 
 
-def copy_page_tokens(src, dst, used: int) -> None:
-    """Copies the first `used` tokens of every head of src into dst.
+def copy_page_tokens(src, dst, used: int) -> bool:
+    """Copies the first `used` tokens of every head of src into dst; True when the copy was queued.
 
-    Store-backed pages copy slot to slot with one copy of the [2, Hkv, used, D]
-    block.  A device -> host copy is asynchronous into pinned memory; the host
-    store records an event and every CPU-side view waits for it, so a later
-    CPU read never sees the copy in flight (the hazard the reference avoids
-    with synchronous copies, kv_allocator.py:108-110)."""
+    A device -> pinned-host copy between store-backed pages is queued on the host store
+    (PageStore.defer_move) and issued with the other queued evictions as one batched launch on the
+    device's transfer stream; every CPU-side view, host slab growth and staging copy of the host
+    store flushes and waits first, so a later read never sees the copy in flight (the hazard the
+    reference avoids with synchronous copies, kv_allocator.py:108-110).  The whole slot is moved:
+    tokens past `used` are never read.  Other store-backed pairs copy the [2, Hkv, used, D] block
+    slot to slot."""
     if src.has_store() and dst.has_store():
         s_st, d_st = src.store, dst.store
+        if d_st.pinned and s_st.device.type == "cuda" and s_st.page_bytes == d_st.page_bytes:
+            d_st.defer_move(s_st, src.slot, dst.slot)
+            return True
+        s_st.sync_host()   # a host source may still be receiving its own queued copy
         s_blk = s_st.slab[src.slot, :, :, :used]
         d_blk = d_st.slab[dst.slot, :, :, :used]
-        async_ok = d_st.pinned and s_st.device.type == "cuda"
-        d_blk.copy_(s_blk, non_blocking=async_ok)
-        if async_ok:
-            ev = torch.cuda.Event()
-            ev.record(torch.cuda.current_stream(s_st.device))
-            d_st.pending_event = ev
-        return
+        d_blk.copy_(s_blk)
+        return False
     dst.k_tensor[:, :, :used, :].copy_(src.k_tensor[:, :, :used, :])
     dst.v_tensor[:, :, :used, :].copy_(src.v_tensor[:, :, :used, :])
+    return False

@@ -148,6 +148,7 @@ class KVCacheManager:
         self._rank: dict = {}            # layer id -> position among self.layers' keys
         self._tie = itertools.count()
         self._n_evictable = 0            # live entries of the heap
+        self._prefill_writes = None      # the append_prefill chunks not yet written (during the call)
 
     def _page_bytes(self) -> int:
         a = self.allocator
@@ -182,21 +183,26 @@ class KVCacheManager:
         page_size = self.allocator.page_size
         device = K_prefill.device
         pending = _PrefillWrites(K_prefill, V_prefill)
-        for start_idx in range(0, seq_len, page_size):
-            chunk_len = min(page_size, seq_len - start_idx)
-            page = self.allocator.allocate(device)
-            page.layer_id = layer_id
-            page.start_token = layer.total_tokens
-            page.used_tokens = chunk_len
-            pending.add(page, start_idx, chunk_len)
-            self._append_page(layer, page)
-            layer._version += 1
-            layer.total_tokens += chunk_len
-            # An eviction copies pages out: their data must be written first.
-            if self._gpu_evictable_bytes() > self.gpu_high_watermark_bytes:
-                pending.flush()
-            self._enforce_residency_policy()
-        pending.flush()
+        self._prefill_writes = pending    # an eviction of a page still in it writes it first
+        try:
+            for start_idx in range(0, seq_len, page_size):
+                chunk_len = min(page_size, seq_len - start_idx)
+                page = self.allocator.allocate(device)
+                page.layer_id = layer_id
+                page.start_token = layer.total_tokens
+                page.used_tokens = chunk_len
+                pending.add(page, start_idx, chunk_len)
+                self._append_page(layer, page)
+                layer._version += 1
+                layer.total_tokens += chunk_len
+                self._enforce_residency_policy()
+            pending.flush()
+        finally:
+            self._prefill_writes = None
+        # the evictions of this call leave as batched copies on the transfer stream
+        flush = getattr(self.allocator, "flush_migrations", None)
+        if flush is not None:
+            flush()
 
     def append_decode(self, layer_id: int, K_new: torch.Tensor, V_new: torch.Tensor,
                       skip_residency: bool = False):
@@ -265,6 +271,9 @@ class KVCacheManager:
             if not self._live(entry):
                 continue
             _, _, idx, _, layer, page = entry
+            pw = self._prefill_writes
+            if pw is not None and pw.holds(page):
+                pw.flush()                # the page's data must be written before it is copied out
             original_start_token = page.start_token
             new_page = self.allocator.move_page(page, torch.device("cpu"))
             assert new_page.start_token == original_start_token, "Page invariant broken during migration"
@@ -410,12 +419,18 @@ class _PrefillWrites:
     def __init__(self, K: torch.Tensor, V: torch.Tensor):
         self.K, self.V = K, V
         self.items = []   # (page, start token in K, tokens)
+        self.ids = set()
 
     def add(self, page, start: int, n: int) -> None:
         self.items.append((page, start, n))
+        self.ids.add(id(page))
+
+    def holds(self, page) -> bool:
+        return id(page) in self.ids
 
     def flush(self) -> None:
         items, self.items = self.items, []
+        self.ids = set()
         i = 0
         while i < len(items):
             page, start, n = items[i]

@@ -12,12 +12,37 @@ request exceeds its capacity (slot indices stay valid; tensors handed out as
 page views before a growth keep pointing at the old storage, which is why
 KVPage materialises its views lazily).  Large pools should be sized up front
 with reserve().
+
+Evictions (device -> pinned host) are batched: KVAllocator.move_page queues
+the page copy on the host store (defer_move) instead of copying it, and
+flush_moves() issues every queued copy as one helm_move_pages launch on the
+device's transfer stream, ordered after the work already queued on the
+current stream.  Until their copy has completed, the source slots stay out of
+the free list (quarantine) and the host slab's readers wait for its events
+(pending_events): a CPU-side view, a host slab growth and a staging copy all
+flush and wait first.
 """
 from __future__ import annotations
 
 from typing import List, Optional
 
 import torch
+
+_TRANSFER_STREAMS = {}
+
+# Queued migrations flushed as soon as this many are pending (one kernel launch carries 2048).
+MAX_PENDING_MOVES = 2048
+
+
+def transfer_stream(device) -> "torch.cuda.Stream":
+    """The side stream of `device` that carries page migrations and host-page staging copies
+    (the reference's per-device copy stream, kv_cache.py:315)."""
+    dev = device_key(device)
+    st = _TRANSFER_STREAMS.get(dev)
+    if st is None:
+        st = torch.cuda.Stream(device=dev)
+        _TRANSFER_STREAMS[dev] = st
+    return st
 
 
 def device_key(device) -> torch.device:
@@ -40,7 +65,11 @@ class PageStore:
         self.next_slot = 0           # slots [0, next_slot) have been handed out at least once
         self.free_slots: List[int] = []
         self.growths = 0
-        self.pending_event = None    # event after which host pages written by D2H copies are valid
+        self.pending_events = []     # events after which host pages written by D2H copies are valid
+        self.pending_moves = []      # queued migrations into this store: (source store, source slot, slot)
+        self.quarantine = []         # (event, slots): sources of migrations still in flight
+        self.last_reader = None      # event after the last staging copy that read this (host) slab
+        self.outbound = {}           # host stores holding queued migrations out of this store
         if initial:
             self.reserve(initial)
 
@@ -74,6 +103,13 @@ class PageStore:
         """Makes room for `capacity` slots in total (no-op if already there)."""
         if capacity <= self.capacity:
             return
+        # The old slab is copied below and then dropped: a host slab must first receive every
+        # queued and in-flight migration (the copy runs on the CPU), and no staging copy may still
+        # be reading it when its pinned block goes back to the allocator.
+        self.sync_host()
+        if self.last_reader is not None:
+            self.last_reader.synchronize()
+            self.last_reader = None
         new = self._alloc(capacity)
         if self.slab is not None and self.next_slot > 0:
             new[:self.next_slot].copy_(self.slab[:self.next_slot])
@@ -86,6 +122,12 @@ class PageStore:
         out: List[int] = []
         while self.free_slots and len(out) < n:
             out.append(self.free_slots.pop())
+        if len(out) < n and (self.quarantine or self.outbound):
+            for dst in list(self.outbound.values()):
+                dst.flush_moves()            # queued migrations hold slots of this store
+            self._release_quarantine()
+            while self.free_slots and len(out) < n:
+                out.append(self.free_slots.pop())
         need = n - len(out)
         if need:
             if self.next_slot + need > self.capacity:
@@ -107,11 +149,56 @@ class PageStore:
         return self.slab[slot, 1].unsqueeze(0)
 
     def sync_host(self) -> None:
-        """Host slabs written by asynchronous D2H copies: wait for them before a CPU-side read."""
-        ev = self.pending_event
-        if ev is not None:
+        """Host slabs written by asynchronous D2H copies: issue the queued ones and wait for all of
+        them before a CPU-side read."""
+        self.flush_moves()
+        evs, self.pending_events = self.pending_events, []
+        for ev in evs:
             ev.synchronize()
-            self.pending_event = None
+
+    # ---- batched migrations ---------------------------------------------------------
+    def defer_move(self, src: "PageStore", src_slot: int, dst_slot: int) -> None:
+        """Queues the copy of slot src_slot of `src` (a device store) into slot dst_slot of this
+        (host) store.  The source slot is held until the copy has run, then quarantined."""
+        self.pending_moves.append((src, src_slot, dst_slot))
+        src.outbound[id(self)] = self
+        if len(self.pending_moves) >= MAX_PENDING_MOVES:
+            self.flush_moves()
+
+    def flush_moves(self) -> None:
+        """Issues every queued migration: per source store, one helm_move_pages on that device's
+        transfer stream after the work queued so far on its current stream; the event that ends
+        it guards this slab's readers and the source slots."""
+        moves, self.pending_moves = self.pending_moves, []
+        if not moves:
+            return
+        from .. import ops
+        self.pending_events = [e for e in self.pending_events if not e.query()]
+        groups = {}
+        for src, s_slot, d_slot in moves:
+            groups.setdefault(id(src), (src, [], []))
+            groups[id(src)][1].append(s_slot)
+            groups[id(src)][2].append(d_slot)
+        for src, s_slots, d_slots in groups.values():
+            dev = src.device
+            side = transfer_stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            ops.move_pages(self.slab, d_slots, src.slab, s_slots, self.page_bytes, stream=side.cuda_stream)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            src.slab.record_stream(side)     # a reallocation of the source slab waits for these reads
+            self.pending_events.append(ev)
+            src.quarantine.append((ev, s_slots))
+            src.outbound.pop(id(self), None)
+
+    def _release_quarantine(self) -> None:
+        """Returns migrated-out slots to the free list; the current stream waits (on the device, not
+        the host) for the copies that read them, so any later write to them comes after."""
+        q, self.quarantine = self.quarantine, []
+        cur = torch.cuda.current_stream(self.device)
+        for ev, slots in q:
+            cur.wait_event(ev)
+            self.free_slots.extend(slots)
 
     def base_ptrs(self):
         """(k_base, v_base) views whose data_ptr()s are the kernel's pool bases."""

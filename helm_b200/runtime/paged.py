@@ -21,7 +21,7 @@ import numpy as np
 import torch
 
 from .. import ops
-from .page_store import PageStore
+from .page_store import PageStore, transfer_stream
 
 
 def _is_cuda(device) -> bool:
@@ -46,6 +46,7 @@ class Staging:
         self.stream = None
         self.ready = [None, None]
         self.done = [None, None]             # consumer-side events: the half's last reader finished
+        self.slab_seen = None                # the device slab the side stream last wrote into
 
     def _reserve(self, r: int, n: int) -> bool:
         """Makes half r hold >= n slots; True when the slab had to grow (a reallocation copy on
@@ -77,7 +78,7 @@ class Staging:
         enqueueing the kernel that reads them."""
         r = self.turn
         self.turn ^= 1
-        grew = self._reserve(r, len(host_slots))
+        self._reserve(r, len(host_slots))
         start = self.ranges[r][0]
         if not host_slots:
             return start
@@ -86,19 +87,26 @@ class Staging:
         dev = self.store.device
         cur = torch.cuda.current_stream(dev)
         if self.stream is None:
-            self.stream = torch.cuda.Stream(device=dev)
+            self.stream = transfer_stream(dev)
             self.ready = [torch.cuda.Event(), torch.cuda.Event()]
         side = self.stream
-        if grew:
-            side.wait_stream(cur)             # the slab was reallocated (copied) on this stream
-        elif self.done[r] is not None:
+        # Evictions queued into the host store must be issued before their pages are read.
+        host_store.flush_moves()
+        slab = self.store.slab
+        if slab is not self.slab_seen or self.done[r] is None:
+            # The device slab is new to the side stream (first use, or reallocated by a growth
+            # anywhere: its old -> new copy sits on the consumer stream), or this half has no
+            # reader event yet: wait for everything queued so far.
+            side.wait_stream(cur)
+            slab.record_stream(side)
+            self.slab_seen = slab
+        else:
             side.wait_event(self.done[r])     # the half's previous reader has finished
-        pend = host_store.pending_event
-        if pend is not None:
-            side.wait_event(pend)             # pages evicted just now: their D2H copies
-        ops.copy_pages(self.store.slab, start, host_store.slab, host_slots, self.store.page_bytes,
-                       stream=side.cuda_stream)
+        for ev in host_store.pending_events:
+            side.wait_event(ev)               # pages evicted just now: their D2H copies
+        ops.copy_pages(slab, start, host_store.slab, host_slots, self.store.page_bytes, stream=side.cuda_stream)
         self.ready[r].record(side)
+        host_store.last_reader = self.ready[r]
         cur.wait_event(self.ready[r])
         self._last = r
         return start

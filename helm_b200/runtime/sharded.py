@@ -37,7 +37,11 @@ def shard_bounds(n: int, rank: int, world: int) -> Tuple[int, int]:
 
 
 class KVShardGroup:
-    def __init__(self, rows: int, head_dim: int, device, group=None, exchange: str = "fused"):
+    def __init__(self, rows: int, head_dim: int, device, group=None, exchange: str = "fused",
+                 wait_s: float = 0.0):
+        """rows = B*Hq records of head_dim dims per exchange.  wait_s bounds each device-side wait
+        for the peers' records (0: the library default, 2 s); a wait that runs out sets
+        HELM_DEVERR_TIMEOUT in the error word and leaves the affected rows zero."""
         import torch.distributed as dist
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -105,6 +109,7 @@ class KVShardGroup:
         p.flags_local = self.buf.data_ptr() + rb.value
         p.counters = self.counters.data_ptr()
         p.error_flag = self.error_flag.data_ptr()
+        p.wait_ns = x.wait_ns = int(wait_s * 1e9)
         x.recv_local = self.xbuf.data_ptr()
         x.counters = self.xcounters.data_ptr()
         self.params = p

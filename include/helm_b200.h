@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define HELM_ABI_VERSION 2
+#define HELM_ABI_VERSION 3
 #define HELM_MAX_RANKS 8
 
 /* ---- status codes ------------------------------------------------------- */
@@ -81,20 +81,30 @@ const char *helm_last_error(void);
  * query head: float rec[D+2] = { o[0..D-1], m, l }, where m is the running
  * max of the base-2 logits s*scale*log2(e), l = sum 2^(logit-m) and o the
  * unnormalised sum of 2^(logit-m) * v.  An empty range has m = -inf, l = 0,
- * o = 0.  Records are stored [split][B*Hq][D+2] in `workspace`.
+ * o = 0.  Records are stored [split][B*Hq][D+2] in `workspace`, after its
+ * header (below).
  *
  * Output.  When `out` is non-null the records are merged (helm_lse_merge
  * semantics) into out [B, Hq, D] of out_dtype; when `out_record` is non-null
  * the merged but unnormalised record [B*Hq][D+2] is also written, for a later
  * cross-GPU merge.  With num_splits == 1 and only `out` requested, no
  * workspace is touched.
+ *
+ * Workspace.  Its first HELM_WORKSPACE_HEADER_BYTES hold a call token and
+ * arrival counters of the single-launch (persistent) path, tagged with the
+ * token so that no call needs them zeroed: a fresh workspace, or one whose
+ * counters a timed-out call left behind, is valid as it is.  The split
+ * records follow the header.  The kernels are launched with programmatic
+ * dependent launch and read the workspace only after the previous kernel on
+ * the stream has finished, so consecutive calls may share one workspace.
  */
+#define HELM_WORKSPACE_HEADER_BYTES 256
 /* Cross-GPU exchange fused into helm_paged_attn_decode (KV sequence sharding).
  * With params.exchange set, each rank's pages are its share of every sequence:
  * the CTA that completes a (sequence, kv head) pair's rank-local merge stores
  * the pair's record into every other rank's receive slot over NVLink (CUDA IPC
  * mappings) as 64-bit words (value | epoch << 32, so no fence or flag is
- * needed), waits (bounded, 2 s) for the other ranks' words of that pair and
+ * needed), waits (bounded by wait_ns, default 2 s) for the other ranks' words of that pair and
  * merges the records in rank order, so `out` / `out_record` hold the
  * attention over the whole sequence on every rank, bit-identical across ranks.
  * Buffers: per rank one receive buffer of helm_shard_exchange_bytes()
@@ -111,6 +121,7 @@ typedef struct {
   float *recv_local;                     /* == peer_recv[rank] */
   uint32_t *flags_local;                 /* unused; may be null */
   uint32_t *counters;                    /* local */
+  uint64_t wait_ns;                      /* bound of each wait for peers; 0 = 2 s */
 } helm_shard_exchange;
 
 /* Sizes for rows = B*Hq records of D dims: receive slots, flags (0), local counters. */
@@ -161,8 +172,9 @@ int helm_paged_attn_decode(const helm_paged_attn_params *p, void *stream);
  * array of HELM_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds
  * until the process exits.  Nothing is allocated or freed.  With
  * num_splits == 0 the split count is capped to what the array holds; an
- * explicit num_splits whose records (num_splits * B*Hq*(D+2)*4 bytes) exceed
- * it is rejected with HELM_ERR_WORKSPACE.
+ * explicit num_splits whose records (num_splits * B*Hq*(D+2)*4 bytes, after
+ * the HELM_WORKSPACE_HEADER_BYTES header) exceed it is rejected with
+ * HELM_ERR_WORKSPACE.
  *
  * The first call on a device looks up the array's device address (with that
  * device current) and so should come before any stream capture.  All calls in
@@ -317,8 +329,8 @@ int helm_rmsnorm(const void *x, int32_t x_dtype, int64_t x_stride, const void *w
  * r's buffer parts as mapped in this process (this rank's own entries are its
  * local pointers).  `counters` (counters_bytes, zeroed once) stays local.
  * Every rank must make the same sequence of calls with the same rows and D.
- * Waits for peers are bounded (2 s); a wait that gives up sets
- * HELM_DEVERR_TIMEOUT in error_flag and leaves zeros in the affected rows.
+ * Waits for peers are bounded (wait_ns, default 2 s); a wait that gives up
+ * sets HELM_DEVERR_TIMEOUT in error_flag and leaves zeros in the affected rows.
  */
 typedef struct {
   int32_t rank, world, rows, D;
@@ -332,6 +344,7 @@ typedef struct {
   int32_t out_dtype;
   float *out_record;                    /* [rows, D+2] or null */
   int32_t *error_flag;
+  uint64_t wait_ns;                     /* bound of each wait for peers; 0 = 2 s */
 } helm_gather_merge_params;
 
 int64_t helm_gather_merge_state_bytes(int32_t world, int32_t rows, int32_t D, int64_t *recv_bytes_out,
@@ -361,6 +374,25 @@ int helm_ipc_close(void *base);
 int helm_copy_pages(void *dst_base, int64_t dst_first, const void *src_base,
                     const int32_t *src_ids, int32_t count, int64_t page_bytes,
                     int32_t *copies_out, void *stream);
+
+/* ---- batched page migration (eviction copies) ----------------------------- */
+/*
+ * Replaces the per-page synchronous copies of KVAllocator.move_page
+ * (helm/runtime/kv_allocator.py:104-116) for a whole batch of evictions:
+ * copies `count` pages of page_bytes bytes, src_base + src_ids[i]*page_bytes ->
+ * dst_base + dst_ids[i]*page_bytes, on `stream`.  src_ids / dst_ids are HOST
+ * arrays; every id must lie in [0, src_pages) / [0, dst_pages) (the slabs'
+ * page capacities), else HELM_ERR_INVALID_ARGUMENT and nothing is copied.
+ * When the pairs form many runs and both slabs are device-addressable (device
+ * memory, or pinned host memory mapped for the device), one kernel moves every
+ * page (16-byte loads and stores); otherwise runs consecutive in both lists
+ * are copied with one cudaMemcpyAsync each.  *copies_out receives the number
+ * of launches / copies issued.
+ */
+int helm_move_pages(void *dst_base, const int32_t *dst_ids, const void *src_base,
+                    const int32_t *src_ids, int32_t count, int64_t page_bytes,
+                    int64_t dst_pages, int64_t src_pages, int32_t *copies_out,
+                    void *stream);
 
 #ifdef __cplusplus
 }

@@ -21,8 +21,10 @@ import sysconfig
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF_ROOT = pathlib.Path(os.environ.get("HELM_REFERENCE_ROOT", "/root/reference"))
-REF_SRC = REF_ROOT / "helm" / "kernels" / "fp16_gemv.cpp"
+# Root of the HELM checkout whose fp16_gemv.cpp is compiled; required to (re)build the module.
+_ROOT_ENV = os.environ.get("HELM_REFERENCE_ROOT")
+REF_ROOT = pathlib.Path(_ROOT_ENV) if _ROOT_ENV else None
+REF_SRC = REF_ROOT / "helm" / "kernels" / "fp16_gemv.cpp" if REF_ROOT else None
 MODULE = "helm_fp16_gemv_ref"
 
 
@@ -36,8 +38,13 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path | None:
     target = module_path()
     if target.exists() and not force:
         return target
-    if not REF_SRC.exists():
-        return target if target.exists() else None
+    if REF_SRC is None or not REF_SRC.exists():
+        if target.exists():
+            return target
+        why = ("HELM_REFERENCE_ROOT is not set" if REF_SRC is None
+               else f"{REF_SRC} not found")
+        print(f"[oracle] reference GEMV not built: {why}", file=sys.stderr)
+        return None
     import torch.utils.cpp_extension as ce
     OUT.mkdir(exist_ok=True)
     cxx = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"

@@ -34,7 +34,10 @@ import torch
 
 HERE = pathlib.Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = pathlib.Path(os.environ.get("HELM_REFERENCE_ROOT", "/root/reference"))
+if not os.environ.get("HELM_REFERENCE_ROOT"):
+    raise SystemExit("make_golden.py: set HELM_REFERENCE_ROOT to the root of a HELM checkout (the directory "
+                     "that contains helm/runtime/kv_cache.py)")
+REF = pathlib.Path(os.environ["HELM_REFERENCE_ROOT"])
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(REPO))
 

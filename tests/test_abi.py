@@ -111,3 +111,16 @@ def test_ctypes_layouts_match_the_compiled_header(tmp_path):
         assert got[(cname, "size")] == ctypes.sizeof(cls), cname
         for fname, _ in cls._fields_:
             assert got[(cname, fname)] == getattr(cls, fname).offset, f"{cname}.{fname}"
+
+
+def test_move_pages_checks_ids_before_touching_memory():
+    """helm_move_pages rejects ids outside the slabs' page counts on the host, before any copy."""
+    lib = N.lib()
+    src_ids = (ctypes.c_int32 * 2)(0, 5)
+    dst_ids = (ctypes.c_int32 * 2)(0, 1)
+    n = ctypes.c_int32(-1)
+    code = lib.helm_move_pages(ctypes.c_void_p(16), dst_ids, ctypes.c_void_p(16), src_ids, 2, 4096, 4, 5,
+                               ctypes.byref(n), None)
+    assert code == N.ERR_INVALID_ARGUMENT
+    assert b"source page 5" in lib.helm_last_error()
+    assert n.value == 0

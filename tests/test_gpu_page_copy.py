@@ -46,3 +46,52 @@ def test_runs_and_device_source():
     torch.cuda.synchronize()
     assert torch.equal(dst[:15].cpu(), src[ids])
     assert torch.equal(dst[15:35].cpu(), src[ids2])
+
+
+@pytest.mark.parametrize("direction", ["d2h", "h2d", "d2d"])
+def test_move_pages_scatter_gather(direction):
+    """helm_move_pages: (source slot, destination slot) pairs in any order, one kernel for many runs,
+    bytewise equal to torch indexing; destination slots not named stay untouched."""
+    from helm_b200 import ops
+    host = _pages(96, (2, 2, 64, 128), True)
+    page_bytes = host[0].numel() * 2
+    g = torch.Generator().manual_seed(5)
+    src_ids = torch.randperm(96, generator=g)[:70].tolist()
+    dst_ids = torch.randperm(80, generator=g)[:70].tolist()
+    if direction == "d2h":
+        src = host.to(DEV)
+        dst = torch.zeros((80,) + host.shape[1:], dtype=host.dtype).pin_memory()
+    elif direction == "h2d":
+        src = host
+        dst = torch.zeros((80,) + host.shape[1:], dtype=host.dtype, device=DEV)
+    else:
+        src = host.to(DEV)
+        dst = torch.zeros((80,) + host.shape[1:], dtype=host.dtype, device=DEV)
+    n = ops.move_pages(dst, dst_ids, src, src_ids, page_bytes)
+    torch.cuda.synchronize()
+    assert n == 1
+    want = torch.zeros((80,) + host.shape[1:], dtype=host.dtype)
+    want[dst_ids] = host[src_ids]
+    assert torch.equal(dst.cpu(), want)
+
+
+def test_move_pages_runs_use_copies():
+    from helm_b200 import ops
+    host = _pages(32, (2, 2, 64, 128), True)
+    page_bytes = host[0].numel() * 2
+    src = host.to(DEV)
+    dst = torch.zeros((40,) + host.shape[1:], dtype=host.dtype).pin_memory()
+    assert ops.move_pages(dst, list(range(5, 15)) + [30, 31], src, list(range(0, 10)) + [20, 21], page_bytes) == 2
+    torch.cuda.synchronize()
+    assert torch.equal(dst[5:15], host[0:10]) and torch.equal(dst[30:32], host[20:22])
+
+
+def test_move_pages_rejects_out_of_range_ids():
+    from helm_b200 import ops
+    from helm_b200 import _native as N
+    src = torch.zeros((8, 2, 2, 64, 128), dtype=torch.bfloat16, device=DEV)
+    dst = torch.zeros((4, 2, 2, 64, 128), dtype=torch.bfloat16).pin_memory()
+    with pytest.raises(N.HelmError):
+        ops.move_pages(dst, [0, 4], src, [1, 2], src[0].numel() * 2)
+    with pytest.raises(ValueError):
+        ops.copy_pages(src, 7, dst, [0, 1], src[0].numel() * 2)

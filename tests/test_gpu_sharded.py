@@ -1,6 +1,7 @@
-"""KV sequence sharding on 2 GPUs: the P2P record exchange (helm_gather_merge over CUDA IPC) and
-the NCCL exchange, against the single-GPU attention over the whole sequence.  Spawns its own two
-ranks; skipped with fewer than 2 GPUs."""
+"""KV sequence sharding on 2, 4 and 8 GPUs: the exchange fused into the attention kernel, the P2P
+record exchange (helm_gather_merge over CUDA IPC) and the NCCL exchange, against the single-GPU
+attention over the whole sequence, with bit-identical outputs on every rank.  Spawns its own ranks;
+each world size is skipped when the box has fewer GPUs."""
 import math
 import os
 import socket
@@ -89,20 +90,21 @@ def _worker(rank, world, port, exchange, result_q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("exchange", ["fused", "p2p", "nccl"])
-def test_two_gpu_exchange_matches_single_gpu(exchange):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_sharded_exchange_matches_single_gpu(exchange, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, exchange, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=240)
-    results = sorted(q.get(timeout=5) for _ in range(2))
+    results = sorted(q.get(timeout=5) for _ in range(world))
     for p in procs:
         assert p.exitcode == 0
     for rank, err, flag in results:

@@ -77,3 +77,33 @@ def test_noalloc_rejects_too_many_explicit_splits(cuda):
     code = _noalloc_fn()(ctypes.byref(p), torch.cuda.current_stream(cuda).cuda_stream)
     assert code == N.ERR_WORKSPACE
     assert b"static scratch" in N.lib().helm_last_error()
+
+
+def test_noalloc_caps_the_automatic_split_count(cuda):
+    """num_splits = 0 on a call whose automatic split count needs more records than the static
+    array holds: the entry point lowers the split count to what fits, and its result equals the
+    workspace entry point's with that same split count, bit for bit, on two calls in a row."""
+    from helm_b200 import ops
+    from helm_b200 import _native as N
+    B, Hq, Hkv, npages = 1, 64, 1, 300          # GQA group 64: the split path
+    q, kp, vp, pt, pu, npg, total = _inputs(cuda, B, Hq, Hkv, npages, seed=29)
+    common = dict(num_kv_heads=Hkv, page_size=64, page_stride=Hkv * 64 * 128, head_stride=64 * 128,
+                  num_pool_pages=total)
+    probe = ops.make_attn_params(q, kp, vp, pt, pu, npg, out=torch.empty(B, Hq, 128, device=cuda), num_splits=0,
+                                 **common)
+    S = ctypes.c_int32(0)
+    N.lib().helm_paged_attn_workspace_bytes(ctypes.byref(probe), ctypes.byref(S))
+    per_split = B * Hq * (128 + 2) * 4
+    cap = (8 << 20) - 256                        # the array less the workspace header
+    if S.value * per_split <= cap:
+        pytest.skip(f"{S.value} automatic splits fit the static array on this GPU")
+    capped = cap // per_split
+    ref = ops.paged_decode_attention(q, kp, vp, pt, pu, npg, num_splits=capped, out_dtype=torch.float32, **common)
+    fn = _noalloc_fn()
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    for call in range(2):
+        out = torch.full((B, Hq, 128), float("nan"), dtype=torch.float32, device=cuda)
+        p = ops.make_attn_params(q, kp, vp, pt, pu, npg, out=out, num_splits=0, **common)
+        N.check("helm_paged_attn_decode_noalloc", fn(ctypes.byref(p), stream))
+        torch.cuda.synchronize(cuda)
+        assert torch.equal(out, ref), f"call {call}"
