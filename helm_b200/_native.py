@@ -16,9 +16,6 @@ LIB_PATH = pathlib.Path(os.environ.get(
 
 ABI_VERSION = 3
 
-# bytes at the start of an attention workspace reserved for the call token and arrival counters
-WORKSPACE_HEADER_BYTES = 256
-
 # helm_dtype
 F32, F16, BF16, I8 = 0, 1, 2, 3
 
@@ -108,6 +105,7 @@ SIGNATURES = [
     ("helm_paged_attn_decode", _c.c_int, [_c.POINTER(PagedAttnParams), _p]),
     ("helm_lse_merge", _c.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p]),
     ("helm_int8_linear", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
+    ("helm_int8_linear_glu", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
     ("helm_int8_linear_error", _c.c_int, [_p, _i32]),
     ("helm_kv_append", _c.c_int, [_c.POINTER(KVAppendParams), _p]),
     ("helm_decode_prologue", _c.c_int, [_c.POINTER(DecodePrologueParams), _p]),

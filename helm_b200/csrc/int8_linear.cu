@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
                                                             const __grid_constant__ CUtensorMap tmX,
                                                             const void *__restrict__ scale, int scale_dt,
                                                             const XT *__restrict__ bias, XT *__restrict__ y, int M,
-                                                            int N, int K, int ST, int XR, int xbox_bytes) {
+                                                            int N, int K, int ST, int XR, int xbox_bytes, int glu) {
   constexpr int kWBoxBytes = kBoxK * 16 * RT;
   constexpr int P = RT * MT * 128;  // floats of one warp's partial tile
   const int stage_bytes = (kCWarps * (kWBoxBytes + xbox_bytes) + 1023) & ~1023;
@@ -281,6 +281,36 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
   asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
   if (any_fail) return;  // a stage never arrived: leave the rows unwritten (error word set)
   asm volatile("griddepcontrol.wait;" ::: "memory");  // y may still be read by the previous kernel
+  if (glu) {
+    // Gated unit: row tiles 2u and 2u+1 of W hold the gate and the up rows of outputs 16u..16u+15;
+    // y[m, 16u + r] = silu(gate) * up, y [M, N/2].  The CTA owns whole tile pairs (RT even).
+    const int half = N >> 1;
+    for (int pos = threadIdx.x; pos < P; pos += kCWarps * 32) {
+      const int ln = pos & 31, e = (pos >> 5) & 3, tile = pos >> 7;
+      const int rt = tile / MT, nt = tile - rt * MT;
+      if (rt & 1) continue;
+      const int pos_up = pos + MT * 128;  // same (nt, e, lane) of tile rt + 1
+      float gv = 0.f, uv = 0.f;
+#pragma unroll
+      for (int wp = 0; wp < kCWarps; ++wp) {
+        gv += red[wp * P + pos];
+        uv += red[wp * P + pos_up];
+      }
+      const int row = (ln >> 2) + ((e & 2) ? 8 : 0), col = (ln & 3) * 2 + (e & 1);
+      const int ng = n_base + rt * 16 + row, nu = ng + 16, m = m_base + nt * 8 + col;
+      if (nu < N && m < M) {
+        gv *= load_f(scale, scale_dt, ng);
+        uv *= load_f(scale, scale_dt, nu);
+        if (bias) {
+          gv += Elem<XT>::to_f(bias[ng]);
+          uv += Elem<XT>::to_f(bias[nu]);
+        }
+        const float act = gv / (1.f + __expf(-gv));
+        y[(int64_t)m * half + (ng >> 5) * 16 + (ng & 15)] = Elem<XT>::from_f(act * uv);
+      }
+    }
+    return;
+  }
   for (int pos = threadIdx.x; pos < P; pos += kCWarps * 32) {
     float v = 0.f;
 #pragma unroll
@@ -383,7 +413,7 @@ bool act_map(CUtensorMap *m, const void *x, int xdt, int M, int K, int rows) {
 
 template <typename XT, int RT, int MT>
 int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y,
-               int M, int N, int K, cudaStream_t st) {
+               int M, int N, int K, cudaStream_t st, int glu) {
   const int XR = M < 8 * MT ? M : 8 * MT;                          // x rows per box
   const int xbox_bytes = ((kBoxK * XR * (int)sizeof(XT)) + 127) & ~127;   // 128-byte aligned x boxes
   const int stage_bytes = (kCWarps * (kBoxK * 16 * RT + xbox_bytes) + 1023) & ~1023;
@@ -421,7 +451,7 @@ int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, xmap, scale, sdt, static_cast<const XT *>(bias),
-                                           static_cast<XT *>(y), M, N, K, ST, XR, xbox_bytes);
+                                           static_cast<XT *>(y), M, N, K, ST, XR, xbox_bytes, glu);
   if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_linear: launch: %s", cudaGetErrorString(e));
   return check_launch("int8_tma_kernel");
 }
@@ -430,26 +460,49 @@ int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int s
 // at once -- 3 CTAs per SM with one tile (64 KB ring), 2 with more (96 KB ring).
 template <typename XT, int MT>
 int launch_m(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
-             int K, cudaStream_t st) {
+             int K, cudaStream_t st, int glu) {
   const int sms = num_sms();
   const int tiles = (N + 15) / 16;
+  if (glu) {  // whole (gate, up) tile pairs per CTA
+    if constexpr (MT >= 4) {
+      return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1);
+    } else {
+      if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1);
+      return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1);
+    }
+  }
   if constexpr (MT >= 4) {  // wide x tiles: one row tile per CTA (register budget)
-    return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+    return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
   } else {
-    if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
-    if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
-    if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
-    return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+    if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
+    if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
+    if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
+    return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
   }
 }
 
 template <typename XT>
 int launch(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
-           int K, cudaStream_t st) {
-  if (M <= 8) return launch_m<XT, 1>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
-  if (M <= 16) return launch_m<XT, 2>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
-  if (M <= 32) return launch_m<XT, 4>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
-  return launch_m<XT, 8>(x, xdt, w, scale, sdt, bias, y, M, N, K, st);
+           int K, cudaStream_t st, int glu) {
+  if (M <= 8) return launch_m<XT, 1>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
+  if (M <= 16) return launch_m<XT, 2>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
+  if (M <= 32) return launch_m<XT, 4>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
+  return launch_m<XT, 8>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
+}
+
+int check_args(const void *x, int32_t x_dtype, const int8_t *w, const void *w_scale, int32_t scale_dtype, void *y,
+               int32_t M, int32_t N, int32_t K, const char *what) {
+  if (M < 0 || N < 0 || K <= 0) return fail(HELM_ERR_INVALID_ARGUMENT, "%s: bad sizes M=%d N=%d K=%d", what, M, N, K);
+  if (K % 16) return fail(HELM_ERR_UNSUPPORTED, "%s: K=%d is not a multiple of 16", what, K);
+  if (x_dtype != HELM_F16 && x_dtype != HELM_BF16) return fail(HELM_ERR_UNSUPPORTED, "%s: x dtype %d", what, x_dtype);
+  if (scale_dtype != HELM_F16 && scale_dtype != HELM_BF16 && scale_dtype != HELM_F32)
+    return fail(HELM_ERR_UNSUPPORTED, "%s: scale dtype %d", what, scale_dtype);
+  if (M == 0 || N == 0) return HELM_OK;
+  if (!x || !w || !w_scale || !y) return fail(HELM_ERR_INVALID_ARGUMENT, "%s: null pointer", what);
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)
+    return fail(HELM_ERR_INVALID_ARGUMENT, "%s: x and w must be 16-byte aligned", what);
+  if ((int64_t)M > 65535ll * 8) return fail(HELM_ERR_UNSUPPORTED, "%s: M=%d too large", what, M);
+  return HELM_OK;
 }
 
 }  // namespace
@@ -459,19 +512,23 @@ extern "C" int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
                                 int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t N, int32_t K,
                                 void *stream) {
   using namespace helm;
-  if (M < 0 || N < 0 || K <= 0) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear: bad sizes M=%d N=%d K=%d", M, N, K);
-  if (K % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_linear: K=%d is not a multiple of 16", K);
-  if (x_dtype != HELM_F16 && x_dtype != HELM_BF16) return fail(HELM_ERR_UNSUPPORTED, "int8_linear: x dtype %d", x_dtype);
-  if (scale_dtype != HELM_F16 && scale_dtype != HELM_BF16 && scale_dtype != HELM_F32)
-    return fail(HELM_ERR_UNSUPPORTED, "int8_linear: scale dtype %d", scale_dtype);
-  if (M == 0 || N == 0) return HELM_OK;
-  if (!x || !w || !w_scale || !y) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear: null pointer");
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15)
-    return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear: x and w must be 16-byte aligned");
-  if ((int64_t)M > 65535ll * 8) return fail(HELM_ERR_UNSUPPORTED, "int8_linear: M=%d too large", M);
+  const int rc = check_args(x, x_dtype, w, w_scale, scale_dtype, y, M, N, K, "int8_linear");
+  if (rc != HELM_OK || M == 0 || N == 0) return rc;
   cudaStream_t st = as_stream(stream);
-  return x_dtype == HELM_F16 ? launch<__half>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, N, K, st)
-                             : launch<__nv_bfloat16>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, N, K, st);
+  return x_dtype == HELM_F16 ? launch<__half>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, N, K, st, 0)
+                             : launch<__nv_bfloat16>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, N, K, st, 0);
+}
+
+extern "C" int helm_int8_linear_glu(const void *x, int32_t x_dtype, const int8_t *w, const void *w_scale,
+                                    int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t I, int32_t K,
+                                    void *stream) {
+  using namespace helm;
+  if (I < 0 || I % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_linear_glu: I=%d is not a multiple of 16", I);
+  const int rc = check_args(x, x_dtype, w, w_scale, scale_dtype, y, M, 2 * I, K, "int8_linear_glu");
+  if (rc != HELM_OK || M == 0 || I == 0) return rc;
+  cudaStream_t st = as_stream(stream);
+  return x_dtype == HELM_F16 ? launch<__half>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, 2 * I, K, st, 1)
+                             : launch<__nv_bfloat16>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, 2 * I, K, st, 1);
 }
 
 extern "C" int helm_int8_linear_error(int32_t *flag_out, int32_t reset) {

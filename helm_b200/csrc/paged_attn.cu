@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "tma.cuh"
 
+#include <atomic>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -238,6 +239,205 @@ __global__ void __launch_bounds__(128) attn_generic_kernel(AttnArgs a) {
       const float wt = rescale_weight(m_s[w * gq + h], M);
       L = fmaf(l_s[w * gq + h], wt, L);
       O = fmaf(o_s[(w * gq + h) * D + d], wt, O);
+    }
+    if (M == -INFINITY) { L = 0.f; O = 0.f; }
+    emit(a, s, b, g * gq + h, d, M, L, O);
+  }
+}
+
+// ===========================================================================
+// Warp-per-token-octet kernel (CUDA cores): fp32 pages, and 16-bit pages the
+// tensor-core kernels do not take, for D = 32*DPL (DPL 1..8) and GQA group <= 8.
+//
+// grid (S, Hkv, B), 256 threads.  Lane l owns dims [l*DPL, l*DPL + DPL) of
+// every row, so a K or V row is one coalesced 32*DPL-element load per warp.
+// The split's pages are cut into octets of 8 tokens; warp w takes octets w,
+// w+8, ... of each page.  Per octet a warp loads the 8 K and 8 V rows at once
+// (many loads in flight per warp), forms the 8 x GQ scores with a butterfly
+// sum over the lanes, and updates its running (m, l, o) with one rescale per
+// octet.  The eight warps' states are merged in shared memory at the end.
+// ===========================================================================
+constexpr int kWWarps = 8;
+constexpr int kOct = 8;
+
+template <typename KT, int DPL> struct RowLoad;
+template <int DPL> struct RowLoad<float, DPL> {
+  __device__ __forceinline__ static void run(const float *p, float (&v)[DPL]) {
+    if constexpr (DPL % 4 == 0) {
+#pragma unroll
+      for (int j = 0; j < DPL; j += 4) {
+        const float4 x = __ldg(reinterpret_cast<const float4 *>(p + j));
+        v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
+      }
+    } else if constexpr (DPL % 2 == 0) {
+#pragma unroll
+      for (int j = 0; j < DPL; j += 2) {
+        const float2 x = __ldg(reinterpret_cast<const float2 *>(p + j));
+        v[j] = x.x; v[j + 1] = x.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) v[j] = __ldg(p + j);
+    }
+  }
+};
+template <typename T16, int DPL> struct RowLoad16 {
+  __device__ __forceinline__ static void run(const T16 *p, float (&v)[DPL]) {
+    if constexpr (DPL % 8 == 0) {
+#pragma unroll
+      for (int j = 0; j < DPL; j += 8) {
+        const uint4 x = __ldg(reinterpret_cast<const uint4 *>(p + j));
+        const T16 *h = reinterpret_cast<const T16 *>(&x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[j + i] = Elem<T16>::to_f(h[i]);
+      }
+    } else if constexpr (DPL % 4 == 0) {
+#pragma unroll
+      for (int j = 0; j < DPL; j += 4) {
+        const uint2 x = __ldg(reinterpret_cast<const uint2 *>(p + j));
+        const T16 *h = reinterpret_cast<const T16 *>(&x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[j + i] = Elem<T16>::to_f(h[i]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < DPL; ++j) v[j] = Elem<T16>::to_f(p[j]);
+    }
+  }
+};
+template <int DPL> struct RowLoad<__half, DPL> : RowLoad16<__half, DPL> {};
+template <int DPL> struct RowLoad<__nv_bfloat16, DPL> : RowLoad16<__nv_bfloat16, DPL> {};
+
+size_t warp_smem_bytes(int GQ, int D) { return sizeof(float) * (size_t)kWWarps * GQ * (D + 2); }
+
+template <typename KT, int DPL, int GQ>
+__global__ void __launch_bounds__(kWWarps * 32) attn_warp_kernel(AttnArgs a) {
+  extern __shared__ float smem_w[];   // [warps][GQ][D] o, then [warps][GQ] m, [warps][GQ] l
+  constexpr int D = 32 * DPL;
+  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = a.gq;
+  float *o_s = smem_w;
+  float *m_s = o_s + kWWarps * GQ * D;
+  float *l_s = m_s + kWWarps * GQ;
+
+  pdl_trigger();
+  pdl_wait();
+
+  // q of the group, this lane's dims, pre-scaled into the base-2 logit domain.
+  float q[GQ][DPL];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h)
+#pragma unroll
+    for (int j = 0; j < DPL; ++j)
+      q[h][j] = h < gq ? load_f(a.q, a.q_dtype, ((int64_t)b * a.Hq + g * gq + h) * D + lane * DPL + j) * a.scale_log2
+                       : 0.f;
+  float m[GQ], l[GQ], o[GQ][DPL];
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) o[h][j] = 0.f;
+  }
+
+  const int n = read_num_pages(a, b);
+  int lo, hi;
+  split_range(n, s, a.num_splits, lo, hi);
+  const KT *kb = reinterpret_cast<const KT *>(a.k_base);
+  const KT *vb = reinterpret_cast<const KT *>(a.v_base);
+  for (int pi = lo; pi < hi; ++pi) {
+    const int pid = a.page_table[(int64_t)b * a.pt_stride + pi];
+    const int used = a.page_used[(int64_t)b * a.pt_stride + pi];
+    if (pid < 0 || pid >= a.num_pool_pages) {
+      if (lane == 0 && warp == 0) flag_error(a.error_flag, HELM_DEVERR_PAGE_ID);
+      continue;
+    }
+    if (used < 0 || used > a.P) {
+      if (lane == 0 && warp == 0) flag_error(a.error_flag, HELM_DEVERR_PAGE_USED);
+      continue;
+    }
+    const KT *kp = kb + (int64_t)pid * a.page_stride + (int64_t)g * a.head_stride + lane * DPL;
+    const KT *vp = vb + (int64_t)pid * a.page_stride + (int64_t)g * a.head_stride + lane * DPL;
+    for (int t0 = warp * kOct; t0 < used; t0 += kWWarps * kOct) {
+      const int nt = min(kOct, used - t0);
+      float kr[kOct][DPL], vr[kOct][DPL];
+#pragma unroll
+      for (int t = 0; t < kOct; ++t) {
+        if (t < nt) {
+          RowLoad<KT, DPL>::run(kp + (int64_t)(t0 + t) * D, kr[t]);
+          RowLoad<KT, DPL>::run(vp + (int64_t)(t0 + t) * D, vr[t]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) kr[t][j] = vr[t][j] = 0.f;
+        }
+      }
+      // scores: lane partials over its dims, summed over the warp (every lane gets every score)
+      float sc[GQ][kOct];
+#pragma unroll
+      for (int h = 0; h < GQ; ++h)
+#pragma unroll
+        for (int t = 0; t < kOct; ++t) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) acc = fmaf(q[h][j], kr[t][j], acc);
+          sc[h][t] = acc;
+        }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int h = 0; h < GQ; ++h)
+#pragma unroll
+          for (int t = 0; t < kOct; ++t) sc[h][t] += __shfl_xor_sync(0xffffffffu, sc[h][t], off);
+#pragma unroll
+      for (int h = 0; h < GQ; ++h) {
+        if (h >= gq) break;
+        float mx = m[h];
+#pragma unroll
+        for (int t = 0; t < kOct; ++t)
+          if (t < nt) mx = fmaxf(mx, sc[h][t]);
+        const float alpha = rescale_weight(m[h], mx);
+        m[h] = mx;
+        float ps = 0.f;
+        float acc[DPL];
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[j] = o[h][j] * alpha;
+#pragma unroll
+        for (int t = 0; t < kOct; ++t) {
+          const float p = t < nt ? fast_exp2(sc[h][t] - mx) : 0.f;
+          ps += p;
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) acc[j] = fmaf(p, vr[t][j], acc[j]);
+        }
+        l[h] = fmaf(l[h], alpha, ps);
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) o[h][j] = acc[j];
+      }
+    }
+  }
+
+  // merge the warps' states
+#pragma unroll
+  for (int h = 0; h < GQ; ++h) {
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) o_s[(warp * GQ + h) * D + lane * DPL + j] = o[h][j];
+    if (lane == 0) {
+      m_s[warp * GQ + h] = m[h];
+      l_s[warp * GQ + h] = l[h];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < gq * D; i += blockDim.x) {
+    const int h = i / D, d = i - h * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWWarps; ++w) M = fmaxf(M, m_s[w * GQ + h]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWWarps; ++w) {
+      const float wt = rescale_weight(m_s[w * GQ + h], M);
+      L = fmaf(l_s[w * GQ + h], wt, L);
+      O = fmaf(o_s[(w * GQ + h) * D + d], wt, O);
     }
     if (M == -INFINITY) { L = 0.f; O = 0.f; }
     emit(a, s, b, g * gq + h, d, M, L, O);
@@ -600,8 +800,7 @@ struct PersistArgs {
   float *rec_o;        // [C + pairs][gq][D]: CTA c's unnormalised o for pair p at slot c + p
   float *rec_ml;       // [C + pairs][gq][2]: its (m, l)
   uint64_t *counter;   // [pairs]: (call token << 32) | arrivals; a word with another token counts 0
-  uint32_t *token;     // workspace header: token of the last completed call
-  uint64_t *done;      // workspace header: (token << 32) | CTAs finished
+  uint32_t token;      // this call's token (host-issued; a captured graph replays its own)
   int C;               // grid size
   // Fused cross-GPU exchange (xworld > 1).  Receive slots of every rank: [2][G][B*Hq][D+2] words
   // of 64 bits, each one value (o[0..D), m, l) in the low half and the call's epoch in the high
@@ -667,7 +866,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   __shared__ float mg_M[HN], mg_L[HN], mg_A[HN];
   __shared__ int pending[kMaxPending];
   __shared__ int npending;
-  __shared__ uint32_t call_tok;
   __shared__ uint32_t xs_epoch;
   __shared__ int xs_dead;  // a wait of this CTA ran out: later exchanges do not wait again
   __shared__ uint64_t *xs_peer[HELM_MAX_RANKS];  // pa.xrecv (dynamic indexing of a kernel parameter array
@@ -696,7 +894,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   // kernel; page tables, q, the workspace and the outputs are touched only after it finished.
   pdl_trigger();
   pdl_wait();
-  if (tid == 0) call_tok = *reinterpret_cast<volatile uint32_t *>(pa.token) + 1u;
   // Units per sequence and their prefix sums (warp 0: chunked scan).
   if (warp == 0) {
     const int per = (B + 31) / 32;
@@ -1155,7 +1352,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int b = pair / Hkv, g = pair - b * Hkv;
           const int64_t up = seq_prefix[b] + (int64_t)g * seq_pages[b];
           const int c0 = owner_cta(up, U, C), c1 = owner_cta(up + seq_pages[b] - 1, U, C);
-          if (tagged_arrive(&pa.counter[pair], call_tok) == (uint32_t)(c1 - c0 + 1)) pending[npending++] = pair;
+          if (tagged_arrive(&pa.counter[pair], pa.token) == (uint32_t)(c1 - c0 + 1)) {
+            // the last arrival of this call: leave the word at (token, 0) for the next call, which
+            // starts after this grid has finished (a graph replay reuses the token)
+            pa.counter[pair] = (unsigned long long)pa.token << 32;
+            pending[npending++] = pair;
+          }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       } else if (nvalid > 0 && nvalid < 16) {
@@ -1262,15 +1464,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
     }
   }
-
-  // The last CTA to finish publishes this call's token: the next call (which starts reading the
-  // workspace only after this grid has finished) then treats every counter word of this call
-  // as stale, so no counter ever needs zeroing.
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    if (tagged_arrive(pa.done, call_tok) == gridDim.x) *reinterpret_cast<volatile uint32_t *>(pa.token) = call_tok;
-  }
 }
 
 }  // namespace tc
@@ -1284,6 +1477,8 @@ __global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict_
   const int row = blockIdx.x;
   const int rl = D + 2;
   const float *base = parts + (int64_t)row * rl;
+  pdl_trigger();
+  pdl_wait();
   float M = -INFINITY;
   for (int s = 0; s < S; ++s) M = fmaxf(M, base[s * pstride + D]);
   float L = 0.f;
@@ -1367,6 +1562,14 @@ bool encode_pool_map(CUtensorMap *m, const void *base, int kv_dtype, const helm_
   return r == CUDA_SUCCESS;
 }
 
+// Token of one persistent-kernel call: tags its arrival counters, so that words left by any other
+// call (or never written) count as zero and no counter has to be zeroed before a call.
+uint32_t next_call_token() {
+  static std::atomic<uint32_t> counter{0};
+  uint32_t t = counter.fetch_add(1u, std::memory_order_relaxed) + 1u;
+  return t ? t : counter.fetch_add(1u, std::memory_order_relaxed) + 1u;
+}
+
 // Debug switches, read on every call so that tests can flip them between calls (cheap: no
 // allocation, a short environment scan).
 bool env_flag(const char *name) {
@@ -1403,8 +1606,31 @@ bool tc_eligible(const helm_paged_attn_params *p) {
   return true;
 }
 
+// The warp-per-octet kernel: D in {64, 128, 256}, GQA group <= 8 (<= 4 at D = 256), and the
+// vector loads' alignment (a lane reads D/32 consecutive elements of a row).
+bool warp_eligible(const helm_paged_attn_params *p) {
+  if (env_flag("HELM_B200_FORCE_GENERIC")) return false;
+  if (p->D != 64 && p->D != 128 && p->D != 256) return false;
+  const int gq = p->Hq / p->Hkv;
+  const int dpl = p->D / 32;
+  int GQ = 1;
+  while (GQ < gq) GQ *= 2;
+  if (GQ > 8 || GQ * dpl > 32) return false;
+  const int es = dtype_size(p->kv_dtype);
+  int vb = es == 4 ? (dpl % 4 == 0 ? 16 : 8) : (dpl % 8 == 0 ? 16 : 8);
+  const uintptr_t kb = reinterpret_cast<uintptr_t>(p->k_base), vbp = reinterpret_cast<uintptr_t>(p->v_base);
+  return kb % vb == 0 && vbp % vb == 0 && (p->page_stride * es) % vb == 0 && (p->head_stride * es) % vb == 0;
+}
+
 int resolve_splits(const helm_paged_attn_params *p) {
   if (p->num_splits > 0) return p->num_splits;
+  if (!tc_eligible(p) && warp_eligible(p)) {
+    // about two CTAs of 8 warps per SM, every CTA with at least one page
+    const int pairs = p->B * p->Hkv;
+    if (pairs <= 0 || p->max_pages <= 1) return 1;
+    int S = (2 * num_sms() + pairs - 1) / pairs;
+    return S > p->max_pages ? p->max_pages : S;
+  }
   const int pairs = p->B * p->Hkv;
   const int maxp = p->max_pages;
   if (maxp <= 1 || pairs <= 0) return 1;
@@ -1442,9 +1668,8 @@ Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
   if (Cp < 1) Cp = 1;
   // a CTA covers at most units_max/C + 1 units, hence at most that many + 1 pairs
   const bool pending_ok = pairs_all <= tc::kMaxPending || units_max / Cp + 2 <= tc::kMaxPending;
-  // Workspace layout: the header (call token at byte 0, finished-CTA word at byte 8), then the
-  // CTA records (persistent path) or the split records (split path).
-  constexpr int64_t H = HELM_WORKSPACE_HEADER_BYTES;
+  // Workspace layout: the CTA records then the tagged arrival counters (persistent path), or the
+  // split records (split path).
   if (p->num_splits == 0 && eligible && p->B <= tc::kMaxSeqs && pending_ok && units_max < (1ll << 31) &&
       !env_flag("HELM_B200_NO_PERSISTENT")) {
     pl.persistent = true;
@@ -1453,13 +1678,13 @@ Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
     const int gq = p->Hq / p->Hkv;
     const int64_t slots = pl.C + (int64_t)pairs;
     pl.rec_bytes = slots * gq * p->D * (int64_t)sizeof(float);                 // o
-    pl.ml_off = H + (pl.rec_bytes + 255) / 256 * 256;
+    pl.ml_off = (pl.rec_bytes + 255) / 256 * 256;
     pl.counter_off = (pl.ml_off + slots * gq * 2 * (int64_t)sizeof(float) + 255) / 256 * 256;
     pl.bytes = pl.counter_off + (int64_t)pairs * sizeof(uint64_t);
     return pl;
   }
   pl.S = resolve_splits(p);
-  pl.bytes = pl.S > 1 ? H + (int64_t)pl.S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
+  pl.bytes = pl.S > 1 ? (int64_t)pl.S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
   return pl;
 }
 
@@ -1518,6 +1743,34 @@ int launch_generic(const AttnArgs &a, cudaStream_t st) {
   dim3 grid(a.num_splits, a.Hkv, a.B);
   attn_generic_kernel<KT><<<grid, 128, smem, st>>>(a);
   return check_launch("attn_generic_kernel");
+}
+
+template <typename KT, int DPL, int GQ>
+int launch_warp_cfg(const AttnArgs &a, cudaStream_t st) {
+  const size_t smem = warp_smem_bytes(GQ, 32 * DPL);
+  ensure_smem_attr(attn_warp_kernel<KT, DPL, GQ>, (int)smem);
+  const cudaError_t e = launch_pdl(attn_warp_kernel<KT, DPL, GQ>, dim3(a.num_splits, a.Hkv, a.B), dim3(kWWarps * 32),
+                                   smem, st, a);
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: launch: %s", cudaGetErrorString(e));
+  return check_launch("attn_warp_kernel");
+}
+
+template <typename KT, int DPL>
+int launch_warp_d(const AttnArgs &a, cudaStream_t st) {
+  if (a.gq <= 1) return launch_warp_cfg<KT, DPL, 1>(a, st);
+  if (a.gq <= 2) return launch_warp_cfg<KT, DPL, 2>(a, st);
+  if (a.gq <= 4) return launch_warp_cfg<KT, DPL, 4>(a, st);
+  if constexpr (DPL <= 4) return launch_warp_cfg<KT, DPL, 8>(a, st);
+  return fail(HELM_ERR_UNSUPPORTED, "paged_attn: GQA group %d at head dim %d", a.gq, a.D);
+}
+
+template <typename KT>
+int launch_warp(const AttnArgs &a, cudaStream_t st) {
+  switch (a.D) {
+    case 64: return launch_warp_d<KT, 2>(a, st);
+    case 128: return launch_warp_d<KT, 4>(a, st);
+    default: return launch_warp_d<KT, 8>(a, st);
+  }
 }
 
 template <typename T, int NT>
@@ -1586,7 +1839,7 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
   a.scale_log2 = p->scale * kLog2e;
   a.num_splits = S;
   a.error_flag = p->error_flag;
-  float *const records = p->workspace ? p->workspace + HELM_WORKSPACE_HEADER_BYTES / sizeof(float) : nullptr;
+  float *const records = p->workspace;
   if (S > 1) {
     a.rec = records;
   } else {
@@ -1609,8 +1862,7 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
       pa.rec_o = records;
       pa.rec_ml = reinterpret_cast<float *>(ws + pl.ml_off);
       pa.counter = reinterpret_cast<uint64_t *>(ws + pl.counter_off);
-      pa.token = reinterpret_cast<uint32_t *>(ws);
-      pa.done = reinterpret_cast<uint64_t *>(ws + 8);
+      pa.token = next_call_token();
       pa.C = pl.C;
       pa.xwait_ns = tc::kExchangeWaitNs;
       pa.xrank = 0;
@@ -1638,6 +1890,12 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
       rc = two ? launch_tc<__nv_bfloat16, 2>(mk, mv, a, st) : launch_tc<__nv_bfloat16, 1>(mk, mv, a, st);
     else
       rc = two ? launch_tc<__half, 2>(mk, mv, a, st) : launch_tc<__half, 1>(mk, mv, a, st);
+  } else if (warp_eligible(p)) {
+    switch (p->kv_dtype) {
+      case HELM_F32: rc = launch_warp<float>(a, st); break;
+      case HELM_F16: rc = launch_warp<__half>(a, st); break;
+      default: rc = launch_warp<__nv_bfloat16>(a, st); break;
+    }
   } else {
     switch (p->kv_dtype) {
       case HELM_F32: rc = launch_generic<float>(a, st); break;
@@ -1646,8 +1904,9 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
     }
   }
   if (rc != HELM_OK || S == 1) return rc;
-  lse_merge_kernel<<<rows, 128, 0, st>>>(records, S, (int64_t)rows * (p->D + 2), rows, p->D, p->out,
-                                         p->out_dtype, p->out_record);
+  const cudaError_t e = launch_pdl(lse_merge_kernel, dim3(rows), dim3(128), 0, st, (const float *)records, S,
+                                   (int64_t)rows * (p->D + 2), rows, p->D, p->out, p->out_dtype, p->out_record);
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: launch: %s", cudaGetErrorString(e));
   return check_launch("lse_merge_kernel");
 }
 
@@ -1705,7 +1964,7 @@ extern "C" int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, v
   int rc = validate(p);
   if (rc != HELM_OK) return rc;
   if (p->B == 0 || p->Hq == 0) return HELM_OK;
-  const int64_t cap = HELM_NOALLOC_SCRATCH_BYTES - HELM_WORKSPACE_HEADER_BYTES;  // bytes for records
+  const int64_t cap = HELM_NOALLOC_SCRATCH_BYTES;
   const int64_t per_split = (int64_t)p->B * p->Hq * (p->D + 2) * (int64_t)sizeof(float);
   int S = resolve_splits(p);
   if (S > 1 && (int64_t)S * per_split > cap) {

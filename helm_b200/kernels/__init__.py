@@ -12,9 +12,17 @@ Quantisation is symmetric per output channel: scale[n] = max_k |W[n, k]| / 127,
 W_q = round(W / scale) clipped to [-127, 127].  Decode-sized inputs
 (rows <= 64 of x) run the INT8 kernel; larger (prefill) inputs dequantise the
 weight to the activation dtype and use a dense GEMM.
+
+Projections that read the same input are fused (fuse=True, the default):
+an attention module's q_proj / k_proj / v_proj share one int8 weight, so a
+decode step projects q, k and v with one launch (Int8QKV; the three modules
+stay, as views of it, for prefill), and a SwiGLU MLP's gate_proj / up_proj and
+silu(gate) * up become one launch with the activation in the epilogue
+(Int8GLU, helm_int8_linear_glu).
 """
 from __future__ import annotations
 
+import types
 from typing import Iterable, Optional, Tuple
 
 import torch
@@ -95,23 +103,125 @@ class Int8Linear(nn.Module):
                 f"bias={self.bias is not None}, int8=True")
 
 
+class Int8QKV(nn.Module):
+    """q_proj, k_proj and v_proj of one attention module as one int8 weight [Nq+Nk+Nv, K] (and one
+    scale / bias vector): a decode step projects all three with one helm_int8_linear launch.  The
+    module's own q_proj / k_proj / v_proj become Int8Linear views of the fused buffers."""
+
+    def __init__(self, q: nn.Linear, k: nn.Linear, v: nn.Linear):
+        super().__init__()
+        parts = [quantize_weight(m.weight) for m in (q, k, v)]
+        self.splits = tuple(m.out_features for m in (q, k, v))
+        self.register_buffer("weight", torch.cat([p[0] for p in parts]).contiguous())
+        self.register_buffer("scale", torch.cat([p[1] for p in parts]).contiguous())
+        if q.bias is not None:
+            self.register_buffer("bias", torch.cat([m.bias.detach() for m in (q, k, v)]).contiguous())
+        else:
+            self.bias = None
+
+    def views(self):
+        """Int8Linear modules over the q, k and v rows of the fused buffers."""
+        out, lo = [], 0
+        K = self.weight.shape[1]
+        for n in self.splits:
+            m = Int8Linear(K, n, bias=self.bias is not None, device=self.weight.device, dtype=self.scale.dtype)
+            m.weight = self.weight[lo:lo + n]
+            m.scale = self.scale[lo:lo + n]
+            if self.bias is not None:
+                m.bias = self.bias[lo:lo + n]
+            out.append(m)
+            lo += n
+        return out
+
+    def forward(self, x: torch.Tensor):
+        """(q, k, v) projections of x as views of one [..., Nq+Nk+Nv] output."""
+        y = int8_linear(x, self.weight, self.scale, self.bias)
+        nq, nk, _ = self.splits
+        return y[..., :nq], y[..., nq:nq + nk], y[..., nq + nk:]
+
+
+class Int8GLU(nn.Module):
+    """gate_proj, up_proj and silu(gate) * up of a SwiGLU MLP as one tile-interleaved int8 weight
+    [2I, K] (ops.interleave_glu_rows): decode-sized inputs run helm_int8_linear_glu (one launch, the
+    activation in the epilogue); larger inputs dequantise the weight, run one dense GEMM and apply
+    silu(gate) * up in the activation dtype, as the unfused MLP does."""
+
+    def __init__(self, gate: nn.Linear, up: nn.Linear):
+        super().__init__()
+        qg, sg = quantize_weight(gate.weight)
+        qu, su = quantize_weight(up.weight)
+        self.I, self.K = gate.out_features, gate.in_features
+        self.register_buffer("weight", ops.interleave_glu_rows(qg, qu).contiguous())
+        self.register_buffer("scale", ops.interleave_glu_rows(sg, su).contiguous())
+        if gate.bias is not None:
+            self.register_buffer("bias", ops.interleave_glu_rows(gate.bias.detach(), up.bias.detach()).contiguous())
+        else:
+            self.bias = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.device.type != "cuda":
+            raise RuntimeError("Int8GLU runs on CUDA devices only (no CPU implementation)")
+        rows = x.numel() // x.shape[-1] if x.numel() else 0
+        if rows <= INT8_KERNEL_MAX_ROWS:
+            return ops.int8_linear_glu(x, self.weight, self.scale, self.bias)
+        w = self.weight.to(x.dtype) * self.scale.to(x.dtype)[:, None]
+        y = F.linear(x, w, None if self.bias is None else self.bias.to(x.dtype))
+        y = y.reshape(*x.shape[:-1], self.I // 16, 2, 16)
+        return (F.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*x.shape[:-1], self.I)
+
+
+def _glu_mlp_forward(mlp_self, x):
+    return mlp_self.down_proj(mlp_self._helm_glu(x))
+
+
+def _is_silu(act) -> bool:
+    return type(act).__name__ in ("SiLU", "SiLUActivation")
+
+
+def _linear_ok(m, skip, name) -> bool:
+    return (isinstance(m, nn.Linear) and name not in skip and m.weight.device.type == "cuda"
+            and m.in_features % 16 == 0 and m.weight.dtype in (torch.float16, torch.bfloat16))
+
+
 def patch_int8_linears(module: nn.Module, verbose: bool = False,
-                       skip: Iterable[str] = ("lm_head",)) -> int:
+                       skip: Iterable[str] = ("lm_head",), fuse: bool = True) -> int:
     """Replaces, in place, every fp16/bf16 nn.Linear child on a CUDA device whose in_features is a
     multiple of 16 with Int8Linear; children named in `skip` are kept.  Returns how many were replaced
-    (the contract of patch_cpu_linears, helm/kernels/__init__.py:133-157)."""
+    (the contract of patch_cpu_linears, helm/kernels/__init__.py:133-157).  With fuse=True, an
+    attention module's q/k/v projections share one fused weight (Int8QKV, module attribute
+    `_helm_qkv`) and a SwiGLU MLP's gate/up projections become one Int8GLU (`_helm_glu`, with the
+    MLP's forward patched on the instance); each still counts as its replaced linears."""
     if not is_available():
         if verbose:
             print(f"[helm_b200 kernels] library unavailable ({load_error()}); skipping patch")
         return 0
     skip = set(skip)
     count = 0
+    if fuse:
+        kids = dict(module.named_children())
+        qkv = [kids.get(n) for n in ("q_proj", "k_proj", "v_proj")]
+        if (all(_linear_ok(m, skip, n) for m, n in zip(qkv, ("q_proj", "k_proj", "v_proj")))
+                and len({(m.in_features, m.weight.dtype, m.bias is not None) for m in qkv}) == 1):
+            fused = Int8QKV(*qkv)
+            module._helm_qkv = fused
+            for n, m in zip(("q_proj", "k_proj", "v_proj"), fused.views()):
+                setattr(module, n, m)
+            count += 3
+        gate, up, down = kids.get("gate_proj"), kids.get("up_proj"), kids.get("down_proj")
+        if (_linear_ok(gate, skip, "gate_proj") and _linear_ok(up, skip, "up_proj") and down is not None
+                and _is_silu(getattr(module, "act_fn", None)) and gate.out_features % 16 == 0
+                and gate.weight.shape == up.weight.shape and (gate.bias is None) == (up.bias is None)):
+            module._helm_glu = Int8GLU(gate, up)
+            del module.gate_proj, module.up_proj
+            module.forward = types.MethodType(_glu_mlp_forward, module)
+            count += 2
     for name, child in list(module.named_children()):
+        if name == "_helm_qkv" or name == "_helm_glu":
+            continue
         if isinstance(child, nn.Linear):
-            if (name not in skip and child.weight.device.type == "cuda" and child.in_features % 16 == 0
-                    and child.weight.dtype in (torch.float16, torch.bfloat16)):
+            if _linear_ok(child, skip, name):
                 setattr(module, name, Int8Linear.from_linear(child))
                 count += 1
-        else:
-            count += patch_int8_linears(child, verbose=verbose, skip=skip)
+        elif not isinstance(child, Int8Linear):
+            count += patch_int8_linears(child, verbose=verbose, skip=skip, fuse=fuse)
     return count

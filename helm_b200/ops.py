@@ -190,6 +190,44 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
     return y.reshape(*lead, Nn)
 
 
+def int8_linear_glu(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+                    bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """helm_int8_linear_glu: silu(x @ Wg.T * sg + bg) * (x @ Wu.T * su + bu) from the tile-interleaved
+    int8 ``weight`` [2I, K] (see interleave_glu_rows) and ``scale`` / ``bias`` [2I]; returns [..., I]."""
+    dev = _need_cuda("int8_linear_glu", x, weight, scale, bias)
+    if weight.dtype != torch.int8 or weight.dim() != 2 or not weight.is_contiguous():
+        raise ValueError("int8_linear_glu: weight must be a contiguous int8 [2I, K] tensor")
+    N2, K = weight.shape
+    if x.shape[-1] != K or N2 % 32:
+        raise ValueError(f"int8_linear_glu: weight [{N2}, {K}] does not fit input [..., {x.shape[-1]}] "
+                         "(2I must be a multiple of 32)")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, K)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    if scale.shape != (N2,) or not scale.is_contiguous():
+        raise ValueError("int8_linear_glu: scale must be a contiguous [2I] tensor")
+    if bias is not None:
+        bias = bias.to(x.dtype).contiguous()
+    y = out if out is not None else torch.empty((M, N2 // 2), dtype=x.dtype, device=dev)
+    code = N.lib().helm_int8_linear_glu(x2.data_ptr(), dtype_code(x.dtype), weight.data_ptr(), scale.data_ptr(),
+                                        dtype_code(scale.dtype), _ptr(bias), y.data_ptr(), M, N2 // 2, K,
+                                        _stream(dev))
+    N.check("helm_int8_linear_glu", code)
+    return y.reshape(*lead, N2 // 2)
+
+
+def interleave_glu_rows(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[2I, ...] rows in the order helm_int8_linear_glu reads them: 16 gate rows, then the same 16
+    up rows, and so on (I a multiple of 16)."""
+    I = gate.shape[0]
+    if up.shape != gate.shape or I % 16:
+        raise ValueError("interleave_glu_rows: gate and up must match, with a multiple of 16 rows")
+    tail = gate.shape[1:]
+    return torch.stack((gate.reshape(I // 16, 16, *tail), up.reshape(I // 16, 16, *tail)), 1).reshape(2 * I, *tail)
+
+
 def int8_linear_error(reset: bool = True) -> int:
     """HELM_DEVERR_* bits raised by the INT8 kernels since the last reset (synchronises)."""
     v = ctypes.c_int32(0)

@@ -459,6 +459,17 @@ def _prefill(attn_self, kvcms, q, k, v, attention_mask, scale, k_exp, v_exp, sha
         dropout_p=attn_self.attention_dropout if attn_self.training else 0.0, scale=scale)
 
 
+def _project_qkv(attn_self, hidden_states, hidden_shape):
+    """The decode step's q, k and v projections, [B, 1, H, D] each: one launch when
+    patch_int8_linears fused the module's projections (Int8QKV; q, k and v are then strided views
+    of one output), else the three projection modules."""
+    fused = getattr(attn_self, "_helm_qkv", None)
+    if fused is not None:
+        return tuple(t.view(hidden_shape) for t in fused(hidden_states))
+    return (attn_self.q_proj(hidden_states).view(hidden_shape), attn_self.k_proj(hidden_states).view(hidden_shape),
+            attn_self.v_proj(hidden_states).view(hidden_shape))
+
+
 def _make_qwen2_forward(kvcms, shard=None):
     def forward(attn_self, hidden_states, position_embeddings, attention_mask=None, past_key_values=None,
                 cache_position=None, **kwargs):
@@ -468,9 +479,7 @@ def _make_qwen2_forward(kvcms, shard=None):
         cos, sin = position_embeddings
         scale = 1.0 / math.sqrt(attn_self.head_dim)
         if q_len == 1:
-            pro = _Prologue(attn_self.q_proj(hidden_states).view(hidden_shape),
-                            attn_self.k_proj(hidden_states).view(hidden_shape),
-                            attn_self.v_proj(hidden_states).view(hidden_shape), cos, sin, apply_rotary_pos_emb)
+            pro = _Prologue(*_project_qkv(attn_self, hidden_states, hidden_shape), cos, sin, apply_rotary_pos_emb)
             out = _decode_batched(kvcms, None, None, None, attn_self.layer_idx, scale, shard=shard, prologue=pro)
         else:
             q = attn_self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)
@@ -494,9 +503,7 @@ def _make_qwen3_forward(kvcms, shard=None):
         cos, sin = position_embeddings
         scale = 1.0 / math.sqrt(attn_self.head_dim)
         if q_len == 1:
-            pro = _Prologue(attn_self.q_proj(hidden_states).view(hidden_shape),
-                            attn_self.k_proj(hidden_states).view(hidden_shape),
-                            attn_self.v_proj(hidden_states).view(hidden_shape), cos, sin, apply_rotary_pos_emb,
+            pro = _Prologue(*_project_qkv(attn_self, hidden_states, hidden_shape), cos, sin, apply_rotary_pos_emb,
                             q_norm=attn_self.q_norm, k_norm=attn_self.k_norm)
             out = _decode_batched(kvcms, None, None, None, attn_self.layer_idx, scale, shard=shard, prologue=pro)
         else:
@@ -521,9 +528,7 @@ def _make_llama_forward(kvcms, shard=None):
         cos, sin = position_embeddings
         scale = 1.0 / math.sqrt(attn_self.head_dim)
         if q_len == 1:
-            pro = _Prologue(attn_self.q_proj(hidden_states).view(hidden_shape),
-                            attn_self.k_proj(hidden_states).view(hidden_shape),
-                            attn_self.v_proj(hidden_states).view(hidden_shape), cos, sin, apply_rotary_pos_emb)
+            pro = _Prologue(*_project_qkv(attn_self, hidden_states, hidden_shape), cos, sin, apply_rotary_pos_emb)
             out = _decode_batched(kvcms, None, None, None, attn_self.layer_idx, scale, shard=shard, prologue=pro)
         else:
             q = attn_self.q_proj(hidden_states).view(hidden_shape).transpose(1, 2)

@@ -81,8 +81,7 @@ const char *helm_last_error(void);
  * query head: float rec[D+2] = { o[0..D-1], m, l }, where m is the running
  * max of the base-2 logits s*scale*log2(e), l = sum 2^(logit-m) and o the
  * unnormalised sum of 2^(logit-m) * v.  An empty range has m = -inf, l = 0,
- * o = 0.  Records are stored [split][B*Hq][D+2] in `workspace`, after its
- * header (below).
+ * o = 0.  Records are stored [split][B*Hq][D+2] in `workspace`.
  *
  * Output.  When `out` is non-null the records are merged (helm_lse_merge
  * semantics) into out [B, Hq, D] of out_dtype; when `out_record` is non-null
@@ -90,15 +89,14 @@ const char *helm_last_error(void);
  * cross-GPU merge.  With num_splits == 1 and only `out` requested, no
  * workspace is touched.
  *
- * Workspace.  Its first HELM_WORKSPACE_HEADER_BYTES hold a call token and
- * arrival counters of the single-launch (persistent) path, tagged with the
- * token so that no call needs them zeroed: a fresh workspace, or one whose
- * counters a timed-out call left behind, is valid as it is.  The split
- * records follow the header.  The kernels are launched with programmatic
- * dependent launch and read the workspace only after the previous kernel on
- * the stream has finished, so consecutive calls may share one workspace.
+ * Workspace.  The single-launch (persistent) path keeps per-CTA records and
+ * per-(sequence, kv head) arrival counters there.  The counters are tagged
+ * with a token the library issues per call, so no call needs them zeroed: a
+ * fresh workspace, or one a split-path call or a timed-out call wrote over, is
+ * valid as it is.  The kernels are launched with programmatic dependent launch
+ * and touch the workspace only after the previous kernel on the stream has
+ * finished, so consecutive calls on one stream may share one workspace.
  */
-#define HELM_WORKSPACE_HEADER_BYTES 256
 /* Cross-GPU exchange fused into helm_paged_attn_decode (KV sequence sharding).
  * With params.exchange set, each rank's pages are its share of every sequence:
  * the CTA that completes a (sequence, kv head) pair's rank-local merge stores
@@ -172,9 +170,8 @@ int helm_paged_attn_decode(const helm_paged_attn_params *p, void *stream);
  * array of HELM_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds
  * until the process exits.  Nothing is allocated or freed.  With
  * num_splits == 0 the split count is capped to what the array holds; an
- * explicit num_splits whose records (num_splits * B*Hq*(D+2)*4 bytes, after
- * the HELM_WORKSPACE_HEADER_BYTES header) exceed it is rejected with
- * HELM_ERR_WORKSPACE.
+ * explicit num_splits whose records (num_splits * B*Hq*(D+2)*4 bytes) exceed
+ * it is rejected with HELM_ERR_WORKSPACE.
  *
  * The first call on a device looks up the array's device address (with that
  * device current) and so should come before any stream capture.  All calls in
@@ -223,6 +220,21 @@ int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
                      const void *w_scale, int32_t scale_dtype,
                      const void *bias, void *y, int32_t M, int32_t N,
                      int32_t K, void *stream);
+
+/* Gated INT8 linear (SwiGLU MLP front half) in one launch:
+ *   y[m, j] = silu(g[m, j]) * u[m, j],  g = x . Wg^T * sg + bg,  u = x . Wu^T * su + bu
+ * for j < I.  w [2I, K] int8 holds the gate and up rows interleaved in tiles of
+ * 16 rows: rows 32t..32t+15 are gate rows 16t..16t+15 and rows 32t+16..32t+31
+ * the up rows 16t..16t+15; w_scale [2I] and bias [2I] (or null) follow the same
+ * order.  y [M, I] of x_dtype; I a multiple of 16; otherwise the contract of
+ * helm_int8_linear (fp32 accumulation, silu in fp32, one rounding to x_dtype).
+ * No counterpart in the reference's kernels: it fuses the decoder MLP's
+ * gate_proj, up_proj and act_fn(gate) * up (transformers' Qwen3MLP / LlamaMLP
+ * forward, run around the patched attention). */
+int helm_int8_linear_glu(const void *x, int32_t x_dtype, const int8_t *w,
+                         const void *w_scale, int32_t scale_dtype,
+                         const void *bias, void *y, int32_t M, int32_t I,
+                         int32_t K, void *stream);
 
 /* HELM_DEVERR_* bits raised by the INT8 kernels since the last reset (a bounded
  * wait of the weight pipeline that gave up: HELM_DEVERR_TIMEOUT; the rows of
