@@ -68,6 +68,10 @@ def parse():
     # Smaller stacks for ncu captures only; the reported workload is config 5 unless these are set.
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=None)
+    # One config-2 GEMV shape / row count only (ncu captures of a single shape); the reported
+    # workload is all nine calls unless these are set.
+    ap.add_argument("--shape", default=None, help="config2 only: N,K of a single shape")
+    ap.add_argument("--rows", type=int, default=None, help="config2 only: a single M")
     args = ap.parse_args()
     if args.layers is not None:
         CFG["layers"] = args.layers
@@ -689,9 +693,10 @@ def config2_line(args, rank, world, dev):
     t_load0 = time.time()
     e2e_bytes_in = e2e_bytes_out = 0
     e2e_ms = 0.0
-    for (Nn, K) in C2_SHAPES:
+    shapes = [tuple(int(v) for v in args.shape.split(","))] if args.shape else C2_SHAPES
+    for (Nn, K) in shapes:
         copies = max(4, -(-4 * l2 // (Nn * K)))
-        for M in C2_ROWS:
+        for M in ([args.rows] if args.rows else C2_ROWS):
             w, s, x = c2_inputs(Nn, K, M, dev, copies)
             y = torch.empty((M, Nn), dtype=torch.float16, device=dev)
 
@@ -755,7 +760,9 @@ def config2_line(args, rank, world, dev):
             "warmup": args.warmup, "ms_per_step": tot_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 x fp16 -> fp32", "data": "synthetic",
             "timing": "per shape: CUDA graph of one call per weight copy, replayed; CUDA events; a step = the 9 calls",
-            "config": {"workload": C2_WORKLOAD, "parallelism": f"replicas{world}",
+            "config": {"workload": C2_WORKLOAD if not (args.shape or args.rows) else
+                       f"REDUCED (profiling only): shape {args.shape or 'all'}, M {args.rows or 'all'}",
+                       "parallelism": f"replicas{world}",
                        "l2": "weight copies rotate through > 4x L2 per shape"},
             "cases": cases,
             "roofline": {"bound": "hbm", "achieved": agg, "peak": hbm_peak, "unit": "GB/s", "frac": agg / hbm_peak,

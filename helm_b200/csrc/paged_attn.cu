@@ -249,16 +249,29 @@ __global__ void __launch_bounds__(128) attn_generic_kernel(AttnArgs a) {
 // Warp-per-token-octet kernel (CUDA cores): fp32 pages, and 16-bit pages the
 // tensor-core kernels do not take, for D = 32*DPL (DPL 1..8) and GQA group <= 8.
 //
-// grid (S, Hkv, B), 256 threads.  Lane l owns dims [l*DPL, l*DPL + DPL) of
+// grid (S, Hkv, B), 128 threads.  Lane l owns dims [l*DPL, l*DPL + DPL) of
 // every row, so a K or V row is one coalesced 32*DPL-element load per warp.
 // The split's pages are cut into octets of 8 tokens; warp w takes octets w,
-// w+8, ... of each page.  Per octet a warp loads the 8 K and 8 V rows at once
+// w+4, ... of each page.  Per octet a warp loads the 8 K and 8 V rows at once
 // (many loads in flight per warp), forms the 8 x GQ scores with a butterfly
 // sum over the lanes, and updates its running (m, l, o) with one rescale per
-// octet.  The eight warps' states are merged in shared memory at the end.
+// octet.  The four warps' states are merged in shared memory at the end.
 // ===========================================================================
-constexpr int kWWarps = 8;
+constexpr int kWWarps = 4;
 constexpr int kOct = 8;
+
+// Adds one arrival to a token-tagged counter word and returns the arrivals after it; a word that
+// carries another call's token (stale, or never written) counts as zero.
+__device__ __forceinline__ uint32_t tagged_arrive(uint64_t *word, uint32_t tok) {
+  unsigned long long old = *reinterpret_cast<volatile unsigned long long *>(word);
+  for (;;) {
+    const uint32_t cnt = (uint32_t)(old >> 32) == tok ? (uint32_t)old : 0u;
+    const unsigned long long nw = ((unsigned long long)tok << 32) | (cnt + 1u);
+    const unsigned long long prev = atomicCAS(reinterpret_cast<unsigned long long *>(word), old, nw);
+    if (prev == old) return cnt + 1u;
+    old = prev;
+  }
+}
 
 template <typename KT, int DPL> struct RowLoad;
 template <int DPL> struct RowLoad<float, DPL> {
@@ -814,18 +827,6 @@ struct PersistArgs {
 
 constexpr uint64_t kExchangeWaitNs = 2000000000ull;
 
-// Adds one arrival to a token-tagged counter word and returns the arrivals after it; a word that
-// carries another call's token (stale, or never written) counts as zero.
-__device__ __forceinline__ uint32_t tagged_arrive(uint64_t *word, uint32_t tok) {
-  unsigned long long old = *reinterpret_cast<volatile unsigned long long *>(word);
-  for (;;) {
-    const uint32_t cnt = (uint32_t)(old >> 32) == tok ? (uint32_t)old : 0u;
-    const unsigned long long nw = ((unsigned long long)tok << 32) | (cnt + 1u);
-    const unsigned long long prev = atomicCAS(reinterpret_cast<unsigned long long *>(word), old, nw);
-    if (prev == old) return cnt + 1u;
-    old = prev;
-  }
-}
 
 __device__ __forceinline__ uint64_t ll_word(float v, uint32_t epoch) {
   return ((uint64_t)epoch << 32) | __float_as_uint(v);
@@ -1474,26 +1475,65 @@ __global__ void __launch_bounds__(kThreads, 2)
 __global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict__ parts, int S, int64_t pstride,
                                                        int rows, int D, void *out, int out_dtype,
                                                        float *out_record) {
+  // One CTA per row.  The partials' (m, l) are read once, in parallel, and their weights
+  // 2^(m_s - M) kept in shared memory (in chunks of kChunk partials); each thread then sums its
+  // dims over the chunk's partials with independent loads.
+  constexpr int kChunk = 1024;
+  __shared__ float w_s[kChunk];
+  __shared__ float red[4];
+  __shared__ float s_M, s_L;
   const int row = blockIdx.x;
   const int rl = D + 2;
   const float *base = parts + (int64_t)row * rl;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_trigger();
   pdl_wait();
+  // M = max_s m_s
   float M = -INFINITY;
-  for (int s = 0; s < S; ++s) M = fmaxf(M, base[s * pstride + D]);
+  for (int sp = tid; sp < S; sp += blockDim.x) M = fmaxf(M, base[sp * pstride + D]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  if (tid == 0) s_M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  M = s_M;
   float L = 0.f;
-  for (int s = 0; s < S; ++s) {
-    const float *p = base + s * pstride;
-    L = fmaf(p[D + 1], rescale_weight(p[D], M), L);
-  }
-  if (M == -INFINITY) L = 0.f;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float O = 0.f;
-    if (M != -INFINITY)
-      for (int s = 0; s < S; ++s) {
-        const float *p = base + s * pstride;
-        O = fmaf(p[d], rescale_weight(p[D], M), O);
+  float O0 = 0.f, O1 = 0.f;   // dims tid and tid + 128 (D <= 256)
+  for (int c0 = 0; c0 < S; c0 += kChunk) {
+    const int n = min(kChunk, S - c0);
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+      const float *p = base + (int64_t)(c0 + i) * pstride;
+      const float w = rescale_weight(p[D], M);
+      w_s[i] = w;
+      L = fmaf(p[D + 1], w, L);
+    }
+    __syncthreads();
+    if (M != -INFINITY) {
+      const float *src = base + (int64_t)c0 * pstride;
+      if (tid < D) {
+#pragma unroll 16
+        for (int i = 0; i < n; ++i) O0 = fmaf(src[(int64_t)i * pstride + tid], w_s[i], O0);
       }
+      if (tid + 128 < D) {
+#pragma unroll 16
+        for (int i = 0; i < n; ++i) O1 = fmaf(src[(int64_t)i * pstride + tid + 128], w_s[i], O1);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  __syncthreads();
+  if (lane == 0) red[warp] = L;
+  __syncthreads();
+  if (tid == 0) s_L = M == -INFINITY ? 0.f : red[0] + red[1] + red[2] + red[3];
+  __syncthreads();
+  L = s_L;
+  for (int k = 0; k < 2; ++k) {
+    const int d = tid + 128 * k;
+    if (d >= D) break;
+    const float O = M == -INFINITY ? 0.f : (k ? O1 : O0);
     if (out) store_f(out, out_dtype, (int64_t)row * D + d, L > 0.f ? O / L : 0.f);
     if (out_record) {
       float *rr = out_record + (int64_t)row * rl;
@@ -1625,10 +1665,11 @@ bool warp_eligible(const helm_paged_attn_params *p) {
 int resolve_splits(const helm_paged_attn_params *p) {
   if (p->num_splits > 0) return p->num_splits;
   if (!tc_eligible(p) && warp_eligible(p)) {
-    // about two CTAs of 8 warps per SM, every CTA with at least one page
+    // up to four CTAs of 4 warps per SM (the register budget keeps four resident), every CTA with
+    // at least one page: the whole grid runs in one wave with most of the call's K/V in flight
     const int pairs = p->B * p->Hkv;
     if (pairs <= 0 || p->max_pages <= 1) return 1;
-    int S = (2 * num_sms() + pairs - 1) / pairs;
+    int S = (4 * num_sms() + pairs - 1) / pairs;
     return S > p->max_pages ? p->max_pages : S;
   }
   const int pairs = p->B * p->Hkv;
@@ -1916,6 +1957,7 @@ extern "C" int helm_lse_merge(const float *partials, int32_t num_partials, int64
     return fail(HELM_ERR_INVALID_ARGUMENT, "lse_merge: bad sizes rows=%d D=%d partials=%d stride=%lld", rows, D,
                 num_partials, (long long)partial_stride);
   if (!partials || (!out && !out_record)) return fail(HELM_ERR_INVALID_ARGUMENT, "lse_merge: null pointer");
+  if (D > 256) return fail(HELM_ERR_UNSUPPORTED, "lse_merge: head dim %d > 256", D);
   if (out && out_dtype != HELM_F32 && out_dtype != HELM_F16 && out_dtype != HELM_BF16)
     return fail(HELM_ERR_UNSUPPORTED, "lse_merge: dtype %d", out_dtype);
   if (rows == 0) return HELM_OK;
@@ -1964,9 +2006,9 @@ extern "C" int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, v
   int rc = validate(p);
   if (rc != HELM_OK) return rc;
   if (p->B == 0 || p->Hq == 0) return HELM_OK;
+  int S = resolve_splits(p);
   const int64_t cap = HELM_NOALLOC_SCRATCH_BYTES;
   const int64_t per_split = (int64_t)p->B * p->Hq * (p->D + 2) * (int64_t)sizeof(float);
-  int S = resolve_splits(p);
   if (S > 1 && (int64_t)S * per_split > cap) {
     if (p->num_splits > 0)
       return fail(HELM_ERR_WORKSPACE,

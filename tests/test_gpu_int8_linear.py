@@ -110,3 +110,45 @@ def test_repeated_calls_identical(cuda):
     w, s, x = _inputs(4, 1024, 16384, seed=5)
     wd, sd, xd = torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda), x.to(cuda)
     assert torch.equal(ops.int8_linear(xd, wd, sd), ops.int8_linear(xd, wd, sd))
+
+
+def _glu_ref(x, wg, sg, bg, wu, su, bu):
+    g = x @ (wg.astype(np.float64) * sg.astype(np.float64)[:, None]).T + bg
+    u = x @ (wu.astype(np.float64) * su.astype(np.float64)[:, None]).T + bu
+    return g / (1.0 + np.exp(-g)) * u
+
+
+@pytest.mark.parametrize("I,K", [(64, 256), (1024, 1024), (2944, 528), (12288, 4096)])
+@pytest.mark.parametrize("M", [1, 4, 9, 33, 64])
+@pytest.mark.parametrize("xdtype", [torch.float16, torch.bfloat16])
+def test_glu_matches_oracle(I, K, M, xdtype, cuda):
+    """helm_int8_linear_glu (gate and up rows tile-interleaved, silu(gate) * up in the epilogue)
+    against float64 gate / up projections; the error is the output rounding."""
+    from helm_b200 import ops
+    rng = np.random.default_rng(I + K + M)
+    wg = rng.integers(-127, 128, size=(I, K), dtype=np.int8)
+    wu = rng.integers(-127, 128, size=(I, K), dtype=np.int8)
+    sg = rng.uniform(0.001, 0.02, size=(I,)).astype(np.float16)
+    su = rng.uniform(0.001, 0.02, size=(I,)).astype(np.float16)
+    bg = rng.standard_normal(I).astype(np.float32)
+    bu = rng.standard_normal(I).astype(np.float32)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32) / np.sqrt(K / 64)).to(xdtype)
+    w = ops.interleave_glu_rows(torch.from_numpy(wg), torch.from_numpy(wu)).contiguous()
+    s = ops.interleave_glu_rows(torch.from_numpy(sg), torch.from_numpy(su)).contiguous()
+    b = ops.interleave_glu_rows(torch.from_numpy(bg), torch.from_numpy(bu)).to(xdtype)
+    y = ops.int8_linear_glu(x.to(cuda), w.to(cuda), s.to(cuda), bias=b.to(cuda))
+    bgx = torch.from_numpy(bg).to(xdtype).double().numpy()
+    bux = torch.from_numpy(bu).to(xdtype).double().numpy()
+    ref = _glu_ref(x.double().numpy(), wg, sg, bgx, wu, su, bux)
+    assert y.shape == (M, I) and y.dtype == xdtype
+    assert rel_err(y, ref) <= 4e-3 * (2.0 if xdtype == torch.bfloat16 else 1.0)
+    assert ops.int8_linear_error() == 0
+
+
+def test_glu_rejects_ragged_intermediate(cuda):
+    from helm_b200 import ops
+    from helm_b200._native import HelmError
+    w = torch.zeros(48, 64, dtype=torch.int8, device=cuda)   # I = 24: not a multiple of 16
+    with pytest.raises((HelmError, ValueError)):
+        ops.int8_linear_glu(torch.zeros(1, 64, dtype=torch.float16, device=cuda), w,
+                            torch.ones(48, dtype=torch.float16, device=cuda))

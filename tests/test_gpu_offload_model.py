@@ -3,7 +3,9 @@ PipelineRuntime (explicit causal / decode masks, one token per step) with KVOffl
 patched attention, against the unpatched model's logits on the full sequence.
 
 Covers the three decode paths (contiguous buffers, all-GPU pages, mixed residency with
-eviction to pinned host memory), batch > 1, page-boundary crossings and reset()."""
+eviction to pinned host memory), batch > 1, page-boundary crossings and reset().  The bar is set by
+bf16's own noise: the patched model's logits against an fp32 run of the same model may differ by
+at most 1.25 x what the unpatched bf16 model's logits do (plus 0.2 % of the logit scale)."""
 import pytest
 import torch
 
@@ -58,12 +60,28 @@ def _pipeline_logits(model, ids, prompt_len):
     return torch.stack(out, dim=1)  # logits predicting tokens prompt_len .. n
 
 
-def _check(ours, ref, what):
+def _check(ours, ref, what, ref32=None):
+    """ours vs the unpatched bf16 model (ref).  With ref32 (the same model run in fp32) the bar is
+    relative to bf16's own noise: our error against fp32 may exceed the unpatched bf16 model's error
+    against fp32 by at most 25 % plus 0.2 % of the logit scale."""
     err = float((ours.float() - ref.float()).abs().max())
     scale = max(1.0, float(ref.float().abs().max()))
-    assert err <= 0.06 * scale, f"{what}: max logit error {err:.4f} (scale {scale:.2f})"
+    assert err <= 0.03 * scale, f"{what}: max logit error {err:.4f} (scale {scale:.2f})"
     agree = (ours.argmax(-1) == ref.argmax(-1)).float().mean().item()
-    assert agree >= 0.9, f"{what}: argmax agreement {agree:.2f}"
+    assert agree >= 0.95, f"{what}: argmax agreement {agree:.2f}"
+    if ref32 is not None:
+        noise = float((ref.float() - ref32).abs().max())
+        ours32 = float((ours.float() - ref32).abs().max())
+        assert ours32 <= 1.25 * noise + 2e-3 * scale, \
+            f"{what}: error vs fp32 {ours32:.4f} > 1.25 x the bf16 model's own {noise:.4f} + 0.2% of {scale:.2f}"
+
+
+def _fp32_logits(model, ids):
+    import copy
+    m32 = copy.deepcopy(model).float()
+    out = _reference_logits(m32, ids).float()
+    del m32
+    return out
 
 
 @pytest.mark.parametrize("mode", ["paged", "contiguous", "offload", "paged_fused_norms"])
@@ -74,12 +92,13 @@ def test_qwen3_decode_paths_match_unpatched(mode):
     torch.manual_seed(1)
     ids = torch.randint(0, 320, (B, S + steps), device=DEV)
     ref = _reference_logits(model, ids)[:, S - 1:]
+    ref32 = _fp32_logits(model, ids)[:, S - 1:]
     cfg = KVOffloadConfig.from_model(model, page_size=64, cont_capacity=4096 if mode == "contiguous" else 0,
                                      gpu_watermark_bytes=(2 * 2 * 64 * 128 * 2 * 2) if mode == "offload" else 10 ** 12)
     mgr = KVOffloadManager(model, cfg, batch_size=B, fused_norms=mode == "paged_fused_norms")
     try:
         ours = _pipeline_logits(model, ids, S)
-        _check(ours, ref, mode)
+        _check(ours, ref, mode, ref32)
         rep = mgr.report()
         if mode == "offload":
             assert rep["active_cpu_pages"] > 0
@@ -104,9 +123,10 @@ def test_other_architectures(arch):
     torch.manual_seed(2)
     ids = torch.randint(0, 320, (1, 150), device=DEV)
     ref = _reference_logits(model, ids)[:, 99:]
+    ref32 = _fp32_logits(model, ids)[:, 99:]
     mgr = KVOffloadManager(model, KVOffloadConfig.from_model(model, cont_capacity=0), batch_size=1)
     try:
-        _check(_pipeline_logits(model, ids, 100), ref, arch)
+        _check(_pipeline_logits(model, ids, 100), ref, arch, ref32)
     finally:
         mgr.restore()
 

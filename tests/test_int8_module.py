@@ -45,6 +45,34 @@ def test_int8_linear_module_matches_dequantised_linear(M):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 8, 64, 200])
+def test_fused_glu_and_qkv_modules(M):
+    """Int8GLU (one launch with silu(gate) * up in the epilogue, or the dequantised GEMM for prefill
+    sizes) and Int8QKV (one launch, three strided views) against float64 on the same int8 weights."""
+    torch.manual_seed(2)
+    gate = nn.Linear(512, 320, bias=False).cuda().to(torch.bfloat16)
+    up = nn.Linear(512, 320, bias=False).cuda().to(torch.bfloat16)
+    glu = K.Int8GLU(gate, up)
+    x = torch.randn(M, 512, device="cuda", dtype=torch.bfloat16)
+    qg, sg = K.quantize_weight(gate.weight)
+    qu, su = K.quantize_weight(up.weight)
+    g = x.double() @ (qg.double() * sg.double()[:, None]).T
+    u = x.double() @ (qu.double() * su.double()[:, None]).T
+    ref = torch.nn.functional.silu(g) * u
+    y = glu(x)
+    assert y.shape == (M, 320) and y.dtype == torch.bfloat16
+    assert float((y.double() - ref).abs().max()) <= 2e-2 * float(ref.abs().max())
+    q, k, v = (nn.Linear(512, n, bias=True).cuda().to(torch.bfloat16) for n in (256, 64, 64))
+    fused = K.Int8QKV(q, k, v)
+    outs = fused(x)
+    for lin, o, view in zip((q, k, v), outs, fused.views()):
+        assert torch.equal(o, view(x)) if M <= 64 else o.shape == view(x).shape
+        qw, sw = K.quantize_weight(lin.weight)
+        r = x.double() @ (qw.double() * sw.double()[:, None]).T + lin.bias.double()
+        assert float((o.double() - r).abs().max()) <= 1e-2 * float(r.abs().max())
+
+
+@pytest.mark.gpu
 def test_patch_tiny_qwen3_and_decode_with_offload():
     """INT8 linears + paged decode attention in one model (the config-4 combination)."""
     import transformers
@@ -59,6 +87,8 @@ def test_patch_tiny_qwen3_and_decode_with_offload():
     n = K.patch_int8_linears(model)
     assert n == 2 * 7  # q, k, v, o, gate, up, down per layer; lm_head kept
     assert isinstance(model.model.layers[0].self_attn.q_proj, K.Int8Linear)
+    assert isinstance(model.model.layers[0].self_attn._helm_qkv, K.Int8QKV)
+    assert isinstance(model.model.layers[0].mlp._helm_glu, K.Int8GLU)
     assert isinstance(model.lm_head, nn.Linear)
     torch.manual_seed(4)
     ids = torch.randint(0, 320, (2, 140), device="cuda")
