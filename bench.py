@@ -698,31 +698,35 @@ def config2_line(args, rank, world, dev):
         copies = max(4, -(-4 * l2 // (Nn * K)))
         for M in ([args.rows] if args.rows else C2_ROWS):
             w, s, x = c2_inputs(Nn, K, M, dev, copies)
+            wp = [ops.int8_pack_weight(wi) for wi in w]   # the layout Int8Linear keeps
             y = torch.empty((M, Nn), dtype=torch.float16, device=dev)
 
-            def calls():
-                for wi in w:
-                    N.check("helm_int8_linear", lib.helm_int8_linear(
-                        x.data_ptr(), ops.dtype_code(x.dtype), wi.data_ptr(), s.data_ptr(), ops.dtype_code(s.dtype),
-                        None, y.data_ptr(), M, Nn, K, torch.cuda.current_stream(dev).cuda_stream))
-            for _ in range(max(args.warmup, 3)):
-                calls()
-            torch.cuda.synchronize(dev)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                calls()
-            graph.replay()
-            torch.cuda.synchronize(dev)
-            reps = max(1, args.steps // 10)
-            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            barrier(world)
-            t0.record(stream)
-            for _ in range(reps):
+            def time_calls(fn, weights):
+                def calls():
+                    for wi in weights:
+                        N.check("helm_int8_linear", fn(
+                            x.data_ptr(), ops.dtype_code(x.dtype), wi.data_ptr(), s.data_ptr(),
+                            ops.dtype_code(s.dtype), None, y.data_ptr(), M, Nn, K,
+                            torch.cuda.current_stream(dev).cuda_stream))
+                for _ in range(max(args.warmup, 3)):
+                    calls()
+                torch.cuda.synchronize(dev)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    calls()
                 graph.replay()
-            t1.record(stream)
-            torch.cuda.synchronize(dev)
-            ms = max_over_ranks(t0.elapsed_time(t1), world, dev) / (reps * copies)
-            del graph
+                torch.cuda.synchronize(dev)
+                reps = max(1, args.steps // 10)
+                t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                barrier(world)
+                t0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                t1.record(stream)
+                torch.cuda.synchronize(dev)
+                return max_over_ranks(t0.elapsed_time(t1), world, dev) / (reps * copies)
+            ms = time_calls(lib.helm_int8_linear_packed, [p.data for p in wp])
+            ms_rowmajor = time_calls(lib.helm_int8_linear, w)
             nbytes = c2_bytes(M, Nn, K)
             tot_bytes += nbytes
             tot_ms += ms
@@ -746,8 +750,9 @@ def config2_line(args, rank, world, dev):
             e2e_bytes_in += x_h.numel() * 2
             e2e_bytes_out += y_h.numel() * 2
             cases.append({"N": Nn, "K": K, "M": M, "us": round(ms * 1e3, 3), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
-                          "copies": copies})
-            del w, x, y, mod
+                          "copies": copies, "rowmajor_us": round(ms_rowmajor * 1e3, 3),
+                          "rowmajor_gbs": round(nbytes / (ms_rowmajor * 1e-3) / 1e9, 1)})
+            del w, wp, x, y, mod
     clk = clocks.stop(t_load0, time.time())
     if rank == 0:
         hbm_peak, peak_kind = peaks()
@@ -759,14 +764,16 @@ def config2_line(args, rank, world, dev):
             "metric": C2_METRIC, "value": agg * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": tot_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 x fp16 -> fp32", "data": "synthetic",
-            "timing": "per shape: CUDA graph of one call per weight copy, replayed; CUDA events; a step = the 9 calls",
+            "timing": ("per shape: CUDA graph of one helm_int8_linear_packed call per weight copy (the packed layout "
+                       "Int8Linear keeps), replayed; CUDA events; a step = the 9 calls; rowmajor_* = the same calls "
+                       "on row-major weights (helm_int8_linear)"),
             "config": {"workload": C2_WORKLOAD if not (args.shape or args.rows) else
                        f"REDUCED (profiling only): shape {args.shape or 'all'}, M {args.rows or 'all'}",
                        "parallelism": f"replicas{world}",
                        "l2": "weight copies rotate through > 4x L2 per shape"},
             "cases": cases,
             "roofline": {"bound": "hbm", "achieved": agg, "peak": hbm_peak, "unit": "GB/s", "frac": agg / hbm_peak,
-                         "traffic": None, "peak_kind": peak_kind, "kernel": "int8 GEMV (helm_int8_linear)",
+                         "traffic": None, "peak_kind": peak_kind, "kernel": "int8 GEMV (int8_tma_kernel, packed weights: helm_int8_linear_packed)",
                          "bytes_per_launch": tot_bytes / len(cases), "avg_launch_ms": tot_ms / len(cases)},
             "cpu_baseline": cpu,
             "e2e": {"value": tot_bytes / (e2e_ms * 1e-3) / 1e9 * world, "unit": "GB/s",

@@ -86,6 +86,21 @@ class DecodePrologueParams(ctypes.Structure):
     ]
 
 
+class KVPrefillParams(ctypes.Structure):
+    _fields_ = [
+        ("k_src", _p), ("v_src", _p), ("src_dtype", _i32),
+        ("src_head_stride", _i64), ("src_tok_stride", _i64),
+        ("k_base", _p), ("v_base", _p),
+        ("page_stride", _i64), ("head_stride", _i64),
+        ("num_pool_pages", _i32), ("kv_dtype", _i32),
+        ("Hkv", _i32), ("D", _i32), ("P", _i32),
+        ("pages", _p), ("count", _i32),
+        ("page_table", _p), ("page_used", _p), ("num_pages", _p),
+        ("page_table_stride", _i32), ("first_index", _i32),
+        ("error_flag", _p),
+    ]
+
+
 class GatherMergeParams(ctypes.Structure):
     _fields_ = [
         ("rank", _i32), ("world", _i32), ("rows", _i32), ("D", _i32),
@@ -106,9 +121,14 @@ SIGNATURES = [
     ("helm_lse_merge", _c.c_int, [_p, _i32, _i64, _i32, _i32, _p, _i32, _p, _p]),
     ("helm_int8_linear", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
     ("helm_int8_linear_glu", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
+    ("helm_int8_packed_bytes", _i64, [_i32, _i32]),
+    ("helm_int8_pack_weight", _c.c_int, [_p, _i32, _i32, _p, _p]),
+    ("helm_int8_linear_packed", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
+    ("helm_int8_linear_glu_packed", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
     ("helm_int8_linear_error", _c.c_int, [_p, _i32]),
     ("helm_kv_append", _c.c_int, [_c.POINTER(KVAppendParams), _p]),
     ("helm_decode_prologue", _c.c_int, [_c.POINTER(DecodePrologueParams), _p]),
+    ("helm_kv_write_pages", _c.c_int, [_c.POINTER(KVPrefillParams), _p]),
     ("helm_rmsnorm", _c.c_int, [_p, _i32, _i64, _p, _i32, _p, _i64, _i64, _i32, ctypes.c_float, _p]),
     ("helm_copy_pages", _c.c_int, [_p, _i64, _p, _p, _i32, _i64, _c.POINTER(_i32), _p]),
     ("helm_move_pages", _c.c_int, [_p, _p, _p, _p, _i32, _i64, _i64, _i64, _c.POINTER(_i32), _p]),

@@ -16,7 +16,8 @@ PKG = pathlib.Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIBDIR = PKG / "lib"
 LIB = LIBDIR / "libhelm_b200.so"
-SOURCES = ["common.cu", "paged_attn.cu", "int8_linear.cu", "kv_append.cu", "gather_merge.cu", "norm.cu", "page_copy.cu"]
+SOURCES = ["common.cu", "paged_attn.cu", "int8_linear.cu", "kv_append.cu", "kv_prefill.cu", "gather_merge.cu", "norm.cu",
+           "page_copy.cu"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

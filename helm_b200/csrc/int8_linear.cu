@@ -41,6 +41,7 @@
 #include "common.cuh"
 #include "tma.cuh"
 
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -69,6 +70,33 @@ inline int ring_stages(int ctas, int sms, int stage_bytes, int other_bytes) {
 }
 
 __device__ int g_int8_error;  // HELM_DEVERR_* bits of the INT8 kernels (helm_int8_linear_error)
+
+// Packed weights (helm_int8_pack_weight): W [N, K] as blocks of 16 rows x 128 k (2 KB), block
+// (t, kb) at byte ((t * KB) + kb) * 2048 with KB = ceil(K / 128), each block laid out exactly as
+// the 128-byte-swizzled TMA box lands in shared memory (row r at r * 128, 16-byte chunk c at
+// (c ^ (r & 7)) * 16), zero-padded past N and K.  A row tile's k range is then contiguous: one
+// bulk copy moves a whole stage of it.
+constexpr int kPackBlock = 16 * kBoxK;   // bytes of one packed block
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__global__ void __launch_bounds__(256) pack_weight_kernel(const int8_t *__restrict__ w, int N, int K, int KB,
+                                                          int8_t *__restrict__ out, int64_t chunks) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < chunks; i += (int64_t)gridDim.x * blockDim.x) {
+    // destination chunk i: block (t, kb), row r, stored chunk q (holding source chunk q ^ (r & 7))
+    const int q = (int)(i & 7), r = (int)((i >> 3) & 15);
+    const int64_t blk = i >> 7;
+    const int kb = (int)(blk % KB), t = (int)(blk / KB);
+    const int row = t * 16 + r, k0 = kb * kBoxK + ((q ^ (r & 7)) << 4);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < N && k0 < K) v = *reinterpret_cast<const uint4 *>(w + (int64_t)row * K + k0);
+    reinterpret_cast<uint4 *>(out)[i] = v;
+  }
+}
 
 
 // Bytes (lo, hi) of `biased` (the int8 word xor 0x80808080) as an exact 16-bit pair of the
@@ -139,7 +167,8 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
                                                             const __grid_constant__ CUtensorMap tmX,
                                                             const void *__restrict__ scale, int scale_dt,
                                                             const XT *__restrict__ bias, XT *__restrict__ y, int M,
-                                                            int N, int K, int ST, int XR, int xbox_bytes, int glu) {
+                                                            int N, int K, int ST, int XR, int xbox_bytes, int glu,
+                                                            const int8_t *__restrict__ wpk) {
   constexpr int kWBoxBytes = kBoxK * 16 * RT;
   constexpr int P = RT * MT * 128;  // floats of one warp's partial tile
   const int stage_bytes = (kCWarps * (kWBoxBytes + xbox_bytes) + 1023) & ~1023;
@@ -154,7 +183,14 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
   const int n_base = blockIdx.x * 16 * RT;
   const int m_base = blockIdx.y * 8 * MT;
   const int nst = (K + kStageK - 1) / kStageK;
-  auto wbox = [&](int slot, int bx) { return ring + (size_t)slot * stage_bytes + bx * kWBoxBytes; };
+  // Weight tile (rt, box bx) of a stage: [bx][rt] for tensor-map boxes (one box spans the CTA's
+  // 16*RT rows), [rt][bx] for packed blocks (one bulk copy per row tile spans its boxes).
+  const int rt_stride = wpk ? kCWarps * kPackBlock : kPackBlock;
+  const int bx_stride = wpk ? kPackBlock : kWBoxBytes;
+  const int KB = (K + kBoxK - 1) / kBoxK;
+  const int n_tiles = (N + 15) / 16;
+  auto wbox = [&](int slot, int bx) { return ring + (size_t)slot * stage_bytes + bx * bx_stride; };
+  auto wtile = [&](int slot, int rt) { return ring + (size_t)slot * stage_bytes + rt * rt_stride; };
   auto xbox = [&](int slot, int bx) {
     return ring + (size_t)slot * stage_bytes + kCWarps * kWBoxBytes + bx * xbox_bytes;
   };
@@ -180,11 +216,24 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
       // The weights of the first stages go out before the previous kernel has finished (they
       // are never written by a preceding kernel of a decode step); x only after it has.
       const int pre = min(ST, nst);
+      const int tiles = wpk ? max(0, min(RT, n_tiles - n_base / 16)) : RT;  // packed: tiles that exist
+      auto load_w = [&](int slot, int s, int boxes) {
+        if (wpk) {
+          for (int rt = 0; rt < tiles; ++rt)
+            bulk_load(wtile(slot, rt), wpk + ((int64_t)(n_base / 16 + rt) * KB + s * kCWarps) * kPackBlock,
+                      (uint32_t)(boxes * kPackBlock), &full_bar[slot]);
+        } else {
+          for (int bx = 0; bx < boxes; ++bx)
+            tma_load_2d(wbox(slot, bx), &tmW, &full_bar[slot], s * kStageK + bx * kBoxK, n_base);
+        }
+      };
+      auto stage_tx = [&](int boxes) {
+        return (uint32_t)(boxes * ((wpk ? tiles * kPackBlock : kWBoxBytes) + xtx));
+      };
       for (int s = 0; s < pre; ++s) {
         const int boxes = boxes_of(s);
-        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(boxes * (kWBoxBytes + xtx)));
-        for (int bx = 0; bx < boxes; ++bx)
-          tma_load_2d(wbox(s, bx), &tmW, &full_bar[s], s * kStageK + bx * kBoxK, n_base);
+        mbar_arrive_expect_tx(&full_bar[s], stage_tx(boxes));
+        load_w(s, s, boxes);
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int s = 0; s < pre; ++s)
@@ -198,11 +247,10 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
           break;
         }
         const int boxes = boxes_of(s);
-        mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(boxes * (kWBoxBytes + xtx)));
-        for (int bx = 0; bx < boxes; ++bx) {
-          tma_load_2d(wbox(slot, bx), &tmW, &full_bar[slot], s * kStageK + bx * kBoxK, n_base);
+        mbar_arrive_expect_tx(&full_bar[slot], stage_tx(boxes));
+        load_w(slot, s, boxes);
+        for (int bx = 0; bx < boxes; ++bx)
           tma_load_2d(xbox(slot, bx), &tmX, &full_bar[slot], s * kStageK + bx * kBoxK, m_base);
-        }
       }
       // drain: the copies of the last stages land before this CTA can finish
       for (int s = max(0, nst - ST); s < nst && ok; ++s)
@@ -230,7 +278,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
       break;
     }
     if (kbox < K) {
-      const uint32_t box = smem_u32(wbox(slot, warp));
+      const uint32_t box = smem_u32(wbox(slot, warp));  // row tile rt at + rt * rt_stride
       const uint32_t xb = smem_u32(xbox(slot, warp));
       // weights: rows g and g+8 of each row tile, 32 bytes each = 16-byte chunks 2j and 2j+1 of
       // the 128-byte row, stored at chunk ^ (row & 7) by the 128-byte swizzle
@@ -242,7 +290,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
           const int r = rt * 16 + g + hr * 8;
 #pragma unroll
           for (int c = 0; c < 2; ++c)
-            wv[rt][hr][c] = lds128(box + r * kBoxK + (((2 * j + c) ^ (r & 7)) << 4));
+            wv[rt][hr][c] = lds128(box + rt * rt_stride + (r - rt * 16) * kBoxK + (((2 * j + c) ^ (r & 7)) << 4));
         }
 #pragma unroll
       for (int nt = 0; nt < MT; ++nt) {
@@ -413,7 +461,7 @@ bool act_map(CUtensorMap *m, const void *x, int xdt, int M, int K, int rows) {
 
 template <typename XT, int RT, int MT>
 int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y,
-               int M, int N, int K, cudaStream_t st, int glu) {
+               int M, int N, int K, cudaStream_t st, int glu, const int8_t *wpk) {
   const int XR = M < 8 * MT ? M : 8 * MT;                          // x rows per box
   const int xbox_bytes = ((kBoxK * XR * (int)sizeof(XT)) + 127) & ~127;   // 128-byte aligned x boxes
   const int stage_bytes = (kCWarps * (kBoxK * 16 * RT + xbox_bytes) + 1023) & ~1023;
@@ -438,7 +486,8 @@ int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int s
     }
   }
   CUtensorMap wmap, xmap;
-  if (!weight_map(&wmap, w, N, K, 16 * RT) || !act_map(&xmap, x, xdt, M, K, XR))
+  if (wpk) memset(&wmap, 0, sizeof(wmap));  // unused: the packed weights move by bulk copies
+  if ((!wpk && !weight_map(&wmap, w, N, K, 16 * RT)) || !act_map(&xmap, x, xdt, M, K, XR))
     return fail(HELM_ERR_CUDA, "int8_linear: cuTensorMapEncodeTiled failed");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N + 16 * RT - 1) / (16 * RT), (M + 8 * MT - 1) / (8 * MT));
@@ -451,7 +500,7 @@ int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, xmap, scale, sdt, static_cast<const XT *>(bias),
-                                           static_cast<XT *>(y), M, N, K, ST, XR, xbox_bytes, glu);
+                                           static_cast<XT *>(y), M, N, K, ST, XR, xbox_bytes, glu, wpk);
   if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_linear: launch: %s", cudaGetErrorString(e));
   return check_launch("int8_tma_kernel");
 }
@@ -460,34 +509,34 @@ int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int s
 // at once -- 3 CTAs per SM with one tile (64 KB ring), 2 with more (96 KB ring).
 template <typename XT, int MT>
 int launch_m(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
-             int K, cudaStream_t st, int glu) {
+             int K, cudaStream_t st, int glu, const int8_t *wpk) {
   const int sms = num_sms();
   const int tiles = (N + 15) / 16;
   if (glu) {  // whole (gate, up) tile pairs per CTA
     if constexpr (MT >= 4) {
-      return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1);
+      return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1, wpk);
     } else {
-      if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1);
-      return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1);
+      if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1, wpk);
+      return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 1, wpk);
     }
   }
   if constexpr (MT >= 4) {  // wide x tiles: one row tile per CTA (register budget)
-    return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
+    return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
   } else {
-    if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
-    if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
-    if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
-    return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0);
+    if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
+    if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
+    if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
+    return launch_cfg<XT, 4, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
   }
 }
 
 template <typename XT>
 int launch(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y, int M, int N,
-           int K, cudaStream_t st, int glu) {
-  if (M <= 8) return launch_m<XT, 1>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
-  if (M <= 16) return launch_m<XT, 2>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
-  if (M <= 32) return launch_m<XT, 4>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
-  return launch_m<XT, 8>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu);
+           int K, cudaStream_t st, int glu, const int8_t *wpk = nullptr) {
+  if (M <= 8) return launch_m<XT, 1>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu, wpk);
+  if (M <= 16) return launch_m<XT, 2>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu, wpk);
+  if (M <= 32) return launch_m<XT, 4>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu, wpk);
+  return launch_m<XT, 8>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, glu, wpk);
 }
 
 int check_args(const void *x, int32_t x_dtype, const int8_t *w, const void *w_scale, int32_t scale_dtype, void *y,
@@ -529,6 +578,52 @@ extern "C" int helm_int8_linear_glu(const void *x, int32_t x_dtype, const int8_t
   cudaStream_t st = as_stream(stream);
   return x_dtype == HELM_F16 ? launch<__half>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, 2 * I, K, st, 1)
                              : launch<__nv_bfloat16>(x, x_dtype, w, w_scale, scale_dtype, bias, y, M, 2 * I, K, st, 1);
+}
+
+extern "C" int64_t helm_int8_packed_bytes(int32_t N, int32_t K) {
+  if (N < 0 || K <= 0 || K % 16) return -1;
+  return (int64_t)((N + 15) / 16) * ((K + 127) / 128) * helm::kPackBlock;
+}
+
+extern "C" int helm_int8_pack_weight(const int8_t *w, int32_t N, int32_t K, int8_t *packed, void *stream) {
+  using namespace helm;
+  if (N < 0 || K <= 0) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_pack_weight: bad sizes N=%d K=%d", N, K);
+  if (K % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_pack_weight: K=%d is not a multiple of 16", K);
+  if (N == 0) return HELM_OK;
+  if (!w || !packed) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_pack_weight: null pointer");
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(packed)) & 15)
+    return fail(HELM_ERR_INVALID_ARGUMENT, "int8_pack_weight: w and packed must be 16-byte aligned");
+  const int KB = (K + kBoxK - 1) / kBoxK;
+  const int64_t chunks = helm_int8_packed_bytes(N, K) / 16;
+  const int64_t want = (chunks + 255) / 256;
+  const int grid = (int)(want < 16 * num_sms() ? want : 16 * num_sms());
+  pack_weight_kernel<<<grid, 256, 0, as_stream(stream)>>>(w, N, K, KB, packed, chunks);
+  return check_launch("pack_weight_kernel");
+}
+
+extern "C" int helm_int8_linear_packed(const void *x, int32_t x_dtype, const int8_t *packed, const void *w_scale,
+                                       int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t N, int32_t K,
+                                       void *stream) {
+  using namespace helm;
+  const int rc = check_args(x, x_dtype, packed, w_scale, scale_dtype, y, M, N, K, "int8_linear_packed");
+  if (rc != HELM_OK || M == 0 || N == 0) return rc;
+  cudaStream_t st = as_stream(stream);
+  return x_dtype == HELM_F16 ? launch<__half>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, N, K, st, 0, packed)
+                             : launch<__nv_bfloat16>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, N, K, st, 0,
+                                                     packed);
+}
+
+extern "C" int helm_int8_linear_glu_packed(const void *x, int32_t x_dtype, const int8_t *packed, const void *w_scale,
+                                           int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t I,
+                                           int32_t K, void *stream) {
+  using namespace helm;
+  if (I < 0 || I % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_linear_glu_packed: I=%d is not a multiple of 16", I);
+  const int rc = check_args(x, x_dtype, packed, w_scale, scale_dtype, y, M, 2 * I, K, "int8_linear_glu_packed");
+  if (rc != HELM_OK || M == 0 || I == 0) return rc;
+  cudaStream_t st = as_stream(stream);
+  return x_dtype == HELM_F16
+             ? launch<__half>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, 2 * I, K, st, 1, packed)
+             : launch<__nv_bfloat16>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, 2 * I, K, st, 1, packed);
 }
 
 extern "C" int helm_int8_linear_error(int32_t *flag_out, int32_t reset) {

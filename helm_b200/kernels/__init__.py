@@ -57,30 +57,57 @@ def quantize_weight(weight: torch.Tensor, scale_dtype: Optional[torch.dtype] = N
     return q.contiguous(), scale.to(scale_dtype or weight.dtype).contiguous()
 
 
-def int8_linear(input: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+def int8_linear(input: torch.Tensor, weight, scale: torch.Tensor,
                 bias: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = (input @ weight.T) * scale + bias, weight int8 [N, K], scale [N]; CUDA tensors only."""
+    """y = (input @ weight.T) * scale + bias, weight int8 [N, K] (a row-major tensor or an
+    ops.PackedInt8), scale [N]; CUDA tensors only."""
     rows = input.numel() // input.shape[-1] if input.numel() else 0
     if rows <= INT8_KERNEL_MAX_ROWS:
         return ops.int8_linear(input, weight, scale, bias)
-    w = weight.to(input.dtype) * scale.to(input.dtype)[:, None]
+    w = weight.unpack() if isinstance(weight, ops.PackedInt8) else weight
+    w = w.to(input.dtype) * scale.to(input.dtype)[:, None]
     return F.linear(input, w, None if bias is None else bias.to(input.dtype))
 
 
-class Int8Linear(nn.Module):
-    """nn.Linear replacement holding an int8 weight [N, K] and a per-channel scale [N]."""
+class _PackedWeight:
+    """Mixin: the int8 weight lives packed (ops.PackedInt8, buffer `packed`); `weight` reads back
+    the row-major int8 [N, K] and assigning it packs."""
+
+    def _set_packed(self, pk: "ops.PackedInt8") -> None:
+        self.packed = pk.data
+        self._shape = (pk.N, pk.K)
+
+    @property
+    def pk(self) -> "ops.PackedInt8":
+        return ops.PackedInt8(self.packed, *self._shape)
+
+    @property
+    def weight(self) -> torch.Tensor:
+        return self.pk.unpack()
+
+    @weight.setter
+    def weight(self, w: torch.Tensor) -> None:
+        self._set_packed(ops.int8_pack_weight(w.contiguous()))
+
+
+class Int8Linear(_PackedWeight, nn.Module):
+    """nn.Linear replacement holding an int8 weight [N, K] (stored packed for the kernel) and a
+    per-channel scale [N]."""
 
     def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None,
                  dtype: torch.dtype = torch.bfloat16):
         super().__init__()
         self.in_features = in_features
         self.out_features = out_features
-        self.register_buffer("weight", torch.zeros((out_features, in_features), dtype=torch.int8, device=device))
+        self.register_buffer("packed", torch.zeros(0, dtype=torch.int8, device=device))
+        self._shape = (out_features, in_features)
         self.register_buffer("scale", torch.ones((out_features,), dtype=dtype, device=device))
         if bias:
             self.register_buffer("bias", torch.zeros((out_features,), dtype=dtype, device=device))
         else:
             self.bias = None
+        if device is not None and torch.device(device).type == "cuda":
+            self.weight = torch.zeros((out_features, in_features), dtype=torch.int8, device=device)
 
     @classmethod
     def from_linear(cls, linear: nn.Linear, scale_dtype: Optional[torch.dtype] = None) -> "Int8Linear":
@@ -96,23 +123,24 @@ class Int8Linear(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if x.device.type != "cuda":
             raise RuntimeError("Int8Linear runs on CUDA devices only (no CPU implementation)")
-        return int8_linear(x, self.weight, self.scale, self.bias)
+        return int8_linear(x, self.pk, self.scale, self.bias)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
                 f"bias={self.bias is not None}, int8=True")
 
 
-class Int8QKV(nn.Module):
+class Int8QKV(_PackedWeight, nn.Module):
     """q_proj, k_proj and v_proj of one attention module as one int8 weight [Nq+Nk+Nv, K] (and one
-    scale / bias vector): a decode step projects all three with one helm_int8_linear launch.  The
-    module's own q_proj / k_proj / v_proj become Int8Linear views of the fused buffers."""
+    scale / bias vector): a decode step projects all three with one INT8 launch.  The module's own
+    q_proj / k_proj / v_proj become Int8Linear views of the fused buffers (for prefill)."""
 
     def __init__(self, q: nn.Linear, k: nn.Linear, v: nn.Linear):
         super().__init__()
         parts = [quantize_weight(m.weight) for m in (q, k, v)]
         self.splits = tuple(m.out_features for m in (q, k, v))
-        self.register_buffer("weight", torch.cat([p[0] for p in parts]).contiguous())
+        self.register_buffer("packed", torch.zeros(0, dtype=torch.int8, device=q.weight.device))
+        self.weight = torch.cat([p[0] for p in parts]).contiguous()
         self.register_buffer("scale", torch.cat([p[1] for p in parts]).contiguous())
         if q.bias is not None:
             self.register_buffer("bias", torch.cat([m.bias.detach() for m in (q, k, v)]).contiguous())
@@ -120,12 +148,14 @@ class Int8QKV(nn.Module):
             self.bias = None
 
     def views(self):
-        """Int8Linear modules over the q, k and v rows of the fused buffers."""
+        """Int8Linear modules over the q, k and v rows of the fused buffers (row bounds are
+        multiples of 16, so each view is a contiguous slice of the packed blocks)."""
         out, lo = [], 0
-        K = self.weight.shape[1]
+        K = self._shape[1]
+        pk = self.pk
         for n in self.splits:
-            m = Int8Linear(K, n, bias=self.bias is not None, device=self.weight.device, dtype=self.scale.dtype)
-            m.weight = self.weight[lo:lo + n]
+            m = Int8Linear(K, n, bias=self.bias is not None, device=None, dtype=self.scale.dtype)
+            m._set_packed(pk.rows(lo, lo + n))
             m.scale = self.scale[lo:lo + n]
             if self.bias is not None:
                 m.bias = self.bias[lo:lo + n]
@@ -135,12 +165,12 @@ class Int8QKV(nn.Module):
 
     def forward(self, x: torch.Tensor):
         """(q, k, v) projections of x as views of one [..., Nq+Nk+Nv] output."""
-        y = int8_linear(x, self.weight, self.scale, self.bias)
+        y = int8_linear(x, self.pk, self.scale, self.bias)
         nq, nk, _ = self.splits
         return y[..., :nq], y[..., nq:nq + nk], y[..., nq + nk:]
 
 
-class Int8GLU(nn.Module):
+class Int8GLU(_PackedWeight, nn.Module):
     """gate_proj, up_proj and silu(gate) * up of a SwiGLU MLP as one tile-interleaved int8 weight
     [2I, K] (ops.interleave_glu_rows): decode-sized inputs run helm_int8_linear_glu (one launch, the
     activation in the epilogue); larger inputs dequantise the weight, run one dense GEMM and apply
@@ -151,7 +181,8 @@ class Int8GLU(nn.Module):
         qg, sg = quantize_weight(gate.weight)
         qu, su = quantize_weight(up.weight)
         self.I, self.K = gate.out_features, gate.in_features
-        self.register_buffer("weight", ops.interleave_glu_rows(qg, qu).contiguous())
+        self.register_buffer("packed", torch.zeros(0, dtype=torch.int8, device=gate.weight.device))
+        self.weight = ops.interleave_glu_rows(qg, qu).contiguous()
         self.register_buffer("scale", ops.interleave_glu_rows(sg, su).contiguous())
         if gate.bias is not None:
             self.register_buffer("bias", ops.interleave_glu_rows(gate.bias.detach(), up.bias.detach()).contiguous())
@@ -163,7 +194,7 @@ class Int8GLU(nn.Module):
             raise RuntimeError("Int8GLU runs on CUDA devices only (no CPU implementation)")
         rows = x.numel() // x.shape[-1] if x.numel() else 0
         if rows <= INT8_KERNEL_MAX_ROWS:
-            return ops.int8_linear_glu(x, self.weight, self.scale, self.bias)
+            return ops.int8_linear_glu(x, self.pk, self.scale, self.bias)
         w = self.weight.to(x.dtype) * self.scale.to(x.dtype)[:, None]
         y = F.linear(x, w, None if self.bias is None else self.bias.to(x.dtype))
         y = y.reshape(*x.shape[:-1], self.I // 16, 2, 16)
@@ -184,10 +215,11 @@ def _linear_ok(m, skip, name) -> bool:
 
 
 def patch_int8_linears(module: nn.Module, verbose: bool = False,
-                       skip: Iterable[str] = ("lm_head",), fuse: bool = True) -> int:
+                       skip: Iterable[str] = (), fuse: bool = True) -> int:
     """Replaces, in place, every fp16/bf16 nn.Linear child on a CUDA device whose in_features is a
-    multiple of 16 with Int8Linear; children named in `skip` are kept.  Returns how many were replaced
-    (the contract of patch_cpu_linears, helm/kernels/__init__.py:133-157).  With fuse=True, an
+    multiple of 16 with Int8Linear -- the lm_head included, as patch_cpu_linears replaces every
+    linear (helm/kernels/__init__.py:133-157); children named in `skip` are kept.  Returns how many
+    were replaced.  With fuse=True, an
     attention module's q/k/v projections share one fused weight (Int8QKV, module attribute
     `_helm_qkv`) and a SwiGLU MLP's gate/up projections become one Int8GLU (`_helm_glu`, with the
     MLP's forward patched on the instance); each still counts as its replaced linears."""

@@ -163,11 +163,73 @@ def lse_merge(partials: torch.Tensor, out: Optional[torch.Tensor] = None, out_dt
     return out
 
 
-def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
-                bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = (x @ weight.T) * scale + bias with int8 ``weight`` [N, K] and per-row ``scale`` [N]."""
-    dev = _need_cuda("int8_linear", x, weight, scale, bias)
+class PackedInt8:
+    """INT8 weights [N, K] in the packed block layout of helm_int8_pack_weight (``data``, a flat int8
+    device tensor); ``rows(lo, hi)`` is the packed weight of rows [lo, hi) (multiples of 16), a view."""
+
+    def __init__(self, data: torch.Tensor, N: int, K: int):
+        self.data, self.N, self.K = data, N, K
+        self.kb = (K + 127) // 128
+
+    @property
+    def device(self):
+        return self.data.device
+
+    @property
+    def shape(self):
+        return (self.N, self.K)
+
+    def rows(self, lo: int, hi: int) -> "PackedInt8":
+        if lo % 16 or (hi % 16 and hi != self.N):
+            raise ValueError("PackedInt8.rows: bounds must be multiples of 16")
+        blk = self.kb * 2048
+        return PackedInt8(self.data[(lo // 16) * blk:((hi + 15) // 16) * blk], hi - lo, self.K)
+
+    def unpack(self) -> torch.Tensor:
+        """The row-major int8 [N, K] weight."""
+        T = (self.N + 15) // 16
+        b = self.data.view(T, self.kb, 16, 8, 16)
+        r = torch.arange(16, device=self.data.device)[:, None]
+        c = torch.arange(8, device=self.data.device)[None, :]
+        src = (c ^ (r & 7))                       # stored chunk of logical chunk c in row r
+        b = b[:, :, r, src]                       # [T, kb, 16, 8, 16]: logical chunk order
+        return b.permute(0, 2, 1, 3, 4).reshape(T * 16, self.kb * 128)[:self.N, :self.K].contiguous()
+
+
+def int8_pack_weight(weight: torch.Tensor) -> PackedInt8:
+    """helm_int8_pack_weight of a contiguous int8 [N, K] tensor.  A weight still on the host (a
+    module quantised before it is moved) is rearranged with the same index arithmetic in torch; the
+    layout is the data's, not a compute path."""
     if weight.dtype != torch.int8 or weight.dim() != 2 or not weight.is_contiguous():
+        raise ValueError("int8_pack_weight: weight must be a contiguous int8 [N, K] tensor")
+    Nn, K = weight.shape
+    nbytes = N.lib().helm_int8_packed_bytes(Nn, K)
+    if nbytes < 0:
+        raise ValueError(f"int8_pack_weight: K={K} must be a positive multiple of 16")
+    if weight.device.type != "cuda":
+        T, KB = (Nn + 15) // 16, (K + 127) // 128
+        w = torch.zeros((T * 16, KB * 128), dtype=torch.int8)
+        w[:Nn, :K] = weight
+        b = w.view(T, 16, KB, 8, 16).permute(0, 2, 1, 3, 4)          # [T, KB, 16 rows, 8 chunks, 16]
+        r = torch.arange(16)[:, None]
+        c = torch.arange(8)[None, :]
+        b = b[:, :, r, c ^ (r & 7)]                                      # stored chunk c <- logical c ^ (r & 7)
+        return PackedInt8(b.contiguous().view(-1), Nn, K)
+    dev = weight.device
+    out = torch.empty(max(nbytes, 16), dtype=torch.int8, device=dev)
+    N.check("helm_int8_pack_weight", N.lib().helm_int8_pack_weight(weight.data_ptr(), Nn, K, out.data_ptr(),
+                                                                     _stream(dev)))
+    return PackedInt8(out[:nbytes], Nn, K)
+
+
+def int8_linear(x: torch.Tensor, weight, scale: torch.Tensor,
+                bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = (x @ weight.T) * scale + bias with int8 ``weight`` [N, K] (a row-major tensor or a
+    PackedInt8) and per-row ``scale`` [N]."""
+    packed = isinstance(weight, PackedInt8)
+    wt = weight.data if packed else weight
+    dev = _need_cuda("int8_linear", x, wt, scale, bias)
+    if not packed and (weight.dtype != torch.int8 or weight.dim() != 2 or not weight.is_contiguous()):
         raise ValueError("int8_linear: weight must be a contiguous int8 [N, K] tensor")
     Nn, K = weight.shape
     if x.shape[-1] != K:
@@ -184,18 +246,22 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
             bias = bias.to(x.dtype)
         bias = bias.contiguous()
     y = out if out is not None else torch.empty((M, Nn), dtype=x.dtype, device=dev)
-    code = N.lib().helm_int8_linear(x2.data_ptr(), dtype_code(x.dtype), weight.data_ptr(), scale.data_ptr(),
-                                    dtype_code(scale.dtype), _ptr(bias), y.data_ptr(), M, Nn, K, _stream(dev))
-    N.check("helm_int8_linear", code)
+    fn = N.lib().helm_int8_linear_packed if packed else N.lib().helm_int8_linear
+    code = fn(x2.data_ptr(), dtype_code(x.dtype), wt.data_ptr(), scale.data_ptr(), dtype_code(scale.dtype),
+              _ptr(bias), y.data_ptr(), M, Nn, K, _stream(dev))
+    N.check("helm_int8_linear_packed" if packed else "helm_int8_linear", code)
     return y.reshape(*lead, Nn)
 
 
-def int8_linear_glu(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
+def int8_linear_glu(x: torch.Tensor, weight, scale: torch.Tensor,
                     bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """helm_int8_linear_glu: silu(x @ Wg.T * sg + bg) * (x @ Wu.T * su + bu) from the tile-interleaved
-    int8 ``weight`` [2I, K] (see interleave_glu_rows) and ``scale`` / ``bias`` [2I]; returns [..., I]."""
-    dev = _need_cuda("int8_linear_glu", x, weight, scale, bias)
-    if weight.dtype != torch.int8 or weight.dim() != 2 or not weight.is_contiguous():
+    int8 ``weight`` [2I, K] (see interleave_glu_rows; a row-major tensor or a PackedInt8) and
+    ``scale`` / ``bias`` [2I]; returns [..., I]."""
+    packed = isinstance(weight, PackedInt8)
+    wt = weight.data if packed else weight
+    dev = _need_cuda("int8_linear_glu", x, wt, scale, bias)
+    if not packed and (weight.dtype != torch.int8 or weight.dim() != 2 or not weight.is_contiguous()):
         raise ValueError("int8_linear_glu: weight must be a contiguous int8 [2I, K] tensor")
     N2, K = weight.shape
     if x.shape[-1] != K or N2 % 32:
@@ -211,10 +277,10 @@ def int8_linear_glu(x: torch.Tensor, weight: torch.Tensor, scale: torch.Tensor,
     if bias is not None:
         bias = bias.to(x.dtype).contiguous()
     y = out if out is not None else torch.empty((M, N2 // 2), dtype=x.dtype, device=dev)
-    code = N.lib().helm_int8_linear_glu(x2.data_ptr(), dtype_code(x.dtype), weight.data_ptr(), scale.data_ptr(),
-                                        dtype_code(scale.dtype), _ptr(bias), y.data_ptr(), M, N2 // 2, K,
-                                        _stream(dev))
-    N.check("helm_int8_linear_glu", code)
+    fn = N.lib().helm_int8_linear_glu_packed if packed else N.lib().helm_int8_linear_glu
+    code = fn(x2.data_ptr(), dtype_code(x.dtype), wt.data_ptr(), scale.data_ptr(), dtype_code(scale.dtype),
+              _ptr(bias), y.data_ptr(), M, N2 // 2, K, _stream(dev))
+    N.check("helm_int8_linear_glu_packed" if packed else "helm_int8_linear_glu", code)
     return y.reshape(*lead, N2 // 2)
 
 
@@ -298,6 +364,35 @@ def decode_prologue(q_in: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor
         p.cs_dtype = N.F32
     p.do_append = 1 if do_append else 0
     N.check("helm_decode_prologue", N.lib().helm_decode_prologue(ctypes.byref(p), _stream(dev)))
+
+
+def kv_write_pages(K: torch.Tensor, V: torch.Tensor, k_base: torch.Tensor, v_base: torch.Tensor, pages, *,
+                   page_stride: int, head_stride: int, num_pool_pages: int, page_size: int,
+                   table=None, error_flag: Optional[torch.Tensor] = None) -> None:
+    """helm_kv_write_pages: K / V [1, Hkv, S, D] (one sequence; head and token strides free, dims
+    contiguous) chunked into pool slots; pages = [(slot, first token, tokens), ...].  table:
+    optional (page_table_row, page_used_row, num_pages_word, first_index) device tensors/int."""
+    import numpy as np
+    dev = _need_cuda("kv_write_pages", K, V, k_base, v_base)
+    if K.dim() != 4 or K.shape[0] != 1 or K.shape != V.shape:
+        raise ValueError("kv_write_pages: K and V must be [1, Hkv, S, D] of one shape")
+    if K.stride(-1) != 1 or V.stride(-1) != 1 or K.stride(1) != V.stride(1) or K.stride(2) != V.stride(2):
+        K, V = K.contiguous(), V.contiguous()
+    arr = np.ascontiguousarray(np.asarray(pages, dtype=np.int32).reshape(-1, 3))
+    p = N.KVPrefillParams()
+    p.k_src, p.v_src, p.src_dtype = K.data_ptr(), V.data_ptr(), dtype_code(K.dtype)
+    p.src_head_stride, p.src_tok_stride = K.stride(1), K.stride(2)
+    p.k_base, p.v_base = k_base.data_ptr(), v_base.data_ptr()
+    p.page_stride, p.head_stride = int(page_stride), int(head_stride)
+    p.num_pool_pages, p.kv_dtype = int(num_pool_pages), dtype_code(k_base.dtype)
+    p.Hkv, p.D, p.P = K.shape[1], K.shape[3], int(page_size)
+    p.pages, p.count = arr.ctypes.data, len(arr)
+    if table is not None:
+        pt, pu, npg, first = table
+        p.page_table, p.page_used, p.num_pages = pt.data_ptr(), pu.data_ptr(), npg.data_ptr()
+        p.page_table_stride, p.first_index = pt.shape[-1], int(first)
+    p.error_flag = _ptr(error_flag)
+    N.check("helm_kv_write_pages", N.lib().helm_kv_write_pages(ctypes.byref(p), _stream(dev)))
 
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:

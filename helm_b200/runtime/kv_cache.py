@@ -413,8 +413,10 @@ class KVCacheManager:
 
 
 class _PrefillWrites:
-    """Prefill chunks waiting to be written: pages in consecutive slots of one store are written
-    with one copy per K and V (a fresh pool hands out consecutive slots), others one by one."""
+    """Prefill chunks waiting to be written.  Store-backed pages on the prompt's CUDA device are
+    written by one helm_kv_write_pages launch per flush (every chunk's slot in the launch's page
+    list); other pages (host stores, loose tensors) with slab copies, runs of consecutive slots
+    with one copy per K and V."""
 
     def __init__(self, K: torch.Tensor, V: torch.Tensor):
         self.K, self.V = K, V
@@ -431,6 +433,20 @@ class _PrefillWrites:
     def flush(self) -> None:
         items, self.items = self.items, []
         self.ids = set()
+        K = self.K
+        if K.device.type == "cuda" and items:
+            dev_items = [it for it in items if it[0].has_store() and it[0].store.device == K.device
+                         and it[0].store.dtype == K.dtype]
+            if dev_items:
+                st = dev_items[0][0].store
+                if all(it[0].store is st for it in dev_items):
+                    from .. import ops
+                    kb, vb = st.base_ptrs()
+                    ops.kv_write_pages(K, self.V, kb, vb, [(pg.slot, start, n) for pg, start, n in dev_items],
+                                       page_stride=st.page_elems, head_stride=st.head_stride,
+                                       num_pool_pages=st.capacity, page_size=st.P)
+                    done = set(id(it[0]) for it in dev_items)
+                    items = [it for it in items if id(it[0]) not in done]
         i = 0
         while i < len(items):
             page, start, n = items[i]

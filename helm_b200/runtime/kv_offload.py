@@ -11,6 +11,8 @@ SDPA (kv_offload.py:201-214 etc.), as in the reference.
 """
 from __future__ import annotations
 
+import ctypes
+
 import math
 from dataclasses import dataclass
 from typing import Optional
@@ -276,14 +278,53 @@ def _append_batch(batch: DecodeBatch, l: int, k, v, all_gpu: bool, store, dev, p
 
 def _attend_batch(batch: DecodeBatch, l: int, q3, scale, store, mixed: bool, out, out_record, exchange=None):
     if not mixed:
-        k_base, v_base = store.base_ptrs()
-        ops.paged_decode_attention(q3, k_base, v_base, batch.table[l], batch.used[l], batch.npages[l],
-                                   num_kv_heads=store.Hkv, page_size=store.P, page_stride=store.page_elems,
-                                   head_stride=store.head_stride, num_pool_pages=store.capacity, scale=scale,
-                                   max_pages=batch.width, out=out, out_record=out_record,
-                                   error_flag=batch.error_flag, exchange=exchange)
+        _attend_cached(batch, l, q3, scale, store, out, out_record, exchange)
         return
     _decode_mixed(batch, l, q3, scale, out, store, out_record=out_record, exchange=exchange)
+
+
+def _attend_cached(batch: DecodeBatch, l: int, q3, scale, store, out, out_record, exchange):
+    """One helm_paged_attn_decode call over the batch's device tables.  The parameter block of each
+    layer is built once and kept on the batch (with one workspace shared by the layers) while the
+    pool, the tables and the shapes stay the same; a call then only sets q, the outputs and the
+    scale."""
+    cache = batch.__dict__.setdefault("_attn_params", {})
+    key = (store.slab.data_ptr(), store.capacity, batch.table.data_ptr(), batch.width, tuple(q3.shape), q3.dtype,
+           None if out is None else out.dtype, out_record is None,
+           None if exchange is None else ctypes.addressof(exchange.contents))
+    ent = cache.get(l)
+    ws = batch.__dict__.get("_attn_ws")
+    if ent is None or ent[0] != key or (ent[2] is not None and ent[2] != ws.data_ptr()):
+        k_base, v_base = store.base_ptrs()
+        p = ops.make_attn_params(q3, k_base, v_base, batch.table[l], batch.used[l], batch.npages[l],
+                                 num_kv_heads=store.Hkv, page_size=store.P, page_stride=store.page_elems,
+                                 head_stride=store.head_stride, num_pool_pages=store.capacity, scale=scale,
+                                 max_pages=batch.width, out=out, out_record=out_record,
+                                 error_flag=batch.error_flag)
+        if exchange is not None:
+            p.exchange = exchange
+        lib = N.lib()
+        S = ctypes.c_int32(0)
+        need = lib.helm_paged_attn_workspace_bytes(ctypes.byref(p), ctypes.byref(S))
+        if need < 0:
+            N.check("helm_paged_attn_workspace_bytes", N.ERR_INVALID_ARGUMENT)
+        p.num_splits = S.value
+        ws_ptr = None
+        if need > 0:
+            # one workspace per batch, shared by the layers' calls (they run in stream order)
+            if ws is None or ws.numel() * 4 < need:
+                ws = torch.empty((need + 3) // 4, dtype=torch.float32, device=q3.device)
+                batch._attn_ws = ws
+            p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel() * 4
+            ws_ptr = ws.data_ptr()
+        ent = (key, p, ws_ptr, ctypes.byref(p), lib.helm_paged_attn_decode)
+        cache[l] = ent
+    p = ent[1]
+    p.q = q3.data_ptr()
+    p.out = None if out is None else out.data_ptr()
+    p.out_record = None if out_record is None else out_record.data_ptr()
+    p.scale = scale
+    N.check("helm_paged_attn_decode", ent[4](ent[3], torch.cuda.current_stream(q3.device).cuda_stream))
 
 
 def _decode_mixed(batch: DecodeBatch, l: int, q3, scale, out, store, out_record=None, exchange=None):

@@ -236,6 +236,30 @@ int helm_int8_linear_glu(const void *x, int32_t x_dtype, const int8_t *w,
                          const void *bias, void *y, int32_t M, int32_t I,
                          int32_t K, void *stream);
 
+/* Packed INT8 weights.  helm_int8_pack_weight rewrites w [N, K] int8 row-major
+ * (K a multiple of 16, both pointers 16-byte aligned) into `packed`, of
+ * helm_int8_packed_bytes(N, K) bytes (-1 for bad sizes): blocks of 16 rows x
+ * 128 k, block (t, kb) at byte (t * ceil(K/128) + kb) * 2048, each block in
+ * the 128-byte-swizzled order the kernel reads (row r at r*128, 16-byte chunk
+ * c at (c ^ (r & 7)) * 16), zero past N and K.  One row tile's k range is then
+ * contiguous in memory, so the kernel streams it with one bulk copy per stage
+ * instead of one 2-D box per 128 k.  helm_int8_linear_packed and
+ * helm_int8_linear_glu_packed are helm_int8_linear / helm_int8_linear_glu on
+ * such weights (same results bit for bit; the GLU row interleaving is applied
+ * before packing).  No counterpart in the reference (a storage layout of the
+ * INT8 weights that replace its fp16 ones). */
+int64_t helm_int8_packed_bytes(int32_t N, int32_t K);
+int helm_int8_pack_weight(const int8_t *w, int32_t N, int32_t K, int8_t *packed,
+                          void *stream);
+int helm_int8_linear_packed(const void *x, int32_t x_dtype, const int8_t *packed,
+                            const void *w_scale, int32_t scale_dtype,
+                            const void *bias, void *y, int32_t M, int32_t N,
+                            int32_t K, void *stream);
+int helm_int8_linear_glu_packed(const void *x, int32_t x_dtype,
+                                const int8_t *packed, const void *w_scale,
+                                int32_t scale_dtype, const void *bias, void *y,
+                                int32_t M, int32_t I, int32_t K, void *stream);
+
 /* HELM_DEVERR_* bits raised by the INT8 kernels since the last reset (a bounded
  * wait of the weight pipeline that gave up: HELM_DEVERR_TIMEOUT; the rows of
  * that CTA are then left unwritten).  Synchronises with the device; reset != 0
@@ -286,6 +310,37 @@ typedef struct {
 } helm_kv_append_params;
 
 int helm_kv_append(const helm_kv_append_params *p, void *stream);
+
+/* ---- Prefill page writes ---------------------------------------------------- */
+/*
+ * Replaces the per-page chunk copies of KVCacheManager.append_prefill
+ * (helm/runtime/kv_cache.py:55-85): writes `count` page-sized chunks of a
+ * prompt's K/V into the pool in one launch.  k_src / v_src hold one sequence's
+ * K and V, element (kv head h, token t, dim d) at h*src_head_stride +
+ * t*src_tok_stride + d (src_dtype, converted to kv_dtype).  pages is a HOST
+ * array int32 [count][3] of {pool slot, first source token, tokens} (tokens <=
+ * P); chunk i lands in tokens 0.. of its slot.  With page_table non-null (one
+ * sequence's device row: page_table / page_used of page_table_stride entries
+ * and its num_pages word), entry first_index + i is set to {slot, tokens} and
+ * num_pages is raised to first_index + count.  Ids are checked on the host.
+ */
+typedef struct {
+  const void *k_src, *v_src;
+  int32_t src_dtype;
+  int64_t src_head_stride, src_tok_stride;
+  void *k_base, *v_base;
+  int64_t page_stride, head_stride;
+  int32_t num_pool_pages;
+  int32_t kv_dtype;
+  int32_t Hkv, D, P;
+  const int32_t *pages;   /* host [count][3] */
+  int32_t count;
+  int32_t *page_table, *page_used, *num_pages;  /* optional device table row */
+  int32_t page_table_stride, first_index;
+  int32_t *error_flag;
+} helm_kv_prefill_params;
+
+int helm_kv_write_pages(const helm_kv_prefill_params *p, void *stream);
 
 /* ---- Decode prologue (fused) ---------------------------------------------- */
 /*

@@ -82,7 +82,7 @@ def test_errors_are_reported_without_a_gpu():
 
 STRUCTS = [("helm_shard_exchange", "ShardExchange"), ("helm_paged_attn_params", "PagedAttnParams"),
            ("helm_kv_append_params", "KVAppendParams"), ("helm_decode_prologue_params", "DecodePrologueParams"),
-           ("helm_gather_merge_params", "GatherMergeParams")]
+           ("helm_gather_merge_params", "GatherMergeParams"), ("helm_kv_prefill_params", "KVPrefillParams")]
 
 
 def test_ctypes_layouts_match_the_compiled_header(tmp_path):
@@ -124,3 +124,31 @@ def test_move_pages_checks_ids_before_touching_memory():
     assert code == N.ERR_INVALID_ARGUMENT
     assert b"source page 5" in lib.helm_last_error()
     assert n.value == 0
+
+
+def test_packed_layout_sizes_and_unpack_on_cpu():
+    """helm_int8_packed_bytes and PackedInt8.unpack (torch index arithmetic, no GPU): a weight packed
+    by a plain-Python restatement of the documented layout unpacks to itself."""
+    import numpy as np
+    import torch
+    from helm_b200 import ops
+    lib = N.lib()
+    assert lib.helm_int8_packed_bytes(33, 144) == 3 * 2 * 2048
+    assert lib.helm_int8_packed_bytes(16, 24) == -1
+    rng = np.random.default_rng(0)
+    Nn, K = 37, 272
+    w = rng.integers(-127, 128, size=(Nn, K), dtype=np.int8)
+    T, KB = -(-Nn // 16), -(-K // 128)
+    packed = np.zeros(T * KB * 2048, dtype=np.int8)
+    for t in range(T):
+        for kb in range(KB):
+            for r in range(16):
+                for c in range(8):
+                    row, k0 = 16 * t + r, 128 * kb + 16 * (c ^ (r & 7))
+                    if row < Nn and k0 < K:
+                        off = (t * KB + kb) * 2048 + r * 128 + c * 16
+                        packed[off:off + 16] = w[row, k0:k0 + 16]
+    pk = ops.PackedInt8(torch.from_numpy(packed), Nn, K)
+    assert torch.equal(pk.unpack(), torch.from_numpy(w))
+    assert torch.equal(ops.int8_pack_weight(torch.from_numpy(w)).data, torch.from_numpy(packed))
+    assert torch.equal(pk.rows(16, 37).unpack(), torch.from_numpy(w[16:]))

@@ -152,3 +152,32 @@ def test_glu_rejects_ragged_intermediate(cuda):
     with pytest.raises((HelmError, ValueError)):
         ops.int8_linear_glu(torch.zeros(1, 64, dtype=torch.float16, device=cuda), w,
                             torch.ones(48, dtype=torch.float16, device=cuda))
+
+
+@pytest.mark.parametrize("N,K", [(12288, 4096), (4096, 12288), (6144, 4096), (333, 528), (77, 16), (96, 4112),
+                                 (20000, 4096)])
+@pytest.mark.parametrize("M", [1, 8, 9, 33, 64])
+@pytest.mark.parametrize("xdtype", [torch.float16, torch.bfloat16])
+def test_packed_equals_rowmajor(N, K, M, xdtype, cuda):
+    """helm_int8_linear_packed on helm_int8_pack_weight's layout gives the row-major kernel's
+    result bit for bit (same MMAs in the same order), including ragged N and K tails."""
+    from helm_b200 import ops
+    w, s, x = _inputs(M, N, K, seed=N + 3 * K + M, xdtype=xdtype)
+    wd, sd, xd = torch.from_numpy(w).to(cuda), torch.from_numpy(s).to(cuda), x.to(cuda)
+    bias = torch.randn(N, dtype=torch.float32).to(xdtype).to(cuda)
+    pk = ops.int8_pack_weight(wd)
+    assert torch.equal(pk.unpack(), wd)
+    assert torch.equal(ops.int8_linear(xd, pk, sd, bias), ops.int8_linear(xd, wd, sd, bias))
+    assert ops.int8_linear_error() == 0
+
+
+@pytest.mark.parametrize("M", [1, 9, 64])
+def test_packed_glu_equals_rowmajor(M, cuda):
+    from helm_b200 import ops
+    rng = np.random.default_rng(M)
+    I, K = 1024, 2048
+    w = torch.from_numpy(rng.integers(-127, 128, size=(2 * I, K), dtype=np.int8)).to(cuda)
+    s = torch.from_numpy(rng.uniform(0.001, 0.02, size=(2 * I,)).astype(np.float16)).to(cuda)
+    x = torch.randn(M, K, dtype=torch.bfloat16, device=cuda) / 8
+    pk = ops.int8_pack_weight(w)
+    assert torch.equal(ops.int8_linear_glu(x, pk, s), ops.int8_linear_glu(x, w, s))

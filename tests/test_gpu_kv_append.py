@@ -62,3 +62,55 @@ def test_device_directed_appends_across_page_boundary(cuda):
                       spare_pages=spare, spare_next=nxt, error_flag=flag)
     from helm_b200 import _native as N
     assert flag.item() & N.DEVERR_APPEND_FULL
+
+
+@pytest.mark.parametrize("src_dtype", [torch.bfloat16, torch.float32])
+def test_kv_write_pages_chunks_and_table(src_dtype, cuda):
+    """helm_kv_write_pages: a prompt's K/V (strided as the patched forward hands them over) cut
+    into 64-token chunks written to scattered pool slots in one launch, the last chunk partial,
+    plus the device page-table row; bytewise against torch indexing."""
+    from helm_b200 import ops
+    Hkv, D, P, S = 4, 128, 64, 64 * 9 + 23
+    g = torch.Generator(device=cuda).manual_seed(9)
+    kv = torch.randn((1, S, 2 * Hkv, D), generator=g, device=cuda).to(src_dtype)
+    K = kv[:, :, :Hkv].transpose(1, 2)            # [1, Hkv, S, D], token stride 2*Hkv*D
+    V = kv[:, :, Hkv:].transpose(1, 2)
+    pool = torch.zeros((40, 2, Hkv, P, D), dtype=torch.bfloat16, device=cuda)
+    slots = torch.randperm(40, generator=torch.Generator().manual_seed(3))[:10].tolist()
+    pages = [(sl, 64 * i, min(64, S - 64 * i)) for i, sl in enumerate(slots)]
+    pt = torch.full((16,), -1, dtype=torch.int32, device=cuda)
+    pu = torch.zeros(16, dtype=torch.int32, device=cuda)
+    npg = torch.tensor([2], dtype=torch.int32, device=cuda)
+    ops.kv_write_pages(K, V, pool[:, 0], pool[:, 1], pages, page_stride=2 * Hkv * P * D, head_stride=P * D,
+                       num_pool_pages=40, page_size=P, table=(pt, pu, npg, 2))
+    torch.cuda.synchronize()
+    for sl, t0, n in pages:
+        assert torch.equal(pool[sl, 0, :, :n], K[0, :, t0:t0 + n].to(torch.bfloat16))
+        assert torch.equal(pool[sl, 1, :, :n], V[0, :, t0:t0 + n].to(torch.bfloat16))
+    assert pt[2:12].tolist() == slots and pt[:2].tolist() == [-1, -1]
+    assert pu[2:12].tolist() == [n for _, _, n in pages]
+    assert int(npg.item()) == 12
+    untouched = [i for i in range(40) if i not in slots]
+    assert torch.count_nonzero(pool[untouched]).item() == 0
+
+
+def test_append_prefill_uses_one_launch_per_call(cuda):
+    """KVCacheManager.append_prefill on a CUDA allocator: every page's data lands in its slot (one
+    helm_kv_write_pages launch per flush), for a fresh pool and for one with recycled slots."""
+    from helm_b200.runtime import KVAllocator, KVCacheManager
+    alloc = KVAllocator(num_layers=2, num_kv_heads=2, head_dim=128, page_size=64, dtype=torch.bfloat16)
+    mgr = KVCacheManager(alloc, gpu_high_watermark_bytes=1 << 40)
+    g = torch.Generator(device=cuda).manual_seed(1)
+    K = torch.randn((1, 2, 64 * 5 + 7, 128), generator=g, device=cuda).to(torch.bfloat16)
+    V = torch.randn((1, 2, 64 * 5 + 7, 128), generator=g, device=cuda).to(torch.bfloat16)
+    mgr.append_prefill(0, K, V)
+    mgr.clear()                                   # pages back to the pools: slots get reused
+    mgr.append_prefill(1, K[:, :, :200], V[:, :, :200])
+    mgr.append_prefill(1, K[:, :, 200:], V[:, :, 200:])
+    torch.cuda.synchronize()
+    pages = mgr.iterate_layer_pages(1)
+    assert sum(p.used_tokens for p in pages) == K.shape[2]
+    for p in pages:
+        t0, u = p.start_token, p.used_tokens
+        assert torch.equal(p.k_tensor[0, :, :u], K[0, :, t0:t0 + u])
+        assert torch.equal(p.v_tensor[0, :, :u], V[0, :, t0:t0 + u])

@@ -85,11 +85,11 @@ def test_patch_tiny_qwen3_and_decode_with_offload():
     torch.manual_seed(0)
     model = transformers.Qwen3ForCausalLM(cfg).cuda().to(torch.bfloat16).eval()
     n = K.patch_int8_linears(model)
-    assert n == 2 * 7  # q, k, v, o, gate, up, down per layer; lm_head kept
+    assert n == 2 * 7 + 1  # q, k, v, o, gate, up, down per layer, and the lm_head
     assert isinstance(model.model.layers[0].self_attn.q_proj, K.Int8Linear)
     assert isinstance(model.model.layers[0].self_attn._helm_qkv, K.Int8QKV)
     assert isinstance(model.model.layers[0].mlp._helm_glu, K.Int8GLU)
-    assert isinstance(model.lm_head, nn.Linear)
+    assert isinstance(model.lm_head, K.Int8Linear)
     torch.manual_seed(4)
     ids = torch.randint(0, 320, (2, 140), device="cuda")
     ref = _reference_logits(model, ids)[:, 99:]     # int8 model, torch attention
