@@ -125,6 +125,7 @@ SIGNATURES = [
     ("helm_int8_pack_weight", _c.c_int, [_p, _i32, _i32, _p, _p]),
     ("helm_int8_linear_packed", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
     ("helm_int8_linear_glu_packed", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
+    ("helm_int8_gemm_packed", _c.c_int, [_p, _i32, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _p]),
     ("helm_int8_linear_error", _c.c_int, [_p, _i32]),
     ("helm_kv_append", _c.c_int, [_c.POINTER(KVAppendParams), _p]),
     ("helm_decode_prologue", _c.c_int, [_c.POINTER(DecodePrologueParams), _p]),

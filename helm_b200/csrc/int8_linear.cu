@@ -557,6 +557,8 @@ int check_args(const void *x, int32_t x_dtype, const int8_t *w, const void *w_sc
 }  // namespace
 }  // namespace helm
 
+#include "int8_gemm_tc.cuh"
+
 extern "C" int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w, const void *w_scale,
                                 int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t N, int32_t K,
                                 void *stream) {

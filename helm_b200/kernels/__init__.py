@@ -10,8 +10,8 @@ int8 weights and one scale per output channel instead of fp16 weights.
 
 Quantisation is symmetric per output channel: scale[n] = max_k |W[n, k]| / 127,
 W_q = round(W / scale) clipped to [-127, 127].  Decode-sized inputs
-(rows <= 64 of x) run the INT8 kernel; larger (prefill) inputs dequantise the
-weight to the activation dtype and use a dense GEMM.
+(rows <= 64 of x) run the INT8 GEMV kernel; larger (prefill) inputs run the
+tcgen05 INT8 GEMM (helm_int8_gemm_packed) on the same packed weights.
 
 Projections that read the same input are fused (fuse=True, the default):
 an attention module's q_proj / k_proj / v_proj share one int8 weight, so a
@@ -64,8 +64,9 @@ def int8_linear(input: torch.Tensor, weight, scale: torch.Tensor,
     rows = input.numel() // input.shape[-1] if input.numel() else 0
     if rows <= INT8_KERNEL_MAX_ROWS:
         return ops.int8_linear(input, weight, scale, bias)
-    w = weight.unpack() if isinstance(weight, ops.PackedInt8) else weight
-    w = w.to(input.dtype) * scale.to(input.dtype)[:, None]
+    if isinstance(weight, ops.PackedInt8):
+        return ops.int8_linear(input, weight, scale, bias, gemm=True)   # tcgen05 GEMM
+    w = weight.to(input.dtype) * scale.to(input.dtype)[:, None]
     return F.linear(input, w, None if bias is None else bias.to(input.dtype))
 
 
@@ -173,7 +174,7 @@ class Int8QKV(_PackedWeight, nn.Module):
 class Int8GLU(_PackedWeight, nn.Module):
     """gate_proj, up_proj and silu(gate) * up of a SwiGLU MLP as one tile-interleaved int8 weight
     [2I, K] (ops.interleave_glu_rows): decode-sized inputs run helm_int8_linear_glu (one launch, the
-    activation in the epilogue); larger inputs dequantise the weight, run one dense GEMM and apply
+    activation in the epilogue); larger inputs run the tcgen05 GEMM over both halves and apply
     silu(gate) * up in the activation dtype, as the unfused MLP does."""
 
     def __init__(self, gate: nn.Linear, up: nn.Linear):
@@ -195,8 +196,7 @@ class Int8GLU(_PackedWeight, nn.Module):
         rows = x.numel() // x.shape[-1] if x.numel() else 0
         if rows <= INT8_KERNEL_MAX_ROWS:
             return ops.int8_linear_glu(x, self.pk, self.scale, self.bias)
-        w = self.weight.to(x.dtype) * self.scale.to(x.dtype)[:, None]
-        y = F.linear(x, w, None if self.bias is None else self.bias.to(x.dtype))
+        y = ops.int8_linear(x, self.pk, self.scale, self.bias, gemm=True)   # tcgen05 GEMM, [.., 2I]
         y = y.reshape(*x.shape[:-1], self.I // 16, 2, 16)
         return (F.silu(y[..., 0, :]) * y[..., 1, :]).reshape(*x.shape[:-1], self.I)
 

@@ -223,10 +223,14 @@ def int8_pack_weight(weight: torch.Tensor) -> PackedInt8:
 
 
 def int8_linear(x: torch.Tensor, weight, scale: torch.Tensor,
-                bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                gemm: bool = False) -> torch.Tensor:
     """y = (x @ weight.T) * scale + bias with int8 ``weight`` [N, K] (a row-major tensor or a
-    PackedInt8) and per-row ``scale`` [N]."""
+    PackedInt8) and per-row ``scale`` [N].  gemm=True (PackedInt8 only) runs the tcgen05 GEMM
+    (helm_int8_gemm_packed) instead of the GEMV kernel."""
     packed = isinstance(weight, PackedInt8)
+    if gemm and not packed:
+        raise ValueError("int8_linear: the tensor-core GEMM takes packed weights")
     wt = weight.data if packed else weight
     dev = _need_cuda("int8_linear", x, wt, scale, bias)
     if not packed and (weight.dtype != torch.int8 or weight.dim() != 2 or not weight.is_contiguous()):
@@ -246,10 +250,11 @@ def int8_linear(x: torch.Tensor, weight, scale: torch.Tensor,
             bias = bias.to(x.dtype)
         bias = bias.contiguous()
     y = out if out is not None else torch.empty((M, Nn), dtype=x.dtype, device=dev)
-    fn = N.lib().helm_int8_linear_packed if packed else N.lib().helm_int8_linear
-    code = fn(x2.data_ptr(), dtype_code(x.dtype), wt.data_ptr(), scale.data_ptr(), dtype_code(scale.dtype),
-              _ptr(bias), y.data_ptr(), M, Nn, K, _stream(dev))
-    N.check("helm_int8_linear_packed" if packed else "helm_int8_linear", code)
+    lib = N.lib()
+    name = "helm_int8_gemm_packed" if gemm else "helm_int8_linear_packed" if packed else "helm_int8_linear"
+    code = getattr(lib, name)(x2.data_ptr(), dtype_code(x.dtype), wt.data_ptr(), scale.data_ptr(),
+                              dtype_code(scale.dtype), _ptr(bias), y.data_ptr(), M, Nn, K, _stream(dev))
+    N.check(name, code)
     return y.reshape(*lead, Nn)
 
 

@@ -260,6 +260,21 @@ int helm_int8_linear_glu_packed(const void *x, int32_t x_dtype,
                                 int32_t scale_dtype, const void *bias, void *y,
                                 int32_t M, int32_t I, int32_t K, void *stream);
 
+/* Prefill-sized INT8 weight-only GEMM on the tcgen05 tensor cores: the result
+ * of helm_int8_linear_packed for any M (meant for M > 64, where the GEMV's
+ * one-pass design stops paying), computed as a dense contraction: 128 x 128
+ * output tiles, the packed int8 weight converted exactly to x's 16-bit type
+ * in shared memory, x and the converted weight read by tcgen05.mma from
+ * shared memory, fp32 accumulators in tensor memory, scale and bias applied
+ * in the epilogue.  Same arguments and alignment rules as
+ * helm_int8_linear_packed.  Replaces the dequantise-then-dense-GEMM prefill
+ * path of the INT8 linear (no counterpart in the reference, whose linear is
+ * the fp16 GEMV helm/kernels/fp16_gemv.cpp:105-157). */
+int helm_int8_gemm_packed(const void *x, int32_t x_dtype, const int8_t *packed,
+                          const void *w_scale, int32_t scale_dtype,
+                          const void *bias, void *y, int32_t M, int32_t N,
+                          int32_t K, void *stream);
+
 /* HELM_DEVERR_* bits raised by the INT8 kernels since the last reset (a bounded
  * wait of the weight pipeline that gave up: HELM_DEVERR_TIMEOUT; the rows of
  * that CTA are then left unwritten).  Synchronises with the device; reset != 0
