@@ -753,6 +753,7 @@ def config2_line(args, rank, world, dev):
                           "copies": copies, "rowmajor_us": round(ms_rowmajor * 1e3, 3),
                           "rowmajor_gbs": round(nbytes / (ms_rowmajor * 1e-3) / 1e9, 1)})
             del w, wp, x, y, mod
+    prefill = c2_prefill_gemm(args, dev, world) if not (args.shape or args.rows) else None
     clk = clocks.stop(t_load0, time.time())
     if rank == 0:
         hbm_peak, peak_kind = peaks()
@@ -780,10 +781,70 @@ def config2_line(args, rank, world, dev):
                     "h2d_bytes_per_step": e2e_bytes_in, "d2h_bytes_per_step": e2e_bytes_out, "ms_per_step": e2e_ms,
                     "api": "helm_b200.kernels.Int8Linear.forward per call, x from pinned host, y read back"},
             "gpu_launches": len(cases) * 1,
+            "prefill_gemm": prefill,
             "clocks": clk,
         }
         return line
     return None
+
+
+def bf16_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def c2_prefill_gemm(args, dev, world, M=4096):
+    """The same three weights at a prefill-sized M: the tcgen05 INT8 GEMM (helm_int8_gemm_packed,
+    what Int8Linear runs for more than 64 rows) against dequantising the weight and calling cuBLAS
+    (torch.nn.functional.linear), both timed with CUDA events over CUDA graphs of repeated calls."""
+    import torch.nn.functional as F
+    from helm_b200 import ops
+    stream = torch.cuda.current_stream(dev)
+    peak, kind = bf16_peak()
+    out = []
+    for (Nn, K) in C2_SHAPES:
+        g = torch.Generator(device=dev).manual_seed(5)
+        w = torch.randint(-127, 128, (Nn, K), generator=g, device=dev, dtype=torch.int8)
+        s = (torch.rand(Nn, generator=g, device=dev) * 0.019 + 0.001).to(torch.bfloat16)
+        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        pk = ops.int8_pack_weight(w)
+        y = torch.empty((M, Nn), dtype=torch.bfloat16, device=dev)
+
+        def ours():
+            ops.int8_linear(x, pk, s, out=y, gemm=True)
+
+        def dequant_cublas():
+            F.linear(x, w.to(torch.bfloat16) * s[:, None])
+
+        res = {"N": Nn, "K": K, "M": M}
+        for name, fn in (("tcgen05", ours), ("dequant_cublas", dequant_cublas)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(10):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(3):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / 30
+            tf = 2.0 * M * Nn * K / (ms * 1e-3) / 1e12
+            res[name] = {"us": round(ms * 1e3, 2), "tflops": round(tf, 1), "frac": round(tf / peak, 3)}
+            del graph
+        out.append(res)
+        del w, x, pk, y
+    return {"bound": "tensor", "peak_tflops": peak, "peak_kind": kind, "cases": out,
+            "how": "bf16 x, int8 weights; CUDA graph of 10 calls replayed 3 times; 2*M*N*K flops"}
 
 
 def c2_reference_time(min_seconds=2.0):

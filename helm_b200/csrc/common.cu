@@ -2,6 +2,7 @@
 #include "common.cuh"
 #include "tma.cuh"
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -43,6 +44,14 @@ int num_sms() {
     cache[dev] = n > 0 ? n : 148;
   }
   return cache[dev];
+}
+
+bool nvtx_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("HELM_B200_NVTX");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {

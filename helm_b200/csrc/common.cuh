@@ -9,6 +9,8 @@
 #include <cstdarg>
 #include <utility>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/helm_b200.h"
 
 namespace helm {
@@ -33,6 +35,22 @@ inline int dtype_size(int dt) {
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
 int num_sms();  // SM count of the current device (cached per device)
+
+// NVTX range around one C-ABI call (named after the entry point), recorded when the environment
+// sets HELM_B200_NVTX=1 (read once): the kernel families then show as named ranges in a profiler
+// timeline.  Off, it costs one branch.
+bool nvtx_enabled();
+struct NvtxRange {
+  bool on;
+  explicit NvtxRange(const char *name) : on(nvtx_enabled()) {
+    if (on) nvtxRangePushA(name);
+  }
+  ~NvtxRange() {
+    if (on) nvtxRangePop();
+  }
+  NvtxRange(const NvtxRange &) = delete;
+  NvtxRange &operator=(const NvtxRange &) = delete;
+};
 
 // ---------------------------------------------------------------------------
 // Element conversions.

@@ -172,6 +172,7 @@ extern "C" int64_t helm_gather_merge_state_bytes(int32_t world, int32_t rows, in
 }
 
 extern "C" int helm_gather_merge(const helm_gather_merge_params *p, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_gather_merge");
   using namespace helm;
   if (!p) return fail(HELM_ERR_INVALID_ARGUMENT, "gather_merge: params is null");
   if (p->world < 1 || p->world > HELM_MAX_RANKS || p->rank < 0 || p->rank >= p->world || p->rows < 0 || p->D <= 0)
@@ -210,6 +211,7 @@ extern "C" int helm_gather_merge(const helm_gather_merge_params *p, void *stream
 // ---- CUDA IPC helpers --------------------------------------------------------------------
 
 extern "C" int helm_ipc_export(const void *ptr, void *handle_out, int64_t *offset_out) {
+  helm::NvtxRange nvtx_range_("helm_ipc_export");
   using namespace helm;
   if (!ptr || !handle_out || !offset_out) return fail(HELM_ERR_INVALID_ARGUMENT, "ipc_export: null pointer");
   // The handle names the whole allocation that contains ptr; report ptr's offset in it.
@@ -243,6 +245,7 @@ extern "C" int helm_ipc_export(const void *ptr, void *handle_out, int64_t *offse
 }
 
 extern "C" int helm_ipc_import(const void *handle, int64_t offset, void **ptr_out, void **base_out) {
+  helm::NvtxRange nvtx_range_("helm_ipc_import");
   using namespace helm;
   if (!handle || !ptr_out || !base_out) return fail(HELM_ERR_INVALID_ARGUMENT, "ipc_import: null pointer");
   cudaIpcMemHandle_t h;
@@ -256,6 +259,7 @@ extern "C" int helm_ipc_import(const void *handle, int64_t offset, void **ptr_ou
 }
 
 extern "C" int helm_ipc_close(void *base) {
+  helm::NvtxRange nvtx_range_("helm_ipc_close");
   using namespace helm;
   if (!base) return HELM_OK;
   cudaError_t e = cudaIpcCloseMemHandle(base);

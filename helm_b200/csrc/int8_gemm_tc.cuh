@@ -311,6 +311,7 @@ int launch_gemm(const void *x, int xdt, const int8_t *wpk, const void *scale, in
 extern "C" int helm_int8_gemm_packed(const void *x, int32_t x_dtype, const int8_t *packed, const void *w_scale,
                                      int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t N, int32_t K,
                                      void *stream) {
+  helm::NvtxRange nvtx_range_("helm_int8_gemm_packed");
   using namespace helm;
   if (M < 0 || N < 0 || K <= 0) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_gemm: bad sizes M=%d N=%d K=%d", M, N, K);
   if (K % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_gemm: K=%d is not a multiple of 16", K);

@@ -49,10 +49,10 @@ namespace helm {
 
 namespace {
 
-constexpr int kCWarps = 4;                       // consumer warps
-constexpr int kThreadsT = (kCWarps + 1) * 32;    // + one producer warp
+constexpr int kCWarps = 4;                       // consumer warps (default; 8 for long-K GEMVs),
+                                                 // plus one producer warp; a stage is one 128-k box
+                                                 // per consumer warp
 constexpr int kBoxK = 128;                       // k per TMA box row (128-byte swizzle)
-constexpr int kStageK = kCWarps * kBoxK;         // k per stage: one box per consumer warp
 constexpr int kMaxStages = 16;
 
 // Ring depth: the shared memory left per CTA when ceil(CTAs / SMs) CTAs share an SM (at most 3;
@@ -162,8 +162,8 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 // Grid (ceil(N / (16*RT)), ceil(M / (8*MT))), 160 threads.  Dynamic shared memory: the ring of
 // ST stages (each, 1024-byte aligned: 4 weight boxes of 128 k x 16*RT rows, then 4 x boxes of
 // 128 k x XR rows at 128-byte alignment) + kCWarps * RT * MT * 128 floats for the final sum.
-template <typename XT, int RT, int MT>
-__global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_constant__ CUtensorMap tmW,
+template <typename XT, int RT, int MT, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32) int8_tma_kernel(const __grid_constant__ CUtensorMap tmW,
                                                             const __grid_constant__ CUtensorMap tmX,
                                                             const void *__restrict__ scale, int scale_dt,
                                                             const XT *__restrict__ bias, XT *__restrict__ y, int M,
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
                                                             const int8_t *__restrict__ wpk) {
   constexpr int kWBoxBytes = kBoxK * 16 * RT;
   constexpr int P = RT * MT * 128;  // floats of one warp's partial tile
-  const int stage_bytes = (kCWarps * (kWBoxBytes + xbox_bytes) + 1023) & ~1023;
+  const int stage_bytes = (CW * (kWBoxBytes + xbox_bytes) + 1023) & ~1023;
   const uint32_t xtx = (uint32_t)(kBoxK * XR * sizeof(XT));  // bytes one x box brings
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
@@ -182,17 +182,17 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_base = blockIdx.x * 16 * RT;
   const int m_base = blockIdx.y * 8 * MT;
-  const int nst = (K + kStageK - 1) / kStageK;
+  const int nst = (K + (CW * kBoxK) - 1) / (CW * kBoxK);
   // Weight tile (rt, box bx) of a stage: [bx][rt] for tensor-map boxes (one box spans the CTA's
   // 16*RT rows), [rt][bx] for packed blocks (one bulk copy per row tile spans its boxes).
-  const int rt_stride = wpk ? kCWarps * kPackBlock : kPackBlock;
+  const int rt_stride = wpk ? CW * kPackBlock : kPackBlock;
   const int bx_stride = wpk ? kPackBlock : kWBoxBytes;
   const int KB = (K + kBoxK - 1) / kBoxK;
   const int n_tiles = (N + 15) / 16;
   auto wbox = [&](int slot, int bx) { return ring + (size_t)slot * stage_bytes + bx * bx_stride; };
   auto wtile = [&](int slot, int rt) { return ring + (size_t)slot * stage_bytes + rt * rt_stride; };
   auto xbox = [&](int slot, int bx) {
-    return ring + (size_t)slot * stage_bytes + kCWarps * kWBoxBytes + bx * xbox_bytes;
+    return ring + (size_t)slot * stage_bytes + CW * kWBoxBytes + bx * xbox_bytes;
   };
 
   // Programmatic dependent launch: the next kernel on the stream may start its own prologue now;
@@ -201,18 +201,18 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     for (int i = 0; i < ST; ++i) {
       mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], kCWarps);
+      mbar_init(&empty_bar[i], CW);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     any_fail = 0;
   }
   __syncthreads();
 
-  if (warp == kCWarps) {
+  if (warp == CW) {
     // ---------------- producer ----------------
     if (lane == 0) {
       bool ok = true;
-      auto boxes_of = [&](int s) { return min(kCWarps, (K - s * kStageK + kBoxK - 1) / kBoxK); };
+      auto boxes_of = [&](int s) { return min(CW, (K - s * (CW * kBoxK) + kBoxK - 1) / kBoxK); };
       // The weights of the first stages go out before the previous kernel has finished (they
       // are never written by a preceding kernel of a decode step); x only after it has.
       const int pre = min(ST, nst);
@@ -220,11 +220,11 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
       auto load_w = [&](int slot, int s, int boxes) {
         if (wpk) {
           for (int rt = 0; rt < tiles; ++rt)
-            bulk_load(wtile(slot, rt), wpk + ((int64_t)(n_base / 16 + rt) * KB + s * kCWarps) * kPackBlock,
+            bulk_load(wtile(slot, rt), wpk + ((int64_t)(n_base / 16 + rt) * KB + s * CW) * kPackBlock,
                       (uint32_t)(boxes * kPackBlock), &full_bar[slot]);
         } else {
           for (int bx = 0; bx < boxes; ++bx)
-            tma_load_2d(wbox(slot, bx), &tmW, &full_bar[slot], s * kStageK + bx * kBoxK, n_base);
+            tma_load_2d(wbox(slot, bx), &tmW, &full_bar[slot], s * (CW * kBoxK) + bx * kBoxK, n_base);
         }
       };
       auto stage_tx = [&](int boxes) {
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
       asm volatile("griddepcontrol.wait;" ::: "memory");
       for (int s = 0; s < pre; ++s)
         for (int bx = 0; bx < boxes_of(s); ++bx)
-          tma_load_2d(xbox(s, bx), &tmX, &full_bar[s], s * kStageK + bx * kBoxK, m_base);
+          tma_load_2d(xbox(s, bx), &tmX, &full_bar[s], s * (CW * kBoxK) + bx * kBoxK, m_base);
       for (int s = pre; s < nst; ++s) {
         const int slot = s % ST;
         if (!mbar_wait(&empty_bar[slot], (uint32_t)((s / ST - 1) & 1))) {
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
         mbar_arrive_expect_tx(&full_bar[slot], stage_tx(boxes));
         load_w(slot, s, boxes);
         for (int bx = 0; bx < boxes; ++bx)
-          tma_load_2d(xbox(slot, bx), &tmX, &full_bar[slot], s * kStageK + bx * kBoxK, m_base);
+          tma_load_2d(xbox(slot, bx), &tmX, &full_bar[slot], s * (CW * kBoxK) + bx * kBoxK, m_base);
       }
       // drain: the copies of the last stages land before this CTA can finish
       for (int s = max(0, nst - ST); s < nst && ok; ++s)
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
 
   for (int s = 0; s < nst; ++s) {
     const int slot = s % ST;
-    const int kbox = s * kStageK + warp * kBoxK;
+    const int kbox = s * (CW * kBoxK) + warp * kBoxK;
     if (!mbar_wait(&full_bar[slot], (uint32_t)((s / ST) & 1))) {
       atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
       any_fail = 1;
@@ -326,21 +326,21 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
     for (int nt = 0; nt < MT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) red[warp * P + ((rt * MT + nt) * 4 + e) * 32 + lane] = acc[rt][nt][e];
-  asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(CW * 32) : "memory");
   if (any_fail) return;  // a stage never arrived: leave the rows unwritten (error word set)
   asm volatile("griddepcontrol.wait;" ::: "memory");  // y may still be read by the previous kernel
   if (glu) {
     // Gated unit: row tiles 2u and 2u+1 of W hold the gate and the up rows of outputs 16u..16u+15;
     // y[m, 16u + r] = silu(gate) * up, y [M, N/2].  The CTA owns whole tile pairs (RT even).
     const int half = N >> 1;
-    for (int pos = threadIdx.x; pos < P; pos += kCWarps * 32) {
+    for (int pos = threadIdx.x; pos < P; pos += CW * 32) {
       const int ln = pos & 31, e = (pos >> 5) & 3, tile = pos >> 7;
       const int rt = tile / MT, nt = tile - rt * MT;
       if (rt & 1) continue;
       const int pos_up = pos + MT * 128;  // same (nt, e, lane) of tile rt + 1
       float gv = 0.f, uv = 0.f;
 #pragma unroll
-      for (int wp = 0; wp < kCWarps; ++wp) {
+      for (int wp = 0; wp < CW; ++wp) {
         gv += red[wp * P + pos];
         uv += red[wp * P + pos_up];
       }
@@ -359,10 +359,10 @@ __global__ void __launch_bounds__(kThreadsT) int8_tma_kernel(const __grid_consta
     }
     return;
   }
-  for (int pos = threadIdx.x; pos < P; pos += kCWarps * 32) {
+  for (int pos = threadIdx.x; pos < P; pos += CW * 32) {
     float v = 0.f;
 #pragma unroll
-    for (int wp = 0; wp < kCWarps; ++wp) v += red[wp * P + pos];
+    for (int wp = 0; wp < CW; ++wp) v += red[wp * P + pos];
     const int ln = pos & 31, e = (pos >> 5) & 3, tile = pos >> 7;
     const int rt = tile / MT, nt = tile - rt * MT;
     const int row = (ln >> 2) + ((e & 2) ? 8 : 0), col = (ln & 3) * 2 + (e & 1);
@@ -459,17 +459,17 @@ bool act_map(CUtensorMap *m, const void *x, int xdt, int M, int K, int rows) {
   return true;
 }
 
-template <typename XT, int RT, int MT>
+template <typename XT, int RT, int MT, int CW = kCWarps>
 int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int sdt, const void *bias, void *y,
                int M, int N, int K, cudaStream_t st, int glu, const int8_t *wpk) {
   const int XR = M < 8 * MT ? M : 8 * MT;                          // x rows per box
   const int xbox_bytes = ((kBoxK * XR * (int)sizeof(XT)) + 127) & ~127;   // 128-byte aligned x boxes
-  const int stage_bytes = (kCWarps * (kBoxK * 16 * RT + xbox_bytes) + 1023) & ~1023;
-  const int red_bytes = (int)sizeof(float) * kCWarps * RT * MT * 128;
+  const int stage_bytes = (CW * (kBoxK * 16 * RT + xbox_bytes) + 1023) & ~1023;
+  const int red_bytes = (int)sizeof(float) * CW * RT * MT * 128;
   const int ctas = ((N + 16 * RT - 1) / (16 * RT)) * ((M + 8 * MT - 1) / (8 * MT));
   const int ST = ring_stages(ctas, num_sms(), stage_bytes, red_bytes);
   const size_t smem = 1024 + (size_t)ST * stage_bytes + red_bytes;
-  auto kern = int8_tma_kernel<XT, RT, MT>;
+  auto kern = int8_tma_kernel<XT, RT, MT, CW>;
   {
     static std::mutex mu;
     static std::vector<std::pair<int, size_t>> done;  // (device, bytes allowed)
@@ -491,7 +491,7 @@ int launch_cfg(const void *x, int xdt, const int8_t *w, const void *scale, int s
     return fail(HELM_ERR_CUDA, "int8_linear: cuTensorMapEncodeTiled failed");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N + 16 * RT - 1) / (16 * RT), (M + 8 * MT - 1) / (8 * MT));
-  cfg.blockDim = dim3(kThreadsT);
+  cfg.blockDim = dim3((CW + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -523,6 +523,10 @@ int launch_m(const void *x, int xdt, const int8_t *w, const void *scale, int sdt
   if constexpr (MT >= 4) {  // wide x tiles: one row tile per CTA (register budget)
     return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
   } else {
+    // One row tile per CTA over a long K: eight consumer warps, 1024-k stages (half the stage
+    // round trips of a 512-k ring for the same bytes in flight).
+    if (tiles <= 3 * sms && K >= 8192)
+      return launch_cfg<XT, 1, MT, 8>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
     if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
     if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
     if (tiles <= 2 * 3 * sms) return launch_cfg<XT, 3, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
@@ -562,6 +566,7 @@ int check_args(const void *x, int32_t x_dtype, const int8_t *w, const void *w_sc
 extern "C" int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w, const void *w_scale,
                                 int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t N, int32_t K,
                                 void *stream) {
+  helm::NvtxRange nvtx_range_("helm_int8_linear");
   using namespace helm;
   const int rc = check_args(x, x_dtype, w, w_scale, scale_dtype, y, M, N, K, "int8_linear");
   if (rc != HELM_OK || M == 0 || N == 0) return rc;
@@ -573,6 +578,7 @@ extern "C" int helm_int8_linear(const void *x, int32_t x_dtype, const int8_t *w,
 extern "C" int helm_int8_linear_glu(const void *x, int32_t x_dtype, const int8_t *w, const void *w_scale,
                                     int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t I, int32_t K,
                                     void *stream) {
+  helm::NvtxRange nvtx_range_("helm_int8_linear_glu");
   using namespace helm;
   if (I < 0 || I % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_linear_glu: I=%d is not a multiple of 16", I);
   const int rc = check_args(x, x_dtype, w, w_scale, scale_dtype, y, M, 2 * I, K, "int8_linear_glu");
@@ -588,6 +594,7 @@ extern "C" int64_t helm_int8_packed_bytes(int32_t N, int32_t K) {
 }
 
 extern "C" int helm_int8_pack_weight(const int8_t *w, int32_t N, int32_t K, int8_t *packed, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_int8_pack_weight");
   using namespace helm;
   if (N < 0 || K <= 0) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_pack_weight: bad sizes N=%d K=%d", N, K);
   if (K % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_pack_weight: K=%d is not a multiple of 16", K);
@@ -606,6 +613,7 @@ extern "C" int helm_int8_pack_weight(const int8_t *w, int32_t N, int32_t K, int8
 extern "C" int helm_int8_linear_packed(const void *x, int32_t x_dtype, const int8_t *packed, const void *w_scale,
                                        int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t N, int32_t K,
                                        void *stream) {
+  helm::NvtxRange nvtx_range_("helm_int8_linear_packed");
   using namespace helm;
   const int rc = check_args(x, x_dtype, packed, w_scale, scale_dtype, y, M, N, K, "int8_linear_packed");
   if (rc != HELM_OK || M == 0 || N == 0) return rc;
@@ -618,6 +626,7 @@ extern "C" int helm_int8_linear_packed(const void *x, int32_t x_dtype, const int
 extern "C" int helm_int8_linear_glu_packed(const void *x, int32_t x_dtype, const int8_t *packed, const void *w_scale,
                                            int32_t scale_dtype, const void *bias, void *y, int32_t M, int32_t I,
                                            int32_t K, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_int8_linear_glu_packed");
   using namespace helm;
   if (I < 0 || I % 16) return fail(HELM_ERR_UNSUPPORTED, "int8_linear_glu_packed: I=%d is not a multiple of 16", I);
   const int rc = check_args(x, x_dtype, packed, w_scale, scale_dtype, y, M, 2 * I, K, "int8_linear_glu_packed");
@@ -629,6 +638,7 @@ extern "C" int helm_int8_linear_glu_packed(const void *x, int32_t x_dtype, const
 }
 
 extern "C" int helm_int8_linear_error(int32_t *flag_out, int32_t reset) {
+  helm::NvtxRange nvtx_range_("helm_int8_linear_error");
   using namespace helm;
   if (!flag_out) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_linear_error: null pointer");
   int v = 0;

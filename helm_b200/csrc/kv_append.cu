@@ -303,6 +303,7 @@ int launch_rows(const helm_kv_append_params *p, AppendArgs a, F launch, const ch
 }  // namespace helm
 
 extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_kv_append");
   using namespace helm;
   int rc = check_append(p, true);
   if (rc != HELM_OK || p->B == 0) return rc;
@@ -313,6 +314,7 @@ extern "C" int helm_kv_append(const helm_kv_append_params *p, void *stream) {
 }
 
 extern "C" int helm_decode_prologue(const helm_decode_prologue_params *p, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_decode_prologue");
   using namespace helm;
   if (!p) return fail(HELM_ERR_INVALID_ARGUMENT, "decode_prologue: params is null");
   const helm_kv_append_params *ap = &p->append;

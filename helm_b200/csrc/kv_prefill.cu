@@ -78,6 +78,7 @@ __global__ void __launch_bounds__(kPrefillThreads) prefill_pages_kernel(const __
 }  // namespace helm
 
 extern "C" int helm_kv_write_pages(const helm_kv_prefill_params *p, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_kv_write_pages");
   using namespace helm;
   if (!p) return fail(HELM_ERR_INVALID_ARGUMENT, "kv_write_pages: params is null");
   if (p->count < 0 || p->Hkv <= 0 || p->D <= 0 || p->P <= 0 || p->num_pool_pages < 0)

@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T *__restri
 
 extern "C" int helm_rmsnorm(const void *x, int32_t x_dtype, int64_t x_stride, const void *w, int32_t w_dtype,
                             void *y, int64_t y_stride, int64_t rows, int32_t dim, float eps, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_rmsnorm");
   using namespace helm;
   if (rows < 0 || dim <= 0) return fail(HELM_ERR_INVALID_ARGUMENT, "rmsnorm: bad sizes rows=%lld dim=%d",
                                         (long long)rows, dim);

@@ -117,6 +117,7 @@ bool is_device_memory(const void *p) {
 
 extern "C" int helm_copy_pages(void *dst_base, int64_t dst_first, const void *src_base, const int32_t *src_ids,
                                int32_t count, int64_t page_bytes, int32_t *copies_out, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_copy_pages");
   using namespace helm;
   if (copies_out) *copies_out = 0;
   if (count < 0 || page_bytes <= 0 || dst_first < 0)
@@ -176,6 +177,7 @@ extern "C" int helm_copy_pages(void *dst_base, int64_t dst_first, const void *sr
 extern "C" int helm_move_pages(void *dst_base, const int32_t *dst_ids, const void *src_base, const int32_t *src_ids,
                                int32_t count, int64_t page_bytes, int64_t dst_pages, int64_t src_pages,
                                int32_t *copies_out, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_move_pages");
   using namespace helm;
   if (copies_out) *copies_out = 0;
   if (count < 0 || page_bytes <= 0 || dst_pages < 0 || src_pages < 0)

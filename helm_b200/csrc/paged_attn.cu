@@ -1845,6 +1845,7 @@ extern "C" int64_t helm_paged_attn_workspace_bytes(const helm_paged_attn_params 
 }
 
 extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_paged_attn_decode");
   int rc = validate(p);
   if (rc != HELM_OK) return rc;
   if (p->B == 0 || p->Hq == 0) return HELM_OK;
@@ -1953,6 +1954,7 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
 
 extern "C" int helm_lse_merge(const float *partials, int32_t num_partials, int64_t partial_stride, int32_t rows,
                               int32_t D, void *out, int32_t out_dtype, float *out_record, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_lse_merge");
   if (rows < 0 || D <= 0 || num_partials < 1 || partial_stride < (int64_t)rows * (D + 2))
     return fail(HELM_ERR_INVALID_ARGUMENT, "lse_merge: bad sizes rows=%d D=%d partials=%d stride=%lld", rows, D,
                 num_partials, (long long)partial_stride);
@@ -2002,6 +2004,7 @@ int noalloc_scratch(float **out) {
 }  // namespace helm
 
 extern "C" int helm_paged_attn_decode_noalloc(const helm_paged_attn_params *p, void *stream) {
+  helm::NvtxRange nvtx_range_("helm_paged_attn_decode_noalloc");
   using namespace helm;
   int rc = validate(p);
   if (rc != HELM_OK) return rc;
