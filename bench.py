@@ -54,11 +54,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
-    ap.add_argument("--workload", default="config5", choices=["config5", "config2", "config1", "config3", "config4"],
+    ap.add_argument("--workload", default="config5",
+                    choices=["config5", "config2", "config1", "config3", "config4", "prefill"],
                     help="config5: the sharded decode-attention stack (default); config2: INT8 GEMV shapes; "
                          "config1: the reference's single-layer mixed-residency fp32 case; config3: a "
                          "Qwen3-8B-shaped decode step through KVOffloadManager; config4: a Qwen3-14B-shaped "
-                         "INT8 decode step with half the KV on the host")
+                         "INT8 decode step with half the KV on the host; prefill: the config-2 weights at M=4096 "
+                         "through the tcgen05 INT8 GEMM (and dequantise + cuBLAS beside it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub-records", action="store_true",
                     help="config5 at N=1: skip the config-2 and config-1 sub-records of the line")
@@ -1396,6 +1398,29 @@ def main():
             run_reference_config2(args, rank)
         else:
             run_config2(args, rank, local, world)
+        return
+    if args.workload == "prefill":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference has no INT8 GEMM (its linear is "
+                                  "the fp16 CPU GEMV, timed by --workload config2)"}))
+            return
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        res = c2_prefill_gemm(args, dev, world)
+        if rank == 0:
+            flops = sum(2.0 * c["M"] * c["N"] * c["K"] for c in res["cases"])
+            ms = sum(c["tcgen05"]["us"] for c in res["cases"]) / 1e3
+            tf = flops / (ms * 1e-3) / 1e12
+            print(json.dumps({"metric": "int8 weight-only prefill GEMM TFLOP/s (config-2 weights, M=4096)",
+                              "value": tf, "unit": "TFLOP/s", "n_gpus": world, "steps": 30, "warmup": 3,
+                              "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                              "dtype": "bf16 x int8 -> fp32", "data": "synthetic",
+                              "config": {"workload": "the three config-2 weights at M=4096 tokens"},
+                              "roofline": {"bound": "tensor", "achieved": tf, "peak": res["peak_tflops"],
+                                           "unit": "TFLOP/s", "frac": tf / res["peak_tflops"], "traffic": None,
+                                           "peak_kind": res["peak_kind"], "kernel": "int8_gemm_tc_kernel"},
+                              "cases": res["cases"], "cpu_baseline": None, "e2e": None}), flush=True)
         return
     if args.workload == "config1":
         if args.impl == "reference":

@@ -7,38 +7,42 @@
 // conversion, fp32 accumulation, the per-channel scale and the bias applied once per output -- as
 // a dense contraction, so that prefill no longer builds a dequantised copy of the weight.
 //
-// CTA tile 128 (tokens) x 128 (output channels), k in stages of 128 (one packed block column).
-// Warp roles (192 threads):
-//   warp 0      TMA producer: x tile (two 64-k boxes, 128-byte swizzle) and the eight packed
-//               16-row weight blocks of the stage (bulk copies) into a 2-stage ring;
-//   warps 1-4   converters, then the epilogue: each stage's int8 block is rewritten as 16-bit
-//               values in the canonical K-major 128-byte-swizzled layout the tensor core reads
-//               (exact: |w| <= 127), then fence.proxy.async and an mbarrier arrive; after the
-//               last stage they read the fp32 accumulators back from tensor memory
-//               (tcgen05.ld, one 32-lane quadrant per warp), apply scale and bias, store y;
-//   warp 5      MMA issuer: one elected thread issues tcgen05.mma kind::f16 (M=128, N=128,
-//               K=16, A = x, B = w, both K-major from shared memory descriptors, D in tensor
-//               memory) for the 8 k-steps of a stage and releases the stage with tcgen05.commit.
-// Tensor memory: 128 columns (the 128 x 128 fp32 accumulator), allocated by warp 0.
+// CTA tile 128 (tokens) x 256 (output channels); k in steps of 64 (one 128-byte swizzle atom of
+// 16-bit values).  Three rings in shared memory, each with its own full / empty mbarriers:
+//   A  (x tiles, 16 KB, 4 deep)          filled by TMA, released by the MMAs (tcgen05.commit);
+//   W  (packed int8, 32 KB, 2 deep)       one packed block column (128 k) = two k steps, filled by
+//                                         bulk copies, released by the converters;
+//   B  (converted weights, 32 KB, 2 deep) written by the converters, released by the MMAs.
+// Warp roles (320 threads):
+//   warp 0      producer: TMA for x, bulk copies for the packed weight blocks;
+//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16; A = x,
+//               B = w, both K-major 128-byte-swizzled shared-memory descriptors; D in tensor
+//               memory) four times per k step, then tcgen05.commit to the A and B empty barriers;
+//   warps 2-9   converters, then the epilogue: each k step's int8 half-block is rewritten as
+//               16-bit values (exact: |w| <= 127) in the canonical swizzled layout the tensor core
+//               reads, followed by fence.proxy.async and an mbarrier arrive; after the last k step
+//               they read the fp32 accumulators from tensor memory (tcgen05.ld; a warp reads its
+//               32-lane quadrant, two warps per quadrant split the 256 columns), apply scale and
+//               bias, and store y.
+// Tensor memory: 256 columns (the 128 x 256 fp32 accumulator), allocated by warp 0.
 // Every mbarrier wait is bounded: a wait that gives up sets HELM_DEVERR_TIMEOUT in the library's
-// INT8 error word; the CTA then skips its remaining work, waits (bounded) for the copies it
-// issued and frees its tensor memory.
+// INT8 error word; the CTA then skips its remaining work and its stores, waits (bounded) for the
+// copies it issued, and frees its tensor memory.
 // Included by int8_linear.cu (it shares that file's INT8 error word, g_int8_error).
 #pragma once
 
 namespace helm {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 128;
-constexpr int kGStages = 2;
-constexpr int kAtomBytes = 128 * 128;                 // 128 rows x 64 16-bit values (128 B)
-constexpr int kABytes = 2 * kAtomBytes;               // x tile: two k atoms
-constexpr int kBBytes = 2 * kAtomBytes;               // converted weight tile
-constexpr int kWBytes = BN * BK;                      // eight packed 16 x 128 int8 blocks
-constexpr int kGStageBytes = kABytes + kBBytes + kWBytes;
-constexpr int kGSmem = kGStages * kGStageBytes + 1024;
-constexpr int kGThreads = 192;
-constexpr int kTmemCols = 128;
+constexpr int GM = 128, GN = 256, GK = 64;       // CTA tile and k step
+constexpr int kAStages = 4, kWStages = 2, kBStages = 2;
+constexpr int kAStageBytes = GM * GK * 2;        // 16 KB: 128 rows x 128 B
+constexpr int kBStageBytes = GN * GK * 2;        // 32 KB: 256 rows x 128 B
+constexpr int kWStageBytes = GN * 128;           // 32 KB: 16 packed blocks (16 rows x 128 k)
+constexpr int kGSmem = kAStages * kAStageBytes + kWStages * kWStageBytes + kBStages * kBStageBytes + 1024;
+constexpr int kConvWarps = 8;
+constexpr int kGThreads = (2 + kConvWarps) * 32;
+constexpr int kTmemCols = 256;
 
 __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr) {
   // K-major, 128-byte swizzle: leading byte offset 1 (16 B, unused for this layout), stride byte
@@ -57,10 +61,10 @@ template <> struct UFmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
 template <> struct UFmt<__half> { static constexpr uint32_t v = 0; };
 
 // kind::f16 instruction descriptor: fp32 accumulator, A and B of type XT, both K-major,
-// N = 128 (n_dim = N >> 3), M = 128 (m_dim = M >> 4).
+// N = GN (n_dim = N >> 3), M = GM (m_dim = M >> 4).
 template <typename XT> __device__ __forceinline__ uint32_t umma_idesc() {
-  return (1u << 4) | (UFmt<XT>::v << 7) | (UFmt<XT>::v << 10) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
+  return (1u << 4) | (UFmt<XT>::v << 7) | (UFmt<XT>::v << 10) | ((uint32_t)(GN >> 3) << 17) |
+         ((uint32_t)(GM >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -97,14 +101,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 16 int8 values -> 16 exact 16-bit values of XT, as two 16-byte chunks.
-template <typename XT> __device__ __forceinline__ void cvt16(const int4 &raw, uint4 &lo, uint4 &hi) {
-  const int8_t *b = reinterpret_cast<const int8_t *>(&raw);
-  XT o[16];
+// Two floats rounded to XT, as one 32-bit word (first value in the low half).
+template <typename XT> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// 16 int8 values -> 16 exact 16-bit values of XT, as two 16-byte chunks (the pairwise conversions
+// of the decode GEMV: int8 -> fp16 / bf16 without rounding).
+template <typename XT> __device__ __forceinline__ void cvt16(const uint4 &raw, uint4 &lo, uint4 &hi) {
+  const uint32_t w[4] = {raw.x ^ 0x80808080u, raw.y ^ 0x80808080u, raw.z ^ 0x80808080u, raw.w ^ 0x80808080u};
+  uint32_t o[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i] = Elem<XT>::from_f((float)b[i]);
-  lo = *reinterpret_cast<const uint4 *>(&o[0]);
-  hi = *reinterpret_cast<const uint4 *>(&o[8]);
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = i8pair<XT, 0x4140u>(w[i]);
+    o[2 * i + 1] = i8pair<XT, 0x4342u>(w[i]);
+  }
+  lo = make_uint4(o[0], o[1], o[2], o[3]);
+  hi = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 template <typename XT>
@@ -113,27 +132,37 @@ __global__ void __launch_bounds__(kGThreads, 1)
                         const void *__restrict__ scale, int scale_dt, const XT *__restrict__ bias,
                         XT *__restrict__ y, int M, int N, int K) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[kGStages];
-  __shared__ __align__(8) uint64_t ready_bar[kGStages];
-  __shared__ __align__(8) uint64_t empty_bar[kGStages];
+  __shared__ __align__(8) uint64_t a_full[kAStages], a_empty[kAStages];
+  __shared__ __align__(8) uint64_t w_full[kWStages], w_empty[kWStages];
+  __shared__ __align__(8) uint64_t b_full[kBStages], b_empty[kBStages];
   __shared__ __align__(8) uint64_t acc_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
+  __shared__ float s_scale[GN], s_bias[GN];
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *a_ring = smem;
+  uint8_t *w_ring = a_ring + kAStages * kAStageBytes;
+  uint8_t *b_ring = w_ring + kWStages * kWStageBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-  const int KB = (K + BK - 1) / BK;
+  const int n0 = blockIdx.x * GN, m0 = blockIdx.y * GM;
+  const int KB = (K + 127) / 128;          // packed block columns
+  const int NK = (K + GK - 1) / GK;        // k steps
   const int n_tiles = (N + 15) / 16;
-  auto a_tile = [&](int s) { return smem + (size_t)s * kGStageBytes; };
-  auto b_tile = [&](int s) { return smem + (size_t)s * kGStageBytes + kABytes; };
-  auto w_raw = [&](int s) { return smem + (size_t)s * kGStageBytes + kABytes + kBBytes; };
+  const int tiles = max(0, min(GN / 16, n_tiles - n0 / 16));   // packed 16-row tiles that exist
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGStages; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&ready_bar[s], 4);
-      mbar_init(&empty_bar[s], 1);
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&a_full[s], 1);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], kConvWarps);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&b_full[s], kConvWarps);
+      mbar_init(&b_empty[s], 1);
     }
     mbar_init(&acc_bar, 1);
     failed = 0;
@@ -152,107 +181,137 @@ __global__ void __launch_bounds__(kGThreads, 1)
   pdl_trigger();
   pdl_wait();
 
+  auto give_up = [&]() {
+    atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
+    failed = 1;
+  };
+
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      const int tiles = max(0, min(BN / 16, n_tiles - n0 / 16));
-      int issued = 0;
-      for (int i = 0; i < KB; ++i) {
-        const int s = i % kGStages;
-        if (i >= kGStages && !mbar_wait(&empty_bar[s], (uint32_t)((i / kGStages - 1) & 1))) {
-          atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
-          failed = 1;
+      int a_issued = 0, w_issued = 0;
+      for (int j = 0; j < NK && !*reinterpret_cast<volatile int *>(&failed); ++j) {
+        if ((j & 1) == 0) {                       // the packed block column of k steps j, j + 1
+          const int c = j >> 1, ws = c % kWStages;
+          if (c >= kWStages && !mbar_wait(&w_empty[ws], (uint32_t)((c / kWStages - 1) & 1))) {
+            give_up();
+            break;
+          }
+          mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(tiles * 2048));
+          for (int t = 0; t < tiles; ++t)
+            bulk_g2s(w_ring + ws * kWStageBytes + t * 2048, wpk + ((int64_t)(n0 / 16 + t) * KB + c) * 2048, 2048,
+                     &w_full[ws]);
+          w_issued = c + 1;
+        }
+        const int as = j % kAStages;
+        if (j >= kAStages && !mbar_wait(&a_empty[as], (uint32_t)((j / kAStages - 1) & 1))) {
+          give_up();
           break;
         }
-        mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(kABytes + tiles * 2048));
-        tma_load_2d(a_tile(s), &tmX, &full_bar[s], i * BK, m0);
-        tma_load_2d(a_tile(s) + kAtomBytes, &tmX, &full_bar[s], i * BK + 64, m0);
-        for (int t = 0; t < tiles; ++t)
-          bulk_g2s(w_raw(s) + t * 2048, wpk + ((int64_t)(n0 / 16 + t) * KB + i) * 2048, 2048, &full_bar[s]);
-        issued = i + 1;
+        mbar_arrive_expect_tx(&a_full[as], (uint32_t)kAStageBytes);
+        tma_load_2d(a_ring + as * kAStageBytes, &tmX, &a_full[as], j * GK, m0);
+        a_issued = j + 1;
       }
-      // the copies of the last stages land before this CTA can finish
-      for (int i = max(0, issued - kGStages); i < issued; ++i)
-        if (!mbar_wait(&full_bar[i % kGStages], (uint32_t)((i / kGStages) & 1))) atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
+      // the copies still in flight land before this CTA can finish
+      for (int j = max(0, a_issued - kAStages); j < a_issued; ++j)
+        if (!mbar_wait(&a_full[j % kAStages], (uint32_t)((j / kAStages) & 1))) give_up();
+      for (int c = max(0, w_issued - kWStages); c < w_issued; ++c)
+        if (!mbar_wait(&w_full[c % kWStages], (uint32_t)((c / kWStages) & 1))) give_up();
     }
-  } else if (warp <= 4) {
-    // ---------------- converters ----------------
-    const int tc = threadIdx.x - 32;  // 0..127
-    for (int i = 0; i < KB; ++i) {
-      const int s = i % kGStages;
-      if (!mbar_wait(&full_bar[s], (uint32_t)((i / kGStages) & 1))) {
-        atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
-        failed = 1;
-        break;
-      }
-      const uint8_t *raw = w_raw(s);
-      uint8_t *bt = b_tile(s);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int q = tc + 128 * j;          // packed chunk: row r (0..127), stored position p
-        const int r = q >> 3, p = q & 7;
-        const int lc = p ^ (r & 7);          // logical 16-value chunk: k = 16*lc .. 16*lc + 15
-        const int4 v = *reinterpret_cast<const int4 *>(raw + (r >> 4) * 2048 + (r & 15) * 128 + p * 16);
-        uint4 lo, hi;
-        cvt16<XT>(v, lo, hi);
-        uint8_t *atom = bt + (lc >> 2) * kAtomBytes + r * 128;
-        const int c0 = 2 * (lc & 3);
-        *reinterpret_cast<uint4 *>(atom + (((c0) ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4 *>(atom + (((c0 + 1) ^ (r & 7)) << 4)) = hi;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ready_bar[s]);
-    }
-    // ---------------- epilogue ----------------
-    if (!mbar_wait(&acc_bar, 0u)) {
-      atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
-      failed = 1;
-    } else {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int quad = warp & 3;
-      const int m = m0 + quad * 32 + lane;
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        float acc[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, acc);
-        if (m < M && !*reinterpret_cast<volatile int *>(&failed)) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = n0 + c0 + j;
-            if (n < N) {
-              float v = acc[j] * load_f(scale, scale_dt, n);
-              if (bias) v += Elem<XT>::to_f(bias[n]);
-              y[(int64_t)m * N + n] = Elem<XT>::from_f(v);
-            }
-          }
-        }
-      }
-    }
-  } else {
+  } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = umma_idesc<XT>();
-      bool ok = true;
-      for (int i = 0; i < KB && ok; ++i) {
-        const int s = i % kGStages;
-        if (!mbar_wait(&full_bar[s], (uint32_t)((i / kGStages) & 1)) ||
-            !mbar_wait(&ready_bar[s], (uint32_t)((i / kGStages) & 1))) {
-          atomicOr(&g_int8_error, HELM_DEVERR_TIMEOUT);
-          failed = 1;
-          ok = false;
+      for (int j = 0; j < NK; ++j) {
+        const int as = j % kAStages, bs = j % kBStages;
+        if (!mbar_wait(&a_full[as], (uint32_t)((j / kAStages) & 1)) ||
+            !mbar_wait(&b_full[bs], (uint32_t)((j / kBStages) & 1))) {
+          give_up();
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a0 = smem_u32(a_tile(s)), b0 = smem_u32(b_tile(s));
+        const uint32_t a0 = smem_u32(a_ring + as * kAStageBytes), b0 = smem_u32(b_ring + bs * kBStageBytes);
 #pragma unroll
-        for (int j = 0; j < BK / 16; ++j) {
-          const uint32_t off = (uint32_t)((j >> 2) * kAtomBytes + (j & 3) * 32);
-          umma_f16(tmem, umma_smem_desc(a0 + off), umma_smem_desc(b0 + off), idesc, (i | j) != 0);
-        }
-        umma_commit(&empty_bar[s]);
+        for (int kk = 0; kk < GK / 16; ++kk)
+          umma_f16(tmem, umma_smem_desc(a0 + kk * 32), umma_smem_desc(b0 + kk * 32), idesc, (j | kk) != 0);
+        umma_commit(&a_empty[as]);
+        umma_commit(&b_empty[bs]);
       }
       umma_commit(&acc_bar);
+    }
+  } else {
+    // ---------------- converters ----------------
+    const int tc = threadIdx.x - 64;   // 0..255
+    {  // the tile's scales and biases, for the epilogue
+      const int n = n0 + tc;
+      s_scale[tc] = n < N ? load_f(scale, scale_dt, n) : 0.f;
+      s_bias[tc] = (bias && n < N) ? Elem<XT>::to_f(bias[n]) : 0.f;
+    }
+    for (int j = 0; j < NK; ++j) {
+      const int c = j >> 1, ws = c % kWStages, half = j & 1, bs = j % kBStages;
+      if (!mbar_wait(&w_full[ws], (uint32_t)((c / kWStages) & 1)) ||
+          (j >= kBStages && !mbar_wait(&b_empty[bs], (uint32_t)((j / kBStages - 1) & 1)))) {
+        give_up();
+        break;
+      }
+      const uint8_t *raw = w_ring + ws * kWStageBytes;
+      uint8_t *bt = b_ring + bs * kBStageBytes;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int q = tc + 256 * it;          // (row r, logical chunk 4*half + lq) of the half-block
+        const int r = q >> 2, lq = q & 3;
+        const int lc = 4 * half + lq;         // logical 16-value chunk of the packed row
+        const int p = lc ^ (r & 7);           // where the packing stored it
+        const uint4 v = *reinterpret_cast<const uint4 *>(raw + (r >> 4) * 2048 + (r & 15) * 128 + p * 16);
+        uint4 lo, hi;
+        cvt16<XT>(v, lo, hi);
+        uint8_t *row = bt + r * 128;
+        *reinterpret_cast<uint4 *>(row + (((2 * lq) ^ (r & 7)) << 4)) = lo;
+        *reinterpret_cast<uint4 *>(row + (((2 * lq + 1) ^ (r & 7)) << 4)) = hi;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&b_full[bs]);
+        if (half == 1 || j == NK - 1) mbar_arrive(&w_empty[ws]);
+      }
+    }
+    // ---------------- epilogue ----------------
+    if (!mbar_wait(&acc_bar, 0u)) {
+      give_up();
+    } else {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      // the scales written by the other converter warps (named barrier of the eight warps)
+      asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+      const int quad = warp & 3;                 // the TMEM lanes this warp may read
+      const int col0 = ((warp - 2) >> 2) * 128;  // which half of the 256 columns
+      const int m = m0 + quad * 32 + lane;
+      const bool store = m < M && !*reinterpret_cast<volatile int *>(&failed);
+      const bool vec = (N & 7) == 0;             // rows of y 16-byte aligned
+#pragma unroll 1
+      for (int c0 = col0; c0 < col0 + 128; c0 += 32) {
+        float acc[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, acc);
+        if (!store) continue;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) acc[jj] = fmaf(acc[jj], s_scale[c0 + jj], s_bias[c0 + jj]);
+        XT *dst = y + (int64_t)m * N + n0 + c0;
+        if (vec && n0 + c0 + 32 <= N) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 q;
+            q.x = pack2<XT>(acc[8 * v + 0], acc[8 * v + 1]);
+            q.y = pack2<XT>(acc[8 * v + 2], acc[8 * v + 3]);
+            q.z = pack2<XT>(acc[8 * v + 4], acc[8 * v + 5]);
+            q.w = pack2<XT>(acc[8 * v + 6], acc[8 * v + 7]);
+            reinterpret_cast<uint4 *>(dst)[v] = q;
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj)
+            if (n0 + c0 + jj < N) dst[jj] = Elem<XT>::from_f(acc[jj]);
+        }
+      }
     }
   }
 
@@ -270,7 +329,7 @@ bool x_map_sw128(CUtensorMap *m, const void *x, int xdt, int M, int K) {
   if (!enc) return false;
   cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)M};
   cuuint64_t gstr[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)BM};
+  cuuint32_t box[2] = {64, (cuuint32_t)GM};
   cuuint32_t estr[2] = {1, 1};
   return enc(m, xdt == HELM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
              const_cast<void *>(x), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -298,7 +357,7 @@ int launch_gemm(const void *x, int xdt, const int8_t *wpk, const void *scale, in
   }
   CUtensorMap xm;
   if (!x_map_sw128(&xm, x, xdt, M, K)) return fail(HELM_ERR_CUDA, "int8_gemm: cuTensorMapEncodeTiled failed");
-  const dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  const dim3 grid((N + GN - 1) / GN, (M + GM - 1) / GM);
   const cudaError_t e = launch_pdl(int8_gemm_tc_kernel<XT>, grid, dim3(kGThreads), kGSmem, st, xm, wpk, scale, sdt,
                                    static_cast<const XT *>(bias), static_cast<XT *>(y), M, N, K);
   if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_gemm: launch: %s", cudaGetErrorString(e));
@@ -322,7 +381,7 @@ extern "C" int helm_int8_gemm_packed(const void *x, int32_t x_dtype, const int8_
   if (!x || !packed || !w_scale || !y) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_gemm: null pointer");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(packed)) & 15)
     return fail(HELM_ERR_INVALID_ARGUMENT, "int8_gemm: x and packed must be 16-byte aligned");
-  if ((int64_t)(M + BM - 1) / BM > 65535) return fail(HELM_ERR_UNSUPPORTED, "int8_gemm: M=%d too large", M);
+  if ((int64_t)(M + GM - 1) / GM > 65535) return fail(HELM_ERR_UNSUPPORTED, "int8_gemm: M=%d too large", M);
   cudaStream_t st = as_stream(stream);
   return x_dtype == HELM_F16 ? launch_gemm<__half>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, N, K, st)
                              : launch_gemm<__nv_bfloat16>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, N, K,
