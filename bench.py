@@ -55,12 +55,13 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="helm", choices=["helm", "reference"])
     ap.add_argument("--workload", default="config5",
-                    choices=["config5", "config2", "config1", "config3", "config4", "prefill"],
+                    choices=["config5", "config2", "config1", "config3", "config4", "prefill", "kernels"],
                     help="config5: the sharded decode-attention stack (default); config2: INT8 GEMV shapes; "
                          "config1: the reference's single-layer mixed-residency fp32 case; config3: a "
                          "Qwen3-8B-shaped decode step through KVOffloadManager; config4: a Qwen3-14B-shaped "
                          "INT8 decode step with half the KV on the host; prefill: the config-2 weights at M=4096 "
-                         "through the tcgen05 INT8 GEMM (and dequantise + cuBLAS beside it)")
+                         "through the tcgen05 INT8 GEMM (and dequantise + cuBLAS beside it); kernels: every "
+                         "kernel family once, with its achieved GB/s or TFLOP/s")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub-records", action="store_true",
                     help="config5 at N=1: skip the config-2 and config-1 sub-records of the line")
@@ -74,6 +75,7 @@ def parse():
     # workload is all nine calls unless these are set.
     ap.add_argument("--shape", default=None, help="config2 only: N,K of a single shape")
     ap.add_argument("--rows", type=int, default=None, help="config2 only: a single M")
+    ap.add_argument("--kernel", default=None, help="kernels only: a single case by name")
     args = ap.parse_args()
     if args.layers is not None:
         CFG["layers"] = args.layers
@@ -849,6 +851,261 @@ def c2_prefill_gemm(args, dev, world, M=4096):
             "how": "bf16 x, int8 weights; CUDA graph of 10 calls replayed 3 times; 2*M*N*K flops"}
 
 
+# ----------------------------------------------------------------------------
+# Per-kernel roofline table (--workload kernels)
+# ----------------------------------------------------------------------------
+def _graph_time_ms(fn, reps, stream, warm=3):
+    """Device time of one call: `reps` calls captured in a CUDA graph, replayed once between CUDA
+    events (eager calls between events when the call cannot be captured)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / reps, "cuda graph"
+    except RuntimeError:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, "eager"
+
+
+def kernel_cases(dev):
+    """(name, kernels, bound, algorithmic bytes or flops, setup, description) for every kernel family
+    of the library.  Each setup allocates its inputs and returns (call, check): inputs of the
+    bandwidth-bound cases are larger than L2 (126 MB), so repeated calls stream from HBM; the
+    decode-step kernels (append, prologue, exchange) move a few KB per call and are latency-bound by
+    nature."""
+    import ctypes
+    import numpy as np
+    from helm_b200 import _native as N
+    from helm_b200 import ops
+    bf = torch.bfloat16
+    cases = []
+
+    def pool(B, Hkv, D, P, ctx, dtype, seed):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        npg = ctx // P
+        slab = torch.randn((B * npg, 2, Hkv, P, D), generator=g, device=dev).to(dtype)
+        pt = torch.arange(B * npg, dtype=torch.int32, device=dev).reshape(B, npg)
+        pu = torch.full((B, npg), P, dtype=torch.int32, device=dev)
+        nn = torch.full((B,), npg, dtype=torch.int32, device=dev)
+        return slab, pt, pu, nn
+
+    def attn_case(B, Hq, Hkv, D, P, ctx, dtype, splits, seed):
+        def setup():
+            slab, pt, pu, nn = pool(B, Hkv, D, P, ctx, dtype, seed)
+            q = torch.randn((B, Hq, D), device=dev).to(dtype)
+            out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
+            err = torch.zeros(1, dtype=torch.int32, device=dev)
+            kw = dict(num_kv_heads=Hkv, page_size=P, page_stride=2 * Hkv * P * D, head_stride=P * D,
+                      num_pool_pages=slab.shape[0], out=out, error_flag=err, num_splits=splits)
+
+            def call():
+                ops.paged_decode_attention(q, slab[:, 0], slab[:, 1], pt, pu, nn, **kw)
+            return call, lambda: int(err.item()) == 0 and bool(torch.isfinite(out).all())
+        es = torch.empty((), dtype=dtype).element_size()
+        return 2 * B * Hkv * ctx * D * es + 2 * B * Hq * D * es, setup
+
+    b, s = attn_case(4, 64, 8, 128, 64, 16384, bf, 0, 1)
+    cases.append(("attn_persistent", "attn_tc_persistent_kernel", "hbm", b, s,
+                  "bf16, B 4, 64q/8kv, d128, 16384 tokens (256 pages) per sequence: one config-5 layer at N=8"))
+    b, s = attn_case(4, 64, 8, 128, 64, 16384, bf, 8, 1)
+    cases.append(("attn_split", "attn_tc_kernel + lse_merge_kernel", "hbm", b, s,
+                  "the same call on the split path, 8 splits per sequence"))
+    b, s = attn_case(4, 32, 8, 128, 64, 16384, torch.float32, 0, 2)
+    cases.append(("attn_warp_fp32", "attn_warp_kernel + lse_merge_kernel", "hbm", b, s,
+                  "fp32 pages (config-1 heads), B 4, 32q/8kv, d128, 16384 tokens per sequence"))
+    b, s = attn_case(4, 48, 2, 96, 64, 65536, bf, 0, 3)
+    cases.append(("attn_generic", "attn_generic_kernel (+ lse_merge_kernel)", "hbm", b, s,
+                  "bf16, B 4, 48q/2kv (GQA group 24), d96, 65536 tokens per sequence"))
+
+    def merge_setup():
+        S, rows, D = 16, 16384, 128
+        part = torch.randn((S, rows, D + 2), device=dev)
+        part[:, :, D] = torch.randn((S, rows), device=dev)
+        part[:, :, D + 1] = torch.rand((S, rows), device=dev) + 0.5
+        out = torch.empty((rows, D), device=dev)
+        return (lambda: ops.lse_merge(part, out=out)), (lambda: bool(torch.isfinite(out).all()))
+    cases.append(("lse_merge", "lse_merge_kernel", "hbm", 16 * 16384 * 130 * 4 + 16384 * 128 * 4, merge_setup,
+                  "16 split records of 16384 rows x (128 + 2) fp32 into 16384 x 128 fp32"))
+
+    def append_setup(prologue):
+        B, Hq, Hkv, D, P = 4, 64, 8, 128, 64
+        slab = torch.zeros((B * 4, 2, Hkv, P, D), dtype=bf, device=dev)
+        kn = torch.randn((B, Hkv, D), device=dev).to(bf)
+        vn = torch.randn((B, Hkv, D), device=dev).to(bf)
+        dest = np.ascontiguousarray(np.array([[4 * b_ + 1, 1, 17] for b_ in range(B)], dtype=np.int32))
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        kw = dict(page_stride=2 * Hkv * P * D, head_stride=P * D, num_pool_pages=B * 4, page_size=P,
+                  dest_host=dest, error_flag=err)
+        if not prologue:
+            return (lambda: ops.kv_append(kn, vn, slab[:, 0], slab[:, 1], **kw)), (lambda: int(err.item()) == 0)
+        qi = torch.randn((B, Hq, D), device=dev).to(bf)
+        qo = torch.empty_like(qi)
+        qw = (torch.rand(D, device=dev) + 0.5).to(bf)
+        kwn = (torch.rand(D, device=dev) + 0.5).to(bf)
+        ang = torch.rand((B, D), device=dev)
+        cos, sin = ang.cos().to(bf), ang.sin().to(bf)
+        return (lambda: ops.decode_prologue(qi, kn, vn, qo, slab[:, 0], slab[:, 1], q_norm_w=qw, k_norm_w=kwn,
+                                            cos=cos, sin=sin, **kw)), (lambda: int(err.item()) == 0)
+    cases.append(("kv_append", "kv_append_kernel", "latency", 2 * 4 * 8 * 128 * (2 + 2), lambda: append_setup(False),
+                  "one decode token of B 4 x 8 kv heads x d128, bf16, host-directed destinations"))
+    cases.append(("decode_prologue", "decode_prologue_kernel", "latency",
+                  4 * (64 + 2 * 8) * 128 * 2 * 2 + 2 * 4 * 128 * 2, lambda: append_setup(True),
+                  "q/k RMSNorm + RoPE + q write + K/V append, B 4, 64q/8kv, d128, bf16"))
+
+    def norm_setup():
+        x = torch.randn((16384, 5120), device=dev).to(bf)
+        w = (torch.rand(5120, device=dev) + 0.5).to(bf)
+        y = torch.empty_like(x)
+        return (lambda: ops.rmsnorm(x, w, 1e-6, out=y)), (lambda: bool(torch.isfinite(y).all()))
+    cases.append(("rmsnorm", "rmsnorm_kernel", "hbm", 2 * 16384 * 5120 * 2 + 5120 * 2, norm_setup,
+                  "16384 rows x 5120, bf16 (a prefill-sized norm)"))
+
+    def prefill_setup():
+        Hkv, D, P, S = 8, 128, 64, 32768
+        K = torch.randn((1, Hkv, S, D), device=dev).to(bf)
+        V = torch.randn((1, Hkv, S, D), device=dev).to(bf)
+        slab = torch.empty((S // P, 2, Hkv, P, D), dtype=bf, device=dev)
+        perm = np.random.default_rng(0).permutation(S // P)
+        pages = [(int(perm[i]), i * P, P) for i in range(S // P)]
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def call():
+            ops.kv_write_pages(K, V, slab[:, 0], slab[:, 1], pages, page_stride=2 * Hkv * P * D, head_stride=P * D,
+                               num_pool_pages=S // P, page_size=P, error_flag=err)
+        return call, lambda: int(err.item()) == 0 and torch.equal(slab[int(perm[3]), 0, 2], K[0, 2, 3 * P:4 * P])
+    cases.append(("kv_write_pages", "prefill_pages_kernel", "hbm", 2 * 2 * 8 * 32768 * 128 * 2, prefill_setup,
+                  "one 32768-token prompt, 8 kv heads, d128, bf16, into 512 scattered pool slots"))
+
+    PB = 2 * 8 * 64 * 128 * 2          # one config-5 page (K and V of 8 heads), 256 KiB
+
+    def host_setup(to_host):
+        n = 1024
+        dslab = torch.randn((n, PB // 2), device=dev).to(bf)
+        hslab = torch.empty((n, PB // 2), dtype=bf, pin_memory=True)
+        ids = np.random.default_rng(1).permutation(n).astype(np.int32)
+        if to_host:
+            return (lambda: ops.move_pages(hslab, ids, dslab, np.arange(n, dtype=np.int32), PB)), (lambda: True)
+        return (lambda: ops.copy_pages(dslab, 0, hslab, ids, PB)), (lambda: True)
+    cases.append(("move_pages", "move_pages_kernel", "host link", 1024 * PB, lambda: host_setup(True),
+                  "1024 config-5 pages (256 KiB) device -> pinned host, scattered destinations"))
+    cases.append(("copy_pages", "gather_pages_kernel", "host link", 1024 * PB, lambda: host_setup(False),
+                  "1024 config-5 pages pinned host -> device, scattered sources"))
+
+    def gemv_setup(Nn, K, M, glu):
+        g = torch.Generator(device=dev).manual_seed(5)
+        copies = max(1, -(-4 * 126 * 2 ** 20 // (Nn * K))) if M <= 64 else 1   # weights rotate through > 4x L2
+        pks = [ops.int8_pack_weight(torch.randint(-127, 128, (Nn, K), generator=g, device=dev, dtype=torch.int8))
+               for _ in range(copies)]
+        sc = (torch.rand(Nn, generator=g, device=dev) * 0.019 + 0.001).to(bf)
+        x = torch.randn((M, K), generator=g, device=dev).to(bf)
+        y = torch.empty((M, Nn // 2 if glu else Nn), dtype=bf, device=dev)
+        it = [0]
+
+        def call():
+            pk = pks[it[0] % copies]
+            it[0] += 1
+            if glu:
+                ops.int8_linear_glu(x, pk, sc, out=y)
+            else:
+                ops.int8_linear(x, pk, sc, out=y, gemm=M > 64)
+        return call, lambda: ops.int8_linear_error() == 0
+    cases.append(("int8_gemv", "int8_tma_kernel", "hbm", c2_bytes(8, 12288, 4096),
+                  lambda: gemv_setup(12288, 4096, 8, False), "packed INT8 (12288, 4096), M 8, bf16 x"))
+    cases.append(("int8_gemv_glu", "int8_tma_kernel (gated)", "hbm",
+                  2 * 17408 * 5120 + 2 * 17408 * 2 + 8 * 5120 * 2 + 8 * 17408 * 2,
+                  lambda: gemv_setup(2 * 17408, 5120, 8, True),
+                  "config-4 MLP gate/up: packed INT8 (2 x 17408, 5120), M 8, silu(g) * u epilogue"))
+    cases.append(("int8_gemm", "int8_gemm_tc_kernel", "tensor", 2 * 4096 * 6144 * 4096,
+                  lambda: gemv_setup(6144, 4096, 4096, False), "packed INT8 (6144, 4096), M 4096 tokens, bf16 x"))
+
+    def gm_setup():
+        rows, D = 256, 128
+        rb, fb, cb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        N.lib().helm_gather_merge_state_bytes(1, rows, D, ctypes.byref(rb), ctypes.byref(fb), ctypes.byref(cb))
+        st = torch.zeros(rb.value + fb.value, dtype=torch.uint8, device=dev)
+        cnt = torch.zeros(max(cb.value, 4), dtype=torch.uint8, device=dev)
+        rec = torch.randn((rows, D + 2), device=dev)
+        rec[:, D + 1] = 1.0
+        out = torch.empty((rows, D), device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        p = N.GatherMergeParams()
+        p.rank, p.world, p.rows, p.D = 0, 1, rows, D
+        p.record = rec.data_ptr()
+        p.peer_recv[0], p.peer_flags[0] = st.data_ptr(), st.data_ptr() + rb.value
+        p.recv_local, p.flags_local = st.data_ptr(), st.data_ptr() + rb.value
+        p.counters = cnt.data_ptr()
+        p.out, p.out_dtype, p.error_flag = out.data_ptr(), N.F32, err.data_ptr()
+        p.wait_ns = 10_000_000
+        keep = (st, cnt, rec, out, err, p)
+
+        def call():
+            N.check("helm_gather_merge", N.lib().helm_gather_merge(ctypes.byref(keep[5]),
+                                                                  torch.cuda.current_stream(dev).cuda_stream))
+        return call, lambda: int(err.item()) == 0
+    cases.append(("gather_merge", "gather_merge_kernel", "latency", 2 * 256 * 130 * 4 + 256 * 128 * 4, gm_setup,
+                  "one rank's exchange of 256 rows x (128 + 2) at world 1 (push into its own slot, merge): the "
+                  "kernel's local half; the NVLink half runs only under multi-rank launches"))
+    return cases
+
+
+def run_kernels(args, rank, local, world):
+    """Every kernel family once, at a size that shows its bound, timed with CUDA events over CUDA
+    graphs; one JSON line with a row per kernel (achieved GB/s or TFLOP/s against the measured peak).
+    `--kernel NAME` limits it to one case (ncu captures)."""
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    hbm, hkind = peaks()
+    tf_peak, tkind = bf16_peak()
+    rows = []
+    for name, kern, bound, work, setup, what in kernel_cases(dev):
+        if args.kernel and name != args.kernel:
+            continue
+        call, check = setup()
+        reps = 3 if bound == "host link" else max(5, min(args.steps, 50))
+        ms, how = _graph_time_ms(call, reps, stream, warm=max(3, args.warmup))
+        ok = bool(check())
+        row = {"case": name, "kernel": kern, "bound": bound, "what": what, "us": round(ms * 1e3, 2),
+               "timing": how, "ok": ok}
+        if bound == "tensor":
+            tf = work / (ms * 1e-3) / 1e12
+            row.update(flops=work, tflops=round(tf, 1), frac=round(tf / tf_peak, 3))
+        else:
+            gbs = work / (ms * 1e-3) / 1e9
+            row.update(bytes=work, gbs=round(gbs, 1), frac=round(gbs / hbm, 3) if bound != "host link" else None)
+        rows.append(row)
+        del call, check
+        torch.cuda.empty_cache()
+    if rank == 0:
+        hb = [r for r in rows if r["bound"] == "hbm"]
+        agg = sum(r["bytes"] for r in hb) / max(1e-12, sum(r["us"] for r in hb) * 1e-6) / 1e9 if hb else None
+        print(json.dumps({"metric": "per-kernel achieved GB/s (TFLOP/s for the GEMM), algorithmic bytes / CUDA-event "
+                                    "time", "value": agg, "unit": "GB/s (HBM-bound cases, aggregate)",
+                          "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "per case", "data": "synthetic",
+                          "config": {"workload": "one call of every kernel family (REDUCED sizes, profiling table)",
+                                     "l2": "bandwidth-bound inputs > 126 MB"},
+                          "peaks": {"hbm_gbs": hbm, "hbm_kind": hkind, "bf16_tflops": tf_peak, "bf16_kind": tkind},
+                          "cases": rows, "cpu_baseline": None, "e2e": None}), flush=True)
+
+
 def c2_reference_time(min_seconds=2.0):
     """The reference's own AVX2 fp16 GEMV (helm/kernels/fp16_gemv.cpp, built into oracle/_ref) on the
     fp16-dequantised config-2 weights, every shape and M; median seconds per call."""
@@ -1398,6 +1655,15 @@ def main():
             run_reference_config2(args, rank)
         else:
             run_config2(args, rank, local, world)
+        return
+    if args.workload == "kernels":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "a per-kernel table of this library's CUDA "
+                                  "kernels has no reference counterpart (the reference has no GPU kernels)"}))
+            return
+        if rank == 0:
+            run_kernels(args, rank, local, world)
         return
     if args.workload == "prefill":
         if args.impl == "reference":

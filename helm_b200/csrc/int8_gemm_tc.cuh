@@ -258,8 +258,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
       uint8_t *bt = b_ring + bs * kBStageBytes;
 #pragma unroll
       for (int it = 0; it < 4; ++it) {
-        const int q = tc + 256 * it;          // (row r, logical chunk 4*half + lq) of the half-block
-        const int r = q >> 2, lq = q & 3;
+        // (row r, logical chunk 4*half + lq) of the half-block: the eight lanes of a quarter warp take
+        // eight consecutive rows at one lq, so their swizzled 16-byte chunks fall in distinct banks
+        // for both the int8 read and the two 16-bit writes.
+        const int r = ((((tc >> 5) << 2) + it) << 3) + (lane & 7), lq = lane >> 3;
         const int lc = 4 * half + lq;         // logical 16-value chunk of the packed row
         const int p = lc ^ (r & 7);           // where the packing stored it
         const uint4 v = *reinterpret_cast<const uint4 *>(raw + (r >> 4) * 2048 + (r & 15) * 128 + p * 16);
