@@ -7,24 +7,31 @@
 // conversion, fp32 accumulation, the per-channel scale and the bias applied once per output -- as
 // a dense contraction, so that prefill no longer builds a dequantised copy of the weight.
 //
-// CTA tile 128 (tokens) x 256 (output channels); k in steps of 64 (one 128-byte swizzle atom of
-// 16-bit values).  Three rings in shared memory, each with its own full / empty mbarriers:
-//   A  (x tiles, 16 KB, 4 deep)          filled by TMA, released by the MMAs (tcgen05.commit);
-//   W  (packed int8, 32 KB, 2 deep)       one packed block column (128 k) = two k steps, filled by
-//                                         bulk copies, released by the converters;
-//   B  (converted weights, 32 KB, 2 deep) written by the converters, released by the MMAs.
+// The weight is the A operand and lives in tensor memory; x is the B operand in shared memory:
+//   D[n, m] (128 channels x 256 tokens, fp32, tensor memory) += W[n, k] . x[m, k]
+// CTA tile 128 output channels x 256 tokens; k in steps of 64.  Each converted weight element feeds
+// 256 tokens, and the converted weights go from registers to tensor memory (tcgen05.st) instead of
+// through shared memory, which leaves shared memory to the x tiles and the int8 blocks.
+//   x   (256 tokens x 64 k, 32 KB, 4 deep)   shared memory, filled by TMA (128-byte swizzle), released
+//                                            by the MMAs (tcgen05.commit);
+//   W   (packed int8 block column: 128 channels x 128 k, 16 KB, 3 deep)  shared memory, filled by bulk
+//                                            copies, released by the converters;
+//   A   (converted 16-bit weights: 128 lanes x 32 columns per k step, 4 deep)  tensor memory, written
+//                                            by the converters, released by the MMAs.
 // Warp roles (320 threads):
 //   warp 0      producer: TMA for x, bulk copies for the packed weight blocks;
-//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 (M=128, N=256, K=16; A = x,
-//               B = w, both K-major 128-byte-swizzled shared-memory descriptors; D in tensor
-//               memory) four times per k step, then tcgen05.commit to the A and B empty barriers;
-//   warps 2-9   converters, then the epilogue: each k step's int8 half-block is rewritten as
-//               16-bit values (exact: |w| <= 127) in the canonical swizzled layout the tensor core
-//               reads, followed by fence.proxy.async and an mbarrier arrive; after the last k step
-//               they read the fp32 accumulators from tensor memory (tcgen05.ld; a warp reads its
-//               32-lane quadrant, two warps per quadrant split the 256 columns), apply scale and
-//               bias, and store y.
-// Tensor memory: 256 columns (the 128 x 256 fp32 accumulator), allocated by warp 0.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 with A in tensor memory (M=128
+//               channels, N=256 tokens, K=16; B = x, K-major 128-byte-swizzled descriptor; D in
+//               tensor memory) four times per k step, then tcgen05.commit to the x and A empty
+//               barriers;
+//   warps 2-9   converters, then the epilogue.  Warp w may address the tensor-memory lanes
+//               32*(w%4)..+31, so thread (w, l) owns channel row 32*(w%4) + l; warps 2-5 convert the
+//               first 32 k of each step, warps 6-9 the second.  A row's 32 int8 values (two 16-byte
+//               chunks of its packed block row) become 16 words of exact 16-bit pairs, stored with
+//               tcgen05.st into the stage's columns (column c holds k = 2c, 2c+1).  After the last k
+//               step the same threads read their channel's accumulators (tcgen05.ld, 32 tokens at a
+//               time), apply the channel's scale and bias and store y.
+// Tensor memory: 512 columns -- the 128 x 256 accumulator in columns 0-255, the A ring in 256-383.
 // Every mbarrier wait is bounded: a wait that gives up sets HELM_DEVERR_TIMEOUT in the library's
 // INT8 error word; the CTA then skips its remaining work and its stores, waits (bounded) for the
 // copies it issued, and frees its tensor memory.
@@ -34,15 +41,15 @@
 namespace helm {
 namespace {
 
-constexpr int GM = 128, GN = 256, GK = 64;       // CTA tile and k step
-constexpr int kAStages = 4, kWStages = 2, kBStages = 2;
-constexpr int kAStageBytes = GM * GK * 2;        // 16 KB: 128 rows x 128 B
-constexpr int kBStageBytes = GN * GK * 2;        // 32 KB: 256 rows x 128 B
-constexpr int kWStageBytes = GN * 128;           // 32 KB: 16 packed blocks (16 rows x 128 k)
-constexpr int kGSmem = kAStages * kAStageBytes + kWStages * kWStageBytes + kBStages * kBStageBytes + 1024;
+constexpr int GCH = 128, GTK = 256, GK = 64;     // CTA tile: channels x tokens; k step
+constexpr int kXStages = 4, kWStages = 3, kAStages = 4;
+constexpr int kXStageBytes = GTK * GK * 2;       // 32 KB: 256 token rows x 128 B
+constexpr int kWStageBytes = GCH * 128;          // 16 KB: 8 packed blocks (16 rows x 128 k)
+constexpr int kGSmem = kXStages * kXStageBytes + kWStages * kWStageBytes + 1024;
 constexpr int kConvWarps = 8;
 constexpr int kGThreads = (2 + kConvWarps) * 32;
-constexpr int kTmemCols = 256;
+constexpr int kTmemCols = 512;
+constexpr int kAccCol = 0, kACol0 = 256, kAStageCols = GK / 2;   // 32 columns of 16-bit pairs per k step
 
 __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr) {
   // K-major, 128-byte swizzle: leading byte offset 1 (16 B, unused for this layout), stride byte
@@ -61,17 +68,28 @@ template <> struct UFmt<__nv_bfloat16> { static constexpr uint32_t v = 1; };
 template <> struct UFmt<__half> { static constexpr uint32_t v = 0; };
 
 // kind::f16 instruction descriptor: fp32 accumulator, A and B of type XT, both K-major,
-// N = GN (n_dim = N >> 3), M = GM (m_dim = M >> 4).
+// N = GTK tokens (n_dim = N >> 3), M = GCH channels (m_dim = M >> 4).
 template <typename XT> __device__ __forceinline__ uint32_t umma_idesc() {
-  return (1u << 4) | (UFmt<XT>::v << 7) | (UFmt<XT>::v << 10) | ((uint32_t)(GN >> 3) << 17) |
-         ((uint32_t)(GM >> 4) << 24);
+  return (1u << 4) | (UFmt<XT>::v << 7) | (UFmt<XT>::v << 10) | ((uint32_t)(GTK >> 3) << 17) |
+         ((uint32_t)(GCH >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D[tmem_d] (+)= A[tmem_a] . B[desc]^T, A read from tensor memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 16 consecutive 32-bit columns of this thread's tensor-memory lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
 
@@ -101,17 +119,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Two floats rounded to XT, as one 32-bit word (first value in the low half).
-template <typename XT> __device__ __forceinline__ uint32_t pack2(float a, float b);
-template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
-  __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-
 // 16 int8 values -> 16 exact 16-bit values of XT, as two 16-byte chunks (the pairwise conversions
 // of the decode GEMV: int8 -> fp16 / bf16 without rounding).
 template <typename XT> __device__ __forceinline__ void cvt16(const uint4 &raw, uint4 &lo, uint4 &hi) {
@@ -132,37 +139,35 @@ __global__ void __launch_bounds__(kGThreads, 1)
                         const void *__restrict__ scale, int scale_dt, const XT *__restrict__ bias,
                         XT *__restrict__ y, int M, int N, int K) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t a_full[kAStages], a_empty[kAStages];
+  __shared__ __align__(8) uint64_t x_full[kXStages], x_empty[kXStages];
   __shared__ __align__(8) uint64_t w_full[kWStages], w_empty[kWStages];
-  __shared__ __align__(8) uint64_t b_full[kBStages], b_empty[kBStages];
+  __shared__ __align__(8) uint64_t a_full[kAStages], a_empty[kAStages];
   __shared__ __align__(8) uint64_t acc_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
-  __shared__ float s_scale[GN], s_bias[GN];
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *a_ring = smem;
-  uint8_t *w_ring = a_ring + kAStages * kAStageBytes;
-  uint8_t *b_ring = w_ring + kWStages * kWStageBytes;
+  uint8_t *x_ring = smem;
+  uint8_t *w_ring = x_ring + kXStages * kXStageBytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * GN, m0 = blockIdx.y * GM;
+  const int n0 = blockIdx.x * GCH, m0 = blockIdx.y * GTK;
   const int KB = (K + 127) / 128;          // packed block columns
   const int NK = (K + GK - 1) / GK;        // k steps
   const int n_tiles = (N + 15) / 16;
-  const int tiles = max(0, min(GN / 16, n_tiles - n0 / 16));   // packed 16-row tiles that exist
+  const int tiles = max(0, min(GCH / 16, n_tiles - n0 / 16));   // packed 16-row tiles that exist
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&a_full[s], 1);
-      mbar_init(&a_empty[s], 1);
+    for (int s = 0; s < kXStages; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);
     }
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&w_full[s], 1);
       mbar_init(&w_empty[s], kConvWarps);
     }
-    for (int s = 0; s < kBStages; ++s) {
-      mbar_init(&b_full[s], kConvWarps);
-      mbar_init(&b_empty[s], 1);
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&a_full[s], kConvWarps);
+      mbar_init(&a_empty[s], 1);
     }
     mbar_init(&acc_bar, 1);
     failed = 0;
@@ -189,7 +194,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      int a_issued = 0, w_issued = 0;
+      int x_issued = 0, w_issued = 0;
       for (int j = 0; j < NK && !*reinterpret_cast<volatile int *>(&failed); ++j) {
         if ((j & 1) == 0) {                       // the packed block column of k steps j, j + 1
           const int c = j >> 1, ws = c % kWStages;
@@ -203,18 +208,18 @@ __global__ void __launch_bounds__(kGThreads, 1)
                      &w_full[ws]);
           w_issued = c + 1;
         }
-        const int as = j % kAStages;
-        if (j >= kAStages && !mbar_wait(&a_empty[as], (uint32_t)((j / kAStages - 1) & 1))) {
+        const int xs = j % kXStages;
+        if (j >= kXStages && !mbar_wait(&x_empty[xs], (uint32_t)((j / kXStages - 1) & 1))) {
           give_up();
           break;
         }
-        mbar_arrive_expect_tx(&a_full[as], (uint32_t)kAStageBytes);
-        tma_load_2d(a_ring + as * kAStageBytes, &tmX, &a_full[as], j * GK, m0);
-        a_issued = j + 1;
+        mbar_arrive_expect_tx(&x_full[xs], (uint32_t)kXStageBytes);
+        tma_load_2d(x_ring + xs * kXStageBytes, &tmX, &x_full[xs], j * GK, m0);
+        x_issued = j + 1;
       }
       // the copies still in flight land before this CTA can finish
-      for (int j = max(0, a_issued - kAStages); j < a_issued; ++j)
-        if (!mbar_wait(&a_full[j % kAStages], (uint32_t)((j / kAStages) & 1))) give_up();
+      for (int j = max(0, x_issued - kXStages); j < x_issued; ++j)
+        if (!mbar_wait(&x_full[j % kXStages], (uint32_t)((j / kXStages) & 1))) give_up();
       for (int c = max(0, w_issued - kWStages); c < w_issued; ++c)
         if (!mbar_wait(&w_full[c % kWStages], (uint32_t)((c / kWStages) & 1))) give_up();
     }
@@ -223,59 +228,53 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = umma_idesc<XT>();
       for (int j = 0; j < NK; ++j) {
-        const int as = j % kAStages, bs = j % kBStages;
-        if (!mbar_wait(&a_full[as], (uint32_t)((j / kAStages) & 1)) ||
-            !mbar_wait(&b_full[bs], (uint32_t)((j / kBStages) & 1))) {
+        const int xs = j % kXStages, as = j % kAStages;
+        if (!mbar_wait(&x_full[xs], (uint32_t)((j / kXStages) & 1)) ||
+            !mbar_wait(&a_full[as], (uint32_t)((j / kAStages) & 1))) {
           give_up();
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a0 = smem_u32(a_ring + as * kAStageBytes), b0 = smem_u32(b_ring + bs * kBStageBytes);
+        const uint32_t b0 = smem_u32(x_ring + xs * kXStageBytes);
+        const uint32_t a0 = tmem + (uint32_t)(kACol0 + as * kAStageCols);
 #pragma unroll
         for (int kk = 0; kk < GK / 16; ++kk)
-          umma_f16(tmem, umma_smem_desc(a0 + kk * 32), umma_smem_desc(b0 + kk * 32), idesc, (j | kk) != 0);
+          umma_f16_ts(tmem + kAccCol, a0 + kk * 8, umma_smem_desc(b0 + kk * 32), idesc, (j | kk) != 0);
+        umma_commit(&x_empty[xs]);
         umma_commit(&a_empty[as]);
-        umma_commit(&b_empty[bs]);
       }
       umma_commit(&acc_bar);
     }
   } else {
     // ---------------- converters ----------------
-    const int tc = threadIdx.x - 64;   // 0..255
-    {  // the tile's scales and biases, for the epilogue
-      const int n = n0 + tc;
-      s_scale[tc] = n < N ? load_f(scale, scale_dt, n) : 0.f;
-      s_bias[tc] = (bias && n < N) ? Elem<XT>::to_f(bias[n]) : 0.f;
-    }
+    const int quad = warp & 3;                 // the tensor-memory lanes this warp may address
+    const int hk = (warp - 2) >> 2;            // which 32 k of a step
+    const int r = quad * 32 + lane;            // channel row of the tile
+    const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
     for (int j = 0; j < NK; ++j) {
-      const int c = j >> 1, ws = c % kWStages, half = j & 1, bs = j % kBStages;
+      const int c = j >> 1, ws = c % kWStages, js = j & 1, as = j % kAStages;
       if (!mbar_wait(&w_full[ws], (uint32_t)((c / kWStages) & 1)) ||
-          (j >= kBStages && !mbar_wait(&b_empty[bs], (uint32_t)((j / kBStages - 1) & 1)))) {
+          (j >= kAStages && !mbar_wait(&a_empty[as], (uint32_t)((j / kAStages - 1) & 1)))) {
         give_up();
         break;
       }
-      const uint8_t *raw = w_ring + ws * kWStageBytes;
-      uint8_t *bt = b_ring + bs * kBStageBytes;
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        // (row r, logical chunk 4*half + lq) of the half-block: the eight lanes of a quarter warp take
-        // eight consecutive rows at one lq, so their swizzled 16-byte chunks fall in distinct banks
-        // for both the int8 read and the two 16-bit writes.
-        const int r = ((((tc >> 5) << 2) + it) << 3) + (lane & 7), lq = lane >> 3;
-        const int lc = 4 * half + lq;         // logical 16-value chunk of the packed row
-        const int p = lc ^ (r & 7);           // where the packing stored it
-        const uint4 v = *reinterpret_cast<const uint4 *>(raw + (r >> 4) * 2048 + (r & 15) * 128 + p * 16);
-        uint4 lo, hi;
-        cvt16<XT>(v, lo, hi);
-        uint8_t *row = bt + r * 128;
-        *reinterpret_cast<uint4 *>(row + (((2 * lq) ^ (r & 7)) << 4)) = lo;
-        *reinterpret_cast<uint4 *>(row + (((2 * lq + 1) ^ (r & 7)) << 4)) = hi;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint8_t *row = w_ring + ws * kWStageBytes + (r >> 4) * 2048 + (r & 15) * 128;
+      const int lc = 4 * js + 2 * hk;          // first of this thread's two logical 16-value chunks
+      const uint4 v0 = *reinterpret_cast<const uint4 *>(row + ((lc ^ (r & 7)) << 4));
+      const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((lc + 1) ^ (r & 7)) << 4));
+      uint4 q0, q1, q2, q3;
+      cvt16<XT>(v0, q0, q1);
+      cvt16<XT>(v1, q2, q3);
+      const uint32_t w[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                              q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+      tmem_st16(tmem + lane_addr + (uint32_t)(kACol0 + as * kAStageCols + hk * 16), w);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&b_full[bs]);
-        if (half == 1 || j == NK - 1) mbar_arrive(&w_empty[ws]);
+        mbar_arrive(&a_full[as]);
+        if (js == 1 || j == NK - 1) mbar_arrive(&w_empty[ws]);
       }
     }
     // ---------------- epilogue ----------------
@@ -283,36 +282,19 @@ __global__ void __launch_bounds__(kGThreads, 1)
       give_up();
     } else {
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      // the scales written by the other converter warps (named barrier of the eight warps)
-      asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
-      const int quad = warp & 3;                 // the TMEM lanes this warp may read
-      const int col0 = ((warp - 2) >> 2) * 128;  // which half of the 256 columns
-      const int m = m0 + quad * 32 + lane;
-      const bool store = m < M && !*reinterpret_cast<volatile int *>(&failed);
-      const bool vec = (N & 7) == 0;             // rows of y 16-byte aligned
+      const int n = n0 + r;
+      const float sc = n < N ? load_f(scale, scale_dt, n) : 0.f;
+      const float bi = (bias && n < N) ? Elem<XT>::to_f(bias[n]) : 0.f;
+      const bool store = n < N && !*reinterpret_cast<volatile int *>(&failed);
 #pragma unroll 1
-      for (int c0 = col0; c0 < col0 + 128; c0 += 32) {
+      for (int c0 = hk * 128; c0 < hk * 128 + 128; c0 += 32) {
         float acc[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0, acc);
+        tmem_ld32(tmem + lane_addr + (uint32_t)(kAccCol + c0), acc);
         if (!store) continue;
+        XT *dst = y + (int64_t)(m0 + c0) * N + n;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) acc[jj] = fmaf(acc[jj], s_scale[c0 + jj], s_bias[c0 + jj]);
-        XT *dst = y + (int64_t)m * N + n0 + c0;
-        if (vec && n0 + c0 + 32 <= N) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 q;
-            q.x = pack2<XT>(acc[8 * v + 0], acc[8 * v + 1]);
-            q.y = pack2<XT>(acc[8 * v + 2], acc[8 * v + 3]);
-            q.z = pack2<XT>(acc[8 * v + 4], acc[8 * v + 5]);
-            q.w = pack2<XT>(acc[8 * v + 6], acc[8 * v + 7]);
-            reinterpret_cast<uint4 *>(dst)[v] = q;
-          }
-        } else {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj)
-            if (n0 + c0 + jj < N) dst[jj] = Elem<XT>::from_f(acc[jj]);
-        }
+        for (int jj = 0; jj < 32; ++jj)
+          if (m0 + c0 + jj < M) dst[(int64_t)jj * N] = Elem<XT>::from_f(fmaf(acc[jj], sc, bi));
       }
     }
   }
@@ -325,13 +307,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
   }
 }
 
-// 2-D map over x [M, K] (16-bit): box 64 k x 128 rows, 128-byte swizzle, zero fill past the edges.
+// 2-D map over x [M, K] (16-bit): box 64 k x 256 tokens, 128-byte swizzle, zero fill past the edges.
 bool x_map_sw128(CUtensorMap *m, const void *x, int xdt, int M, int K) {
   auto enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)M};
   cuuint64_t gstr[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)GM};
+  cuuint32_t box[2] = {64, (cuuint32_t)GTK};
   cuuint32_t estr[2] = {1, 1};
   return enc(m, xdt == HELM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
              const_cast<void *>(x), gdim, gstr, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -359,7 +341,7 @@ int launch_gemm(const void *x, int xdt, const int8_t *wpk, const void *scale, in
   }
   CUtensorMap xm;
   if (!x_map_sw128(&xm, x, xdt, M, K)) return fail(HELM_ERR_CUDA, "int8_gemm: cuTensorMapEncodeTiled failed");
-  const dim3 grid((N + GN - 1) / GN, (M + GM - 1) / GM);
+  const dim3 grid((N + GCH - 1) / GCH, (M + GTK - 1) / GTK);
   const cudaError_t e = launch_pdl(int8_gemm_tc_kernel<XT>, grid, dim3(kGThreads), kGSmem, st, xm, wpk, scale, sdt,
                                    static_cast<const XT *>(bias), static_cast<XT *>(y), M, N, K);
   if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "int8_gemm: launch: %s", cudaGetErrorString(e));
@@ -383,7 +365,7 @@ extern "C" int helm_int8_gemm_packed(const void *x, int32_t x_dtype, const int8_
   if (!x || !packed || !w_scale || !y) return fail(HELM_ERR_INVALID_ARGUMENT, "int8_gemm: null pointer");
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(packed)) & 15)
     return fail(HELM_ERR_INVALID_ARGUMENT, "int8_gemm: x and packed must be 16-byte aligned");
-  if ((int64_t)(M + GM - 1) / GM > 65535) return fail(HELM_ERR_UNSUPPORTED, "int8_gemm: M=%d too large", M);
+  if ((int64_t)(M + GTK - 1) / GTK > 65535) return fail(HELM_ERR_UNSUPPORTED, "int8_gemm: M=%d too large", M);
   cudaStream_t st = as_stream(stream);
   return x_dtype == HELM_F16 ? launch_gemm<__half>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, N, K, st)
                              : launch_gemm<__nv_bfloat16>(x, x_dtype, packed, w_scale, scale_dtype, bias, y, M, N, K,

@@ -84,23 +84,49 @@ __device__ void resolve_dest(const AppendArgs &a, int b, int local, int &pid_out
   slot_out = slot;
 }
 
-// One CTA per sequence: thread 0 resolves the destination (page id, slot),
-// then the CTA copies Hkv*D elements of K and of V.
+// One CTA per sequence: thread 0 resolves the destination (page id, slot) while every thread
+// loads its share of the new token's K and V; then the CTA stores Hkv*D elements of each.
+constexpr int kAppendPre = 4;   // elements of K (and of V) a thread holds across the barrier
+
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   __shared__ int s_pid, s_slot;
   const int b = a.b0 + blockIdx.x;
   // Programmatic dependent launch: only the launch overlaps the previous kernel.
   pdl_trigger();
   pdl_wait();
+  const int n = a.Hkv * a.D;
+  const bool pre = n <= kAppendPre * (int)blockDim.x;
+  float kr[kAppendPre], vr[kAppendPre];
+  if (pre) {
+#pragma unroll
+    for (int j = 0; j < kAppendPre; ++j) {
+      const int i = threadIdx.x + j * blockDim.x;
+      kr[j] = i < n ? load_f(a.k_new, a.src_dtype, (int64_t)b * n + i) : 0.f;
+      vr[j] = i < n ? load_f(a.v_new, a.src_dtype, (int64_t)b * n + i) : 0.f;
+    }
+  }
   if (threadIdx.x == 0) resolve_dest(a, b, blockIdx.x, s_pid, s_slot);
   __syncthreads();
   const int pid = s_pid, slot = s_slot;
   if (pid < 0) return;
-  const int n = a.Hkv * a.D;
+  const int64_t base = (int64_t)pid * a.page_stride + (int64_t)slot * a.D;
+  if (pre) {
+#pragma unroll
+    for (int j = 0; j < kAppendPre; ++j) {
+      const int i = threadIdx.x + j * blockDim.x;
+      if (i < n) {
+        const int h = i / a.D, d = i - h * a.D;
+        const int64_t dst = base + (int64_t)h * a.head_stride + d;
+        store_f(a.k_base, a.kv_dtype, dst, kr[j]);
+        store_f(a.v_base, a.kv_dtype, dst, vr[j]);
+      }
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int h = i / a.D, d = i - h * a.D;
     const int64_t src = (int64_t)b * n + i;
-    const int64_t dst = (int64_t)pid * a.page_stride + (int64_t)h * a.head_stride + (int64_t)slot * a.D + d;
+    const int64_t dst = base + (int64_t)h * a.head_stride + d;
     store_f(a.k_base, a.kv_dtype, dst, load_f(a.k_new, a.src_dtype, src));
     store_f(a.v_base, a.kv_dtype, dst, load_f(a.v_new, a.src_dtype, src));
   }
@@ -109,9 +135,15 @@ __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
 // ---------------------------------------------------------------------------
 // Decode prologue: per-head RMSNorm of q and k (Qwen3 q_norm / k_norm), rotary
 // embedding of q and k (x*cos + rotate_half(x)*sin, rotate_half(x) =
-// (-x[D/2:], x[:D/2])), q written out, k and v appended to the pool.  One CTA
-// per sequence, one warp per head; lane l owns the rotary pairs
-// (d, d + D/2) for d = l, l + 32, ...
+// (-x[D/2:], x[:D/2])), q written out, k and v appended to the pool.
+// Grid (sequences, 1 + ceil(Hq / 8)) of 8-warp CTAs, one warp per head:
+//   y = 0   the sequence's append: thread 0 resolves the destination while the
+//           warps normalise and rotate the k heads (and load the v heads) into
+//           shared memory; after the barrier the CTA stores them into the slot;
+//   y >= 1  eight query heads each, written to q_out.
+// A head's loads (x, norm weights, cos, sin) are all issued before any of them
+// is used, so each head costs one memory round trip.  Lane l owns the rotary
+// pairs (d, d + D/2) for d = l, l + 32, ...
 // ---------------------------------------------------------------------------
 struct PrologueArgs {
   const void *q_in;
@@ -128,103 +160,107 @@ struct PrologueArgs {
 };
 
 constexpr int kMaxHalfPerLane = 4;  // D <= 256
+constexpr int kProWarps = 8;
 
 __device__ __forceinline__ void norm_rope_head(const void *src, int src_dt, int64_t src_off, const void *w,
                                                int w_dt, float eps, const void *cs_cos, const void *cs_sin,
                                                int cs_dt, int64_t cs_off, int D, int lane,
                                                float (&lo)[kMaxHalfPerLane], float (&hi)[kMaxHalfPerLane]) {
   const int half = D >> 1;
-  float ss = 0.f;
+  float w0[kMaxHalfPerLane], w1[kMaxHalfPerLane], c0[kMaxHalfPerLane], c1[kMaxHalfPerLane];
+  float s0[kMaxHalfPerLane], s1[kMaxHalfPerLane];
 #pragma unroll
   for (int i = 0; i < kMaxHalfPerLane; ++i) {
     const int d = lane + 32 * i;
-    lo[i] = hi[i] = 0.f;
-    if (d < half) {
-      lo[i] = load_f(src, src_dt, src_off + d);
-      hi[i] = load_f(src, src_dt, src_off + d + half);
-      ss = fmaf(lo[i], lo[i], fmaf(hi[i], hi[i], ss));
-    }
+    const bool in = d < half;
+    lo[i] = in ? load_f(src, src_dt, src_off + d) : 0.f;
+    hi[i] = in ? load_f(src, src_dt, src_off + d + half) : 0.f;
+    w0[i] = in && w ? load_f(w, w_dt, d) : 0.f;
+    w1[i] = in && w ? load_f(w, w_dt, d + half) : 0.f;
+    c0[i] = in && cs_cos ? load_f(cs_cos, cs_dt, cs_off + d) : 0.f;
+    c1[i] = in && cs_cos ? load_f(cs_cos, cs_dt, cs_off + d + half) : 0.f;
+    s0[i] = in && cs_cos ? load_f(cs_sin, cs_dt, cs_off + d) : 0.f;
+    s1[i] = in && cs_cos ? load_f(cs_sin, cs_dt, cs_off + d + half) : 0.f;
   }
   if (w) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxHalfPerLane; ++i)
+      if (lane + 32 * i < half) ss = fmaf(lo[i], lo[i], fmaf(hi[i], hi[i], ss));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     const float r = rsqrtf(ss / (float)D + eps);
 #pragma unroll
     for (int i = 0; i < kMaxHalfPerLane; ++i) {
-      const int d = lane + 32 * i;
-      if (d < half) {
-        lo[i] = lo[i] * r * load_f(w, w_dt, d);
-        hi[i] = hi[i] * r * load_f(w, w_dt, d + half);
-      }
+      lo[i] = lo[i] * r * w0[i];
+      hi[i] = hi[i] * r * w1[i];
     }
   }
   if (cs_cos) {
 #pragma unroll
     for (int i = 0; i < kMaxHalfPerLane; ++i) {
-      const int d = lane + 32 * i;
-      if (d < half) {
-        const float c0 = load_f(cs_cos, cs_dt, cs_off + d), c1 = load_f(cs_cos, cs_dt, cs_off + d + half);
-        const float s0 = load_f(cs_sin, cs_dt, cs_off + d), s1 = load_f(cs_sin, cs_dt, cs_off + d + half);
-        const float x0 = lo[i], x1 = hi[i];
-        lo[i] = x0 * c0 - x1 * s0;  // rotate_half: first half takes -x[d + D/2]
-        hi[i] = x1 * c1 + x0 * s1;  // second half takes x[d]
-      }
+      const float x0 = lo[i], x1 = hi[i];
+      lo[i] = x0 * c0[i] - x1 * s0[i];  // rotate_half: first half takes -x[d + D/2]
+      hi[i] = x1 * c1[i] + x0 * s1[i];  // second half takes x[d]
     }
   }
 }
 
-__global__ void __launch_bounds__(256) decode_prologue_kernel(AppendArgs a, PrologueArgs pr) {
+__global__ void __launch_bounds__(kProWarps * 32) decode_prologue_kernel(AppendArgs a, PrologueArgs pr) {
+  extern __shared__ float kv_stage[];   // [2 * Hkv][D]: k heads after norm + rope, then v heads
   __shared__ int s_pid, s_slot;
   const int b = a.b0 + blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = a.D, half = D >> 1;
+  const int64_t cs_off = (int64_t)b * pr.cs_stride;
   pdl_trigger();
   pdl_wait();
-  if (threadIdx.x == 0) {
-    if (pr.do_append) {
-      resolve_dest(a, b, blockIdx.x, s_pid, s_slot);
-    } else {
-      s_pid = -1;
-      s_slot = -1;
+  float lo[kMaxHalfPerLane], hi[kMaxHalfPerLane];
+  if (blockIdx.y > 0) {  // query head: norm + rope -> q_out
+    const int t = (blockIdx.y - 1) * kProWarps + warp;
+    if (t >= pr.Hq) return;
+    norm_rope_head(pr.q_in, a.src_dtype, (int64_t)b * pr.q_stride + (int64_t)t * D, pr.q_norm_w, pr.norm_dtype,
+                   pr.eps, pr.cos, pr.sin, pr.cs_dtype, cs_off, D, lane, lo, hi);
+    const int64_t o = ((int64_t)b * pr.Hq + t) * D;
+#pragma unroll
+    for (int i = 0; i < kMaxHalfPerLane; ++i) {
+      const int d = lane + 32 * i;
+      if (d < half) {
+        store_f(pr.q_out, a.src_dtype, o + d, lo[i]);
+        store_f(pr.q_out, a.src_dtype, o + d + half, hi[i]);
+      }
+    }
+    return;
+  }
+  if (!pr.do_append) return;
+  if (threadIdx.x == 0) resolve_dest(a, b, blockIdx.x, s_pid, s_slot);
+  for (int t = warp; t < 2 * a.Hkv; t += kProWarps) {
+    float *row = kv_stage + (int64_t)t * D;
+    if (t < a.Hkv) {  // key head: norm + rope
+      norm_rope_head(a.k_new, a.src_dtype, (int64_t)b * pr.k_stride + (int64_t)t * D, pr.k_norm_w, pr.norm_dtype,
+                     pr.eps, pr.cos, pr.sin, pr.cs_dtype, cs_off, D, lane, lo, hi);
+#pragma unroll
+      for (int i = 0; i < kMaxHalfPerLane; ++i) {
+        const int d = lane + 32 * i;
+        if (d < half) {
+          row[d] = lo[i];
+          row[d + half] = hi[i];
+        }
+      }
+    } else {  // value head: as given
+      const int64_t src = (int64_t)b * pr.v_stride + (int64_t)(t - a.Hkv) * D;
+      for (int d = lane; d < D; d += 32) row[d] = load_f(a.v_new, a.src_dtype, src + d);
     }
   }
   __syncthreads();
   const int pid = s_pid, slot = s_slot;
-  const int D = a.D, half = D >> 1;
-  const int tasks = pr.Hq + (pr.do_append && pid >= 0 ? 2 * a.Hkv : 0);
-  const int64_t cs_off = (int64_t)b * pr.cs_stride;
-  for (int t = warp; t < tasks; t += nwarps) {
-    float lo[kMaxHalfPerLane], hi[kMaxHalfPerLane];
-    if (t < pr.Hq) {  // query head: norm + rope -> q_out
-      norm_rope_head(pr.q_in, a.src_dtype, (int64_t)b * pr.q_stride + (int64_t)t * D, pr.q_norm_w, pr.norm_dtype,
-                     pr.eps, pr.cos, pr.sin, pr.cs_dtype, cs_off, D, lane, lo, hi);
-      const int64_t o = ((int64_t)b * pr.Hq + t) * D;
-#pragma unroll
-      for (int i = 0; i < kMaxHalfPerLane; ++i) {
-        const int d = lane + 32 * i;
-        if (d < half) {
-          store_f(pr.q_out, a.src_dtype, o + d, lo[i]);
-          store_f(pr.q_out, a.src_dtype, o + d + half, hi[i]);
-        }
-      }
-    } else if (t < pr.Hq + a.Hkv) {  // key head: norm + rope -> pool
-      const int h = t - pr.Hq;
-      norm_rope_head(a.k_new, a.src_dtype, (int64_t)b * pr.k_stride + (int64_t)h * D, pr.k_norm_w, pr.norm_dtype,
-                     pr.eps, pr.cos, pr.sin, pr.cs_dtype, cs_off, D, lane, lo, hi);
-      const int64_t dst = (int64_t)pid * a.page_stride + (int64_t)h * a.head_stride + (int64_t)slot * D;
-#pragma unroll
-      for (int i = 0; i < kMaxHalfPerLane; ++i) {
-        const int d = lane + 32 * i;
-        if (d < half) {
-          store_f(a.k_base, a.kv_dtype, dst + d, lo[i]);
-          store_f(a.k_base, a.kv_dtype, dst + d + half, hi[i]);
-        }
-      }
-    } else {  // value head: copy -> pool
-      const int h = t - pr.Hq - a.Hkv;
-      const int64_t src = (int64_t)b * pr.v_stride + (int64_t)h * D;
-      const int64_t dst = (int64_t)pid * a.page_stride + (int64_t)h * a.head_stride + (int64_t)slot * D;
-      for (int d = lane; d < D; d += 32) store_f(a.v_base, a.kv_dtype, dst + d, load_f(a.v_new, a.src_dtype, src + d));
-    }
+  if (pid < 0) return;
+  const int64_t base = (int64_t)pid * a.page_stride + (int64_t)slot * D;
+  for (int i = threadIdx.x; i < 2 * a.Hkv * D; i += blockDim.x) {
+    const int t = i / D, d = i - t * D;
+    const bool is_k = t < a.Hkv;
+    const int64_t dst = base + (int64_t)(is_k ? t : t - a.Hkv) * a.head_stride + d;
+    store_f(is_k ? a.k_base : a.v_base, a.kv_dtype, dst, kv_stage[i]);
   }
 }
 
@@ -349,8 +385,17 @@ extern "C" int helm_decode_prologue(const helm_decode_prologue_params *p, void *
   pr.cs_dtype = p->cs_dtype;
   pr.cs_stride = p->cs_stride;
   pr.do_append = p->do_append;
+  const size_t smem = p->do_append ? sizeof(float) * 2 * (size_t)ap->Hkv * ap->D : 0;
+  if (smem > 200 * 1024)
+    return fail(HELM_ERR_UNSUPPORTED, "decode_prologue: 2*Hkv*D = %d staged values exceed 200 KB", 2 * ap->Hkv * ap->D);
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(decode_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem);
+    if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "decode_prologue: %s", cudaGetErrorString(e));
+  }
   cudaStream_t st = as_stream(stream);
+  const unsigned qblocks = (unsigned)((p->Hq + kProWarps - 1) / kProWarps);
   return launch_rows(ap, append_args(ap), [&](const AppendArgs &a, int blocks) {
-    launch_pdl(decode_prologue_kernel, dim3(blocks), dim3(256), 0, st, a, pr);
+    launch_pdl(decode_prologue_kernel, dim3(blocks, 1 + qblocks), dim3(kProWarps * 32), smem, st, a, pr);
   }, "decode_prologue_kernel");
 }

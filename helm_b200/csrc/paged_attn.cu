@@ -39,6 +39,7 @@ struct AttnArgs {
   const int32_t *num_pages;
   int32_t pt_stride;
   int32_t B, Hq, Hkv, D, P, gq;
+  int32_t head_chunks;   // warp kernel: CTAs per (split, kv head, sequence) along the GQA group
   int32_t q_dtype, out_dtype;
   float scale_log2;      // softmax scale * log2(e)
   int32_t num_splits;
@@ -327,9 +328,11 @@ template <typename KT, int DPL, int GQ>
 __global__ void __launch_bounds__(kWWarps * 32) attn_warp_kernel(AttnArgs a) {
   extern __shared__ float smem_w[];   // [warps][GQ][D] o, then [warps][GQ] m, [warps][GQ] l
   constexpr int D = 32 * DPL;
-  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  // blockIdx.y = (kv head g, head chunk): this CTA serves query heads [h0, h0 + gn) of g's group.
+  const int s = blockIdx.x, g = blockIdx.y / a.head_chunks, b = blockIdx.z;
+  const int h0 = (blockIdx.y - g * a.head_chunks) * GQ;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gq = a.gq;
+  const int gq = a.gq, gn = min(GQ, gq - h0), hq0 = g * gq + h0;
   float *o_s = smem_w;
   float *m_s = o_s + kWWarps * GQ * D;
   float *l_s = m_s + kWWarps * GQ;
@@ -343,7 +346,7 @@ __global__ void __launch_bounds__(kWWarps * 32) attn_warp_kernel(AttnArgs a) {
   for (int h = 0; h < GQ; ++h)
 #pragma unroll
     for (int j = 0; j < DPL; ++j)
-      q[h][j] = h < gq ? load_f(a.q, a.q_dtype, ((int64_t)b * a.Hq + g * gq + h) * D + lane * DPL + j) * a.scale_log2
+      q[h][j] = h < gn ? load_f(a.q, a.q_dtype, ((int64_t)b * a.Hq + hq0 + h) * D + lane * DPL + j) * a.scale_log2
                        : 0.f;
   float m[GQ], l[GQ], o[GQ][DPL];
 #pragma unroll
@@ -404,7 +407,7 @@ __global__ void __launch_bounds__(kWWarps * 32) attn_warp_kernel(AttnArgs a) {
           for (int t = 0; t < kOct; ++t) sc[h][t] += __shfl_xor_sync(0xffffffffu, sc[h][t], off);
 #pragma unroll
       for (int h = 0; h < GQ; ++h) {
-        if (h >= gq) break;
+        if (h >= gn) break;
         float mx = m[h];
 #pragma unroll
         for (int t = 0; t < kOct; ++t)
@@ -440,7 +443,7 @@ __global__ void __launch_bounds__(kWWarps * 32) attn_warp_kernel(AttnArgs a) {
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < gq * D; i += blockDim.x) {
+  for (int i = threadIdx.x; i < gn * D; i += blockDim.x) {
     const int h = i / D, d = i - h * D;
     float M = -INFINITY;
 #pragma unroll
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(kWWarps * 32) attn_warp_kernel(AttnArgs a) {
       O = fmaf(o_s[(w * GQ + h) * D + d], wt, O);
     }
     if (M == -INFINITY) { L = 0.f; O = 0.f; }
-    emit(a, s, b, g * gq + h, d, M, L, O);
+    emit(a, s, b, hq0 + h, d, M, L, O);
   }
 }
 
@@ -1646,30 +1649,56 @@ bool tc_eligible(const helm_paged_attn_params *p) {
   return true;
 }
 
-// The warp-per-octet kernel: D in {64, 128, 256}, GQA group <= 8 (<= 4 at D = 256), and the
-// vector loads' alignment (a lane reads D/32 consecutive elements of a row).
+// The warp-per-octet kernel: D a multiple of 32 up to 256 (a lane owns D/32 consecutive elements
+// of a row; D = 224 excepted), any GQA group: the group's query heads are served GQ at a time
+// (GQ <= 8, GQ * D/32 <= 32 registers per row of state), one CTA per chunk of GQ heads.
+struct WarpCfg {
+  int GQ = 0;      // heads per CTA (a power of two)
+  int chunks = 0;  // CTAs along the GQA group
+};
+
+WarpCfg warp_cfg(int gq, int D) {
+  WarpCfg c;
+  if (D <= 0 || D % 32 != 0 || D > 256 || D == 224 || gq <= 0) return c;
+  const int dpl = D / 32;
+  int cap = 8;
+  while (cap * dpl > 32) cap >>= 1;
+  int GQ = 1;
+  while (GQ < gq && GQ < cap) GQ *= 2;
+  c.GQ = GQ;
+  c.chunks = (gq + GQ - 1) / GQ;
+  return c;
+}
+
 bool warp_eligible(const helm_paged_attn_params *p) {
   if (env_flag("HELM_B200_FORCE_GENERIC")) return false;
-  if (p->D != 64 && p->D != 128 && p->D != 256) return false;
-  const int gq = p->Hq / p->Hkv;
+  if (p->Hkv <= 0 || p->Hq % p->Hkv != 0) return false;
+  const WarpCfg c = warp_cfg(p->Hq / p->Hkv, p->D);
+  if (c.GQ == 0) return false;
   const int dpl = p->D / 32;
-  int GQ = 1;
-  while (GQ < gq) GQ *= 2;
-  if (GQ > 8 || GQ * dpl > 32) return false;
   const int es = dtype_size(p->kv_dtype);
-  int vb = es == 4 ? (dpl % 4 == 0 ? 16 : 8) : (dpl % 8 == 0 ? 16 : 8);
+  // the alignment of RowLoad's widest access for this row length
+  int vb;
+  if (es == 4) vb = dpl % 4 == 0 ? 16 : dpl % 2 == 0 ? 8 : 4;
+  else vb = dpl % 8 == 0 ? 16 : dpl % 4 == 0 ? 8 : 2;
   const uintptr_t kb = reinterpret_cast<uintptr_t>(p->k_base), vbp = reinterpret_cast<uintptr_t>(p->v_base);
   return kb % vb == 0 && vbp % vb == 0 && (p->page_stride * es) % vb == 0 && (p->head_stride * es) % vb == 0;
 }
 
+int warp_ctas_per_sm(int kv_dtype, int D, int gq);
+
 int resolve_splits(const helm_paged_attn_params *p) {
   if (p->num_splits > 0) return p->num_splits;
   if (!tc_eligible(p) && warp_eligible(p)) {
-    // up to four CTAs of 4 warps per SM (the register budget keeps four resident), every CTA with
-    // at least one page: the whole grid runs in one wave with most of the call's K/V in flight
-    const int pairs = p->B * p->Hkv;
+    // as many CTAs as are resident at once (the instantiation's registers decide: 2 to 4 per SM),
+    // every CTA with at least one page: the whole grid runs in one wave with most of the call's
+    // K/V in flight
+    const int gq = p->Hq / p->Hkv;
+    const int pairs = p->B * p->Hkv * warp_cfg(gq, p->D).chunks;
     if (pairs <= 0 || p->max_pages <= 1) return 1;
-    int S = (4 * num_sms() + pairs - 1) / pairs;
+    const int per_sm = warp_ctas_per_sm(p->kv_dtype, p->D, gq);
+    int S = (per_sm > 4 ? 4 : per_sm) * num_sms() / pairs;
+    if (S < 1) S = 1;
     return S > p->max_pages ? p->max_pages : S;
   }
   const int pairs = p->B * p->Hkv;
@@ -1786,32 +1815,83 @@ int launch_generic(const AttnArgs &a, cudaStream_t st) {
   return check_launch("attn_generic_kernel");
 }
 
+// query = false: launch; query = true: return how many CTAs of the instantiation fit on an SM
+// (0 when no instantiation serves the shape).
 template <typename KT, int DPL, int GQ>
-int launch_warp_cfg(const AttnArgs &a, cudaStream_t st) {
+int launch_warp_cfg(AttnArgs a, int chunks, cudaStream_t st, bool query) {
   const size_t smem = warp_smem_bytes(GQ, 32 * DPL);
   ensure_smem_attr(attn_warp_kernel<KT, DPL, GQ>, (int)smem);
-  const cudaError_t e = launch_pdl(attn_warp_kernel<KT, DPL, GQ>, dim3(a.num_splits, a.Hkv, a.B), dim3(kWWarps * 32),
-                                   smem, st, a);
+  if (query) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_warp_kernel<KT, DPL, GQ>, kWWarps * 32, smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return 1;
+    }
+    return n > 0 ? n : 1;
+  }
+  a.head_chunks = chunks;
+  const cudaError_t e = launch_pdl(attn_warp_kernel<KT, DPL, GQ>, dim3(a.num_splits, a.Hkv * chunks, a.B),
+                                   dim3(kWWarps * 32), smem, st, a);
   if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: launch: %s", cudaGetErrorString(e));
   return check_launch("attn_warp_kernel");
 }
 
 template <typename KT, int DPL>
-int launch_warp_d(const AttnArgs &a, cudaStream_t st) {
-  if (a.gq <= 1) return launch_warp_cfg<KT, DPL, 1>(a, st);
-  if (a.gq <= 2) return launch_warp_cfg<KT, DPL, 2>(a, st);
-  if (a.gq <= 4) return launch_warp_cfg<KT, DPL, 4>(a, st);
-  if constexpr (DPL <= 4) return launch_warp_cfg<KT, DPL, 8>(a, st);
+int launch_warp_d(const AttnArgs &a, cudaStream_t st, bool query) {
+  const WarpCfg c = warp_cfg(a.gq, a.D);
+  if (c.GQ == 1) return launch_warp_cfg<KT, DPL, 1>(a, c.chunks, st, query);
+  if (c.GQ == 2) return launch_warp_cfg<KT, DPL, 2>(a, c.chunks, st, query);
+  if constexpr (DPL <= 8) {
+    if (c.GQ == 4) return launch_warp_cfg<KT, DPL, 4>(a, c.chunks, st, query);
+  }
+  if constexpr (DPL <= 4) {
+    if (c.GQ == 8) return launch_warp_cfg<KT, DPL, 8>(a, c.chunks, st, query);
+  }
+  if (query) return 0;
   return fail(HELM_ERR_UNSUPPORTED, "paged_attn: GQA group %d at head dim %d", a.gq, a.D);
 }
 
 template <typename KT>
-int launch_warp(const AttnArgs &a, cudaStream_t st) {
+int launch_warp(const AttnArgs &a, cudaStream_t st, bool query = false) {
   switch (a.D) {
-    case 64: return launch_warp_d<KT, 2>(a, st);
-    case 128: return launch_warp_d<KT, 4>(a, st);
-    default: return launch_warp_d<KT, 8>(a, st);
+    case 32: return launch_warp_d<KT, 1>(a, st, query);
+    case 64: return launch_warp_d<KT, 2>(a, st, query);
+    case 96: return launch_warp_d<KT, 3>(a, st, query);
+    case 128: return launch_warp_d<KT, 4>(a, st, query);
+    case 160: return launch_warp_d<KT, 5>(a, st, query);
+    case 192: return launch_warp_d<KT, 6>(a, st, query);
+    case 256: return launch_warp_d<KT, 8>(a, st, query);
+    default:
+      if (query) return 0;
+      return fail(HELM_ERR_UNSUPPORTED, "paged_attn: head dim %d on the warp kernel", a.D);
   }
+}
+
+int warp_ctas_per_sm(int kv_dtype, int D, int gq) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, int>, std::pair<int, int>>> cache;  // ((dtype, D), (gq, n))
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int key = kv_dtype * 4096 + D, key2 = dev * 65536 + gq;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto &c : cache)
+      if (c.first.first == key && c.first.second == key2) return c.second.first;
+  }
+  AttnArgs a{};
+  a.D = D;
+  a.gq = gq;
+  int n = 0;
+  switch (kv_dtype) {
+    case HELM_F32: n = launch_warp<float>(a, nullptr, true); break;
+    case HELM_F16: n = launch_warp<__half>(a, nullptr, true); break;
+    default: n = launch_warp<__nv_bfloat16>(a, nullptr, true); break;
+  }
+  if (n < 1) n = 1;
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({{key, key2}, {n, 0}});
+  return n;
 }
 
 template <typename T, int NT>

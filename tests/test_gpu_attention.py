@@ -121,6 +121,51 @@ def test_random_pool_tensor_core_path(dtype, gq, splits, cuda):
     assert_attn_close(out, ref, dtype, f"gq={gq} splits={splits}")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [32, 64, 96, 160, 192, 256])
+@pytest.mark.parametrize("gq", [1, 3, 12, 24])
+@pytest.mark.parametrize("splits", [0, 2])
+def test_warp_kernel_head_dims_and_groups(dtype, D, gq, splits, cuda):
+    """The CUDA-core warp kernel over head dims that are multiples of 32 and GQA groups of any size
+    (served in chunks of up to 8 heads per CTA), P = 16 pages, ragged lengths."""
+    torch.manual_seed(2000 + D + gq)
+    Hkv, P = 2, 16
+    Hq = Hkv * gq
+    lens = [1, 100, 250]
+    npages = [math.ceil(n / P) for n in lens]
+    total = sum(npages) + 3
+    kp = torch.randn(total, Hkv, P, D).to(dtype)
+    vp = torch.randn(total, Hkv, P, D).to(dtype)
+    perm = torch.randperm(total).tolist()
+    tables, useds, i = [], [], 0
+    for n, npg in zip(lens, npages):
+        tables.append(perm[i:i + npg])
+        useds.append([P] * (npg - 1) + [n - P * (npg - 1)])
+        i += npg
+    q = torch.randn(3, Hq, D).to(dtype)
+    out = run_pages(q.to(cuda), kp.to(cuda), vp.to(cuda), tables, useds, npages, P=P, num_splits=splits,
+                    out_dtype=torch.float32)
+    ref = OA.paged_attention_torch(q, kp, vp, torch.tensor([t + [0] * (max(npages) - len(t)) for t in tables]),
+                                   torch.tensor([u + [0] * (max(npages) - len(u)) for u in useds]),
+                                   torch.tensor(npages))
+    assert_attn_close(out, ref, dtype, f"D={D} gq={gq} splits={splits}")
+
+
+def test_warp_kernel_matches_generic_kernel(cuda, monkeypatch):
+    """A group of 24 at D = 96 on the warp kernel (three head chunks) and on the generic kernel."""
+    torch.manual_seed(9)
+    Hkv, D, P, gq = 2, 96, 64, 24
+    kp = torch.randn(30, Hkv, P, D, dtype=torch.bfloat16, device=cuda)
+    vp = torch.randn(30, Hkv, P, D, dtype=torch.bfloat16, device=cuda)
+    q = torch.randn(2, Hkv * gq, D, dtype=torch.bfloat16, device=cuda)
+    tables = [list(range(0, 15)), list(range(29, 14, -1))]
+    useds = [[64] * 14 + [9], [64] * 15]
+    a = run_pages(q, kp, vp, tables, useds, [15, 15], P=P, out_dtype=torch.float32)
+    monkeypatch.setenv("HELM_B200_FORCE_GENERIC", "1")
+    b = run_pages(q, kp, vp, tables, useds, [15, 15], P=P, out_dtype=torch.float32)
+    assert float((a - b).abs().max()) < 1e-4
+
+
 def test_tensor_core_path_matches_generic_path(cuda, monkeypatch):
     torch.manual_seed(7)
     Hkv, D, P, gq = 8, 128, 64, 8
