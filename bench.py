@@ -931,8 +931,11 @@ def kernel_cases(dev):
     cases.append(("attn_warp_fp32", "attn_warp_kernel + lse_merge_kernel", "hbm", b, s,
                   "fp32 pages (config-1 heads), B 4, 32q/8kv, d128, 16384 tokens per sequence"))
     b, s = attn_case(4, 48, 2, 96, 64, 65536, bf, 0, 3)
-    cases.append(("attn_generic", "attn_generic_kernel (+ lse_merge_kernel)", "hbm", b, s,
+    cases.append(("attn_warp_group24", "attn_warp_kernel (3 head chunks) + lse_merge_kernel", "hbm", b, s,
                   "bf16, B 4, 48q/2kv (GQA group 24), d96, 65536 tokens per sequence"))
+    b, s = attn_case(4, 16, 4, 80, 64, 65536, bf, 0, 4)
+    cases.append(("attn_generic", "attn_generic_kernel + lse_merge_kernel", "hbm", b, s,
+                  "bf16, B 4, 16q/4kv, d80 (not a multiple of 32), 65536 tokens per sequence"))
 
     def merge_setup():
         S, rows, D = 16, 16384, 128

@@ -18,19 +18,21 @@
 //                                            copies, released by the converters;
 //   A   (converted 16-bit weights: 128 lanes x 32 columns per k step, 4 deep)  tensor memory, written
 //                                            by the converters, released by the MMAs.
-// Warp roles (320 threads):
+// Warp roles (576 threads):
 //   warp 0      producer: TMA for x, bulk copies for the packed weight blocks;
 //   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 with A in tensor memory (M=128
 //               channels, N=256 tokens, K=16; B = x, K-major 128-byte-swizzled descriptor; D in
 //               tensor memory) four times per k step, then tcgen05.commit to the x and A empty
 //               barriers;
-//   warps 2-9   converters, then the epilogue.  Warp w may address the tensor-memory lanes
-//               32*(w%4)..+31, so thread (w, l) owns channel row 32*(w%4) + l; warps 2-5 convert the
-//               first 32 k of each step, warps 6-9 the second.  A row's 32 int8 values (two 16-byte
-//               chunks of its packed block row) become 16 words of exact 16-bit pairs, stored with
-//               tcgen05.st into the stage's columns (column c holds k = 2c, 2c+1).  After the last k
-//               step the same threads read their channel's accumulators (tcgen05.ld, 32 tokens at a
-//               time), apply the channel's scale and bias and store y.
+//   warps 2-17  converters, then the epilogue.  Warp w may address the tensor-memory lanes
+//               32*(w%4)..+31, so thread (w, l) owns channel row 32*(w%4) + l.  The warps form four
+//               groups of four (one warp per lane quadrant); group g converts the k steps j with
+//               j % 4 == g into A stage g, so a conversion has four k steps of MMA time to finish.
+//               A row's 64 int8 values of a step (four 16-byte chunks of its packed block row)
+//               become 32 words of exact 16-bit pairs, stored with tcgen05.st into the stage's
+//               columns (column c holds k = 2c, 2c+1).  After the last k step the same threads read
+//               their channel's accumulators (tcgen05.ld, 32 tokens at a time, 64 tokens a warp),
+//               apply the channel's scale and bias and store y.
 // Tensor memory: 512 columns -- the 128 x 256 accumulator in columns 0-255, the A ring in 256-383.
 // Every mbarrier wait is bounded: a wait that gives up sets HELM_DEVERR_TIMEOUT in the library's
 // INT8 error word; the CTA then skips its remaining work and its stores, waits (bounded) for the
@@ -46,7 +48,8 @@ constexpr int kXStages = 4, kWStages = 3, kAStages = 4;
 constexpr int kXStageBytes = GTK * GK * 2;       // 32 KB: 256 token rows x 128 B
 constexpr int kWStageBytes = GCH * 128;          // 16 KB: 8 packed blocks (16 rows x 128 k)
 constexpr int kGSmem = kXStages * kXStageBytes + kWStages * kWStageBytes + 1024;
-constexpr int kConvWarps = 8;
+constexpr int kConvWarps = 16;                  // four groups of four (one per tensor-memory lane quadrant)
+constexpr int kGroupWarps = 4;
 constexpr int kGThreads = (2 + kConvWarps) * 32;
 constexpr int kTmemCols = 512;
 constexpr int kAccCol = 0, kACol0 = 256, kAStageCols = GK / 2;   // 32 columns of 16-bit pairs per k step
@@ -163,10 +166,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&w_full[s], 1);
-      mbar_init(&w_empty[s], kConvWarps);
+      mbar_init(&w_empty[s], 2 * kGroupWarps);   // the two k steps of a column, four warps each
     }
     for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&a_full[s], kConvWarps);
+      mbar_init(&a_full[s], kGroupWarps);
       mbar_init(&a_empty[s], 1);
     }
     mbar_init(&acc_bar, 1);
@@ -247,34 +250,41 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
   } else {
     // ---------------- converters ----------------
+    // Group g (warps 2+4g .. 5+4g, one per lane quadrant) converts k steps g, g+4, g+8, ... into
+    // A stage g, so each group has four k steps of MMA time for one conversion.
     const int quad = warp & 3;                 // the tensor-memory lanes this warp may address
-    const int hk = (warp - 2) >> 2;            // which 32 k of a step
+    const int grp = (warp - 2) >> 2;           // k steps j with j % 4 == grp; A stage grp
     const int r = quad * 32 + lane;            // channel row of the tile
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    for (int j = 0; j < NK; ++j) {
-      const int c = j >> 1, ws = c % kWStages, js = j & 1, as = j % kAStages;
+    const uint32_t a_addr = tmem + lane_addr + (uint32_t)(kACol0 + grp * kAStageCols);
+    for (int j = grp; j < NK; j += kAStages) {
+      const int c = j >> 1, ws = c % kWStages, js = j & 1;
       if (!mbar_wait(&w_full[ws], (uint32_t)((c / kWStages) & 1)) ||
-          (j >= kAStages && !mbar_wait(&a_empty[as], (uint32_t)((j / kAStages - 1) & 1)))) {
+          (j >= kAStages && !mbar_wait(&a_empty[grp], (uint32_t)((j / kAStages - 1) & 1)))) {
         give_up();
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint8_t *row = w_ring + ws * kWStageBytes + (r >> 4) * 2048 + (r & 15) * 128;
-      const int lc = 4 * js + 2 * hk;          // first of this thread's two logical 16-value chunks
-      const uint4 v0 = *reinterpret_cast<const uint4 *>(row + ((lc ^ (r & 7)) << 4));
-      const uint4 v1 = *reinterpret_cast<const uint4 *>(row + (((lc + 1) ^ (r & 7)) << 4));
-      uint4 q0, q1, q2, q3;
-      cvt16<XT>(v0, q0, q1);
-      cvt16<XT>(v1, q2, q3);
-      const uint32_t w[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
-                              q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
-      tmem_st16(tmem + lane_addr + (uint32_t)(kACol0 + as * kAStageCols + hk * 16), w);
+      uint4 v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)             // logical 16-value chunks 4*js .. 4*js + 3 of the row
+        v[i] = *reinterpret_cast<const uint4 *>(row + (((4 * js + i) ^ (r & 7)) << 4));
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint4 q0, q1, q2, q3;
+        cvt16<XT>(v[2 * h], q0, q1);
+        cvt16<XT>(v[2 * h + 1], q2, q3);
+        const uint32_t w[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+                                q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
+        tmem_st16(a_addr + (uint32_t)(h * 16), w);
+      }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&a_full[as]);
-        if (js == 1 || j == NK - 1) mbar_arrive(&w_empty[ws]);
+        mbar_arrive(&a_full[grp]);
+        mbar_arrive(&w_empty[ws]);
       }
     }
     // ---------------- epilogue ----------------
@@ -286,8 +296,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const float sc = n < N ? load_f(scale, scale_dt, n) : 0.f;
       const float bi = (bias && n < N) ? Elem<XT>::to_f(bias[n]) : 0.f;
       const bool store = n < N && !*reinterpret_cast<volatile int *>(&failed);
+      constexpr int kCols = GTK / (kConvWarps / 4);   // token columns per warp
 #pragma unroll 1
-      for (int c0 = hk * 128; c0 < hk * 128 + 128; c0 += 32) {
+      for (int c0 = grp * kCols; c0 < grp * kCols + kCols; c0 += 32) {
         float acc[32];
         tmem_ld32(tmem + lane_addr + (uint32_t)(kAccCol + c0), acc);
         if (!store) continue;
