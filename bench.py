@@ -906,16 +906,19 @@ def kernel_cases(dev):
         nn = torch.full((B,), npg, dtype=torch.int32, device=dev)
         return slab, pt, pu, nn
 
-    def attn_case(B, Hq, Hkv, D, P, ctx, dtype, splits, seed):
+    def attn_case(B, Hq, Hkv, D, P, ctx, dtype, splits, seed, copies=1):
         def setup():
-            slab, pt, pu, nn = pool(B, Hkv, D, P, ctx, dtype, seed)
+            pools = [pool(B, Hkv, D, P, ctx, dtype, seed + i) for i in range(copies)]
             q = torch.randn((B, Hq, D), device=dev).to(dtype)
             out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
             err = torch.zeros(1, dtype=torch.int32, device=dev)
             kw = dict(num_kv_heads=Hkv, page_size=P, page_stride=2 * Hkv * P * D, head_stride=P * D,
-                      num_pool_pages=slab.shape[0], out=out, error_flag=err, num_splits=splits)
+                      num_pool_pages=pools[0][0].shape[0], out=out, error_flag=err, num_splits=splits)
+            it = [0]
 
             def call():
+                slab, pt, pu, nn = pools[it[0] % copies]
+                it[0] += 1
                 ops.paged_decode_attention(q, slab[:, 0], slab[:, 1], pt, pu, nn, **kw)
             return call, lambda: int(err.item()) == 0 and bool(torch.isfinite(out).all())
         es = torch.empty((), dtype=dtype).element_size()
@@ -930,6 +933,9 @@ def kernel_cases(dev):
     b, s = attn_case(4, 32, 8, 128, 64, 16384, torch.float32, 0, 2)
     cases.append(("attn_warp_fp32", "attn_warp_kernel + lse_merge_kernel", "hbm", b, s,
                   "fp32 pages (config-1 heads), B 4, 32q/8kv, d128, 16384 tokens per sequence"))
+    b, s = attn_case(1, 32, 8, 128, 64, 4096, torch.float32, 0, 10, copies=8)
+    cases.append(("attn_config1", "attn_warp_kernel + lse_merge_kernel", "latency", b, s,
+                  "config 1 all resident: fp32, B 1, 32q/8kv, d128, 4096 tokens, 8 instances rotating (268 MB)"))
     b, s = attn_case(4, 48, 2, 96, 64, 65536, bf, 0, 3)
     cases.append(("attn_warp_group24", "attn_warp_kernel (3 head chunks) + lse_merge_kernel", "hbm", b, s,
                   "bf16, B 4, 48q/2kv (GQA group 24), d96, 65536 tokens per sequence"))

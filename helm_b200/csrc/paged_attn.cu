@@ -1473,6 +1473,107 @@ __global__ void __launch_bounds__(kThreads, 2)
 }  // namespace tc
 
 // ===========================================================================
+// Log-sum-exp merge, split-parallel: one CTA of 8 warps per row, for an even D <= 256 and
+// 8-byte-aligned records.  The (m, l) of every partial are read in one parallel pass; then warp w
+// sums partials w, w + 8, ... over the whole row (float2 loads, a 512-byte record row per warp
+// load), four partials in flight per lane; the eight warps' sums meet in shared memory.  Each
+// row costs about three memory round trips whatever the number of partials, where the
+// dim-per-thread kernel below walks the partials one load batch at a time.
+// ===========================================================================
+constexpr int kMergeWarps = 8;
+
+__global__ void __launch_bounds__(kMergeWarps * 32) lse_merge_wide_kernel(const float *__restrict__ parts, int S,
+                                                                         int64_t pstride, int rows, int D,
+                                                                         void *out, int out_dtype,
+                                                                         float *out_record) {
+  constexpr int kChunk = 1024;
+  __shared__ float w_s[kChunk];
+  __shared__ float o_red[kMergeWarps][256];
+  __shared__ float red[kMergeWarps];
+  __shared__ float s_M, s_L;
+  const int row = blockIdx.x;
+  const int rl = D + 2, nv = D >> 1;
+  const float *base = parts + (int64_t)row * rl;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_trigger();
+  pdl_wait();
+  float M = -INFINITY;
+  for (int sp = tid; sp < S; sp += blockDim.x) M = fmaxf(M, base[sp * pstride + D]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  if (tid == 0) {
+    float m = red[0];
+    for (int w = 1; w < kMergeWarps; ++w) m = fmaxf(m, red[w]);
+    s_M = m;
+  }
+  __syncthreads();
+  M = s_M;
+  float L = 0.f;
+  float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  for (int c0 = 0; c0 < S; c0 += kChunk) {
+    const int n = min(kChunk, S - c0);
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+      const float *p = base + (int64_t)(c0 + i) * pstride;
+      const float w = rescale_weight(p[D], M);
+      w_s[i] = w;
+      L = fmaf(p[D + 1], w, L);
+    }
+    __syncthreads();
+    if (M != -INFINITY) {
+#pragma unroll 4
+      for (int i = warp; i < n; i += kMergeWarps) {
+        const float w = w_s[i];
+        const float2 *src = reinterpret_cast<const float2 *>(base + (int64_t)(c0 + i) * pstride);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int v = lane + 32 * k;
+          if (v < nv) {
+            const float2 x = src[v];
+            acc[k].x = fmaf(x.x, w, acc[k].x);
+            acc[k].y = fmaf(x.y, w, acc[k].y);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int v = lane + 32 * k;
+    if (v < nv) {
+      o_red[warp][2 * v] = acc[k].x;
+      o_red[warp][2 * v + 1] = acc[k].y;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  __syncthreads();
+  if (lane == 0) red[warp] = L;
+  __syncthreads();
+  if (tid == 0) {
+    float l = 0.f;
+    for (int w = 0; w < kMergeWarps; ++w) l += red[w];
+    s_L = M == -INFINITY ? 0.f : l;
+  }
+  __syncthreads();
+  L = s_L;
+  for (int d = tid; d < D; d += blockDim.x) {
+    float O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) O += o_red[w][d];
+    if (M == -INFINITY) O = 0.f;
+    if (out) store_f(out, out_dtype, (int64_t)row * D + d, L > 0.f ? O / L : 0.f);
+    if (out_record) {
+      float *rr = out_record + (int64_t)row * rl;
+      rr[d] = O;
+      if (d == 0) { rr[D] = M; rr[D + 1] = L; }
+    }
+  }
+}
+
+// ===========================================================================
 // Log-sum-exp merge: one CTA per row (query head of a sequence).
 // ===========================================================================
 __global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict__ parts, int S, int64_t pstride,
@@ -1685,6 +1786,20 @@ bool warp_eligible(const helm_paged_attn_params *p) {
   return kb % vb == 0 && vbp % vb == 0 && (p->page_stride * es) % vb == 0 && (p->head_stride * es) % vb == 0;
 }
 
+// Launches the merge of S partial records (stride pstride floats) into out / out_record.
+int launch_lse_merge(const float *parts, int S, int64_t pstride, int rows, int D, void *out, int out_dtype,
+                     float *out_record, cudaStream_t st) {
+  // Many rows already fill the GPU with one 128-thread CTA per row; the split-parallel kernel pays
+  // where rows are few (decode batches, sharded exchanges) or the partials many.
+  const bool wide = D % 2 == 0 && D <= 256 && pstride % 2 == 0 && (reinterpret_cast<uintptr_t>(parts) & 7) == 0 &&
+                    (rows < 8 * num_sms() || S >= 64);
+  const cudaError_t e = wide ? launch_pdl(lse_merge_wide_kernel, dim3(rows), dim3(kMergeWarps * 32), 0, st, parts, S,
+                                          pstride, rows, D, out, out_dtype, out_record)
+                             : launch_pdl(lse_merge_kernel, dim3(rows), dim3(128), 0, st, parts, S, pstride, rows, D,
+                                          out, out_dtype, out_record);
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "lse_merge: launch: %s", cudaGetErrorString(e));
+  return check_launch(wide ? "lse_merge_wide_kernel" : "lse_merge_kernel");
+}
 int warp_ctas_per_sm(int kv_dtype, int D, int gq);
 
 int resolve_splits(const helm_paged_attn_params *p) {
@@ -2026,10 +2141,7 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
     }
   }
   if (rc != HELM_OK || S == 1) return rc;
-  const cudaError_t e = launch_pdl(lse_merge_kernel, dim3(rows), dim3(128), 0, st, (const float *)records, S,
-                                   (int64_t)rows * (p->D + 2), rows, p->D, p->out, p->out_dtype, p->out_record);
-  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "paged_attn: launch: %s", cudaGetErrorString(e));
-  return check_launch("lse_merge_kernel");
+  return launch_lse_merge(records, S, (int64_t)rows * (p->D + 2), rows, p->D, p->out, p->out_dtype, p->out_record, st);
 }
 
 extern "C" int helm_lse_merge(const float *partials, int32_t num_partials, int64_t partial_stride, int32_t rows,
@@ -2043,9 +2155,8 @@ extern "C" int helm_lse_merge(const float *partials, int32_t num_partials, int64
   if (out && out_dtype != HELM_F32 && out_dtype != HELM_F16 && out_dtype != HELM_BF16)
     return fail(HELM_ERR_UNSUPPORTED, "lse_merge: dtype %d", out_dtype);
   if (rows == 0) return HELM_OK;
-  lse_merge_kernel<<<rows, 128, 0, as_stream(stream)>>>(partials, num_partials, partial_stride, rows, D, out,
-                                                        out_dtype, out_record);
-  return check_launch("lse_merge_kernel");
+  return launch_lse_merge(partials, num_partials, partial_stride, rows, D, out, out_dtype, out_record,
+                          as_stream(stream));
 }
 
 // ===========================================================================

@@ -225,10 +225,13 @@ def test_bad_page_id_sets_error_flag(cuda):
         assert torch.equal(out, ref)
 
 
-def test_lse_merge_matches_oracle(cuda):
+@pytest.mark.parametrize("S,D", [(5, 128), (74, 128), (1100, 64), (9, 256), (6, 65)])
+def test_lse_merge_matches_oracle(S, D, cuda):
+    """Split-parallel merge (even D) and the dim-per-thread merge (odd D), including more partials
+    than one shared-memory chunk (1100) and the config-1 split count (74)."""
     from helm_b200 import ops
-    rng = np.random.default_rng(5)
-    S, rows, D = 5, 12, 128
+    rng = np.random.default_rng(5 + S + D)
+    rows = 12
     recs = np.zeros((S, rows, D + 2))
     recs[..., :D] = rng.standard_normal((S, rows, D))
     recs[..., D] = rng.standard_normal((S, rows)) * 4
