@@ -89,6 +89,10 @@ def parse():
 # byte, and the record/output writes of a batch-4, 64-head call.
 ATTN_READ_PER_ALG_BYTE = 269.749504 / 268.664832
 ATTN_WRITE_BYTES = 5.910784e6
+# The same for the split path (attention + merge launches of one call), from
+# profiles/attn_tc_kernel_config5.md; None until captured.
+ATTN_SPLIT_READ_PER_ALG_BYTE = None
+ATTN_SPLIT_WRITE_BYTES = None
 
 
 def peaks():
@@ -469,12 +473,19 @@ def run_helm(args, rank, local, world):
             "hbm_gbs": step_bytes_all / (ms_step * 1e-3) / 1e9 / world,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak,
-                         "traffic": (ATTN_READ_PER_ALG_BYTE * bytes_launch + ATTN_WRITE_BYTES
-                                     if (world == 1 and st.splits == 0) else None),
-                         "traffic_source": "ncu dram__bytes_read/write.sum of a 268.7 MB launch, reads scaled "
-                                           "by the units streamed (profiles/attn_tc_persistent_config5.txt)",
+                         "traffic": (ATTN_SPLIT_READ_PER_ALG_BYTE * bytes_launch + ATTN_SPLIT_WRITE_BYTES
+                                     if (world == 1 and st.splits > 0 and ATTN_SPLIT_READ_PER_ALG_BYTE) else
+                                     ATTN_READ_PER_ALG_BYTE * bytes_launch + ATTN_WRITE_BYTES
+                                     if (world == 1 and st.splits < 0) else None),
+                         "traffic_source": ("ncu dram__bytes_read/write.sum of the attention + merge launches of a "
+                                            "268.7 MB call, reads scaled by the bytes streamed "
+                                            "(profiles/attn_tc_kernel_config5.md)" if st.splits > 0 else
+                                            "ncu dram__bytes_read/write.sum of a 268.7 MB launch, reads scaled "
+                                            "by the units streamed (profiles/attn_tc_persistent_config5.txt)"),
                          "peak_kind": peak_kind,
-                         "kernel": "attn_tc_persistent_kernel (one helm_paged_attn_decode call = one launch)",
+                         "kernel": (f"attn_tc_kernel ({st.splits} splits) + lse_merge_wide_kernel (one "
+                                    "helm_paged_attn_decode call)" if st.splits > 0 else
+                                    "attn_tc_persistent_kernel (one helm_paged_attn_decode call = one launch)"),
                          "bytes_per_launch": bytes_launch, "avg_launch_ms": attn_avg_ms},
             "breakdown_ms_per_layer": breakdown,
             "check": check,

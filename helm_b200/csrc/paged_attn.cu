@@ -937,6 +937,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     u1 = U * (c + 1) / C;
   }
 
+  // (sequence, kv head) pair of unit u: the last b with seq_prefix[b] <= u (and pages > 0)
+  auto unit_pair = [&](int64_t u) {
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (seq_prefix[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    int b = lo;
+    while (seq_pages[b] == 0 && b > 0) --b;
+    return b * Hkv + (int)((u - seq_prefix[b]) / seq_pages[b]);
+  };
+
   if (warp == kConsumerWarps) {
     // ------------------------------ producer ------------------------------
     // The 32 lanes decode and fetch the (page id, used, pair, last) of the next 32 units ahead of
@@ -1202,6 +1214,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     };
 
     const int64_t n_units = u1 - u0;
+    if (n_units > 0) {  // the first pair's q loads while the producer fetches page ids and K/V
+      cur_pair = unit_pair(u0);
+      load_q(cur_pair);
+    }
     for (int64_t i = 0; i < n_units; ++i) {
       const int st = (int)(i % kStages);
       if (!mbar_wait(&full_bar[st], (uint32_t)((i / kStages) & 1))) {
@@ -1819,6 +1835,14 @@ int resolve_splits(const helm_paged_attn_params *p) {
   const int pairs = p->B * p->Hkv;
   const int maxp = p->max_pages;
   if (maxp <= 1 || pairs <= 0) return 1;
+  if (tc_eligible(p)) {
+    // About one resident wave of the tensor-core split kernel (two CTAs per SM): measured against
+    // more splits (several waves) and against the persistent kernel over 34 MB - 2.1 GB calls with
+    // 8 to 64 (sequence, kv head) pairs, this count was the fastest or within 3 % of it.
+    int S = (2 * num_sms() + pairs / 2) / pairs;
+    if (S > maxp) S = maxp;
+    return S < 1 ? 1 : S;
+  }
   const int slots = num_sms() * 2;  // two resident CTAs per SM
   for (int waves = 4; waves >= 1; --waves) {
     int S = (waves * slots) / pairs;
@@ -1831,8 +1855,10 @@ int resolve_splits(const helm_paged_attn_params *p) {
   return S < 1 ? 1 : S;
 }
 
-// Launch plan.  num_splits == 0 on a tensor-core-eligible call selects the persistent kernel
-// (one launch, C CTAs, fused merge); otherwise the split grid + lse_merge_kernel.
+// Launch plan.  The persistent kernel (one launch, C CTAs, stream-K over all pages, fused merge)
+// runs tensor-core-eligible calls that ask for it (num_splits == -1) or that carry a cross-GPU
+// exchange (which it fuses); every other call runs the split grid + the LSE merge, which has the
+// lower fixed cost per call (10 vs 16 us) and the higher streaming rate (7.3 vs 7.0 TB/s).
 struct Plan {
   bool persistent = false;
   int S = 1;          // split mode: splits
@@ -1855,7 +1881,9 @@ Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
   const bool pending_ok = pairs_all <= tc::kMaxPending || units_max / Cp + 2 <= tc::kMaxPending;
   // Workspace layout: the CTA records then the tagged arrival counters (persistent path), or the
   // split records (split path).
-  if (p->num_splits == 0 && eligible && p->B <= tc::kMaxSeqs && pending_ok && units_max < (1ll << 31) &&
+  const bool sharded = p->exchange && p->exchange->world > 1;
+  const bool want = p->num_splits == -1 || (p->num_splits == 0 && sharded);
+  if (want && eligible && p->B <= tc::kMaxSeqs && pending_ok && units_max < (1ll << 31) &&
       !env_flag("HELM_B200_NO_PERSISTENT")) {
     pl.persistent = true;
     const int pairs = pairs_all;
@@ -1895,7 +1923,7 @@ int validate(const helm_paged_attn_params *p) {
   if (p->max_pages > p->page_table_stride)
     return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: max_pages %d > page_table_stride %d", p->max_pages,
                 p->page_table_stride);
-  if (p->num_splits < 0) return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: negative num_splits");
+  if (p->num_splits < -1) return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: num_splits %d < -1", p->num_splits);
   if (p->exchange && p->exchange->world > 1) {
     const helm_shard_exchange *x = p->exchange;
     if (x->world > HELM_MAX_RANKS || x->rank < 0 || x->rank >= x->world)
@@ -1910,8 +1938,8 @@ int validate(const helm_paged_attn_params *p) {
       if (reinterpret_cast<uintptr_t>(x->peer_recv[r]) % 16 != 0)
         return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: exchange slots of rank %d not 16-byte aligned", r);
     }
-    if (p->num_splits != 0)
-      return fail(HELM_ERR_UNSUPPORTED, "paged_attn: the fused exchange needs num_splits == 0");
+    if (p->num_splits > 0)
+      return fail(HELM_ERR_UNSUPPORTED, "paged_attn: the fused exchange needs num_splits 0 or -1");
   }
   return HELM_OK;
 }
@@ -2035,7 +2063,7 @@ using namespace helm;
 extern "C" int64_t helm_paged_attn_workspace_bytes(const helm_paged_attn_params *p, int32_t *num_splits_out) {
   if (validate(p) != HELM_OK) return -1;
   const Plan pl = make_plan(p, tc_eligible(p));
-  if (num_splits_out) *num_splits_out = pl.persistent ? 0 : pl.S;
+  if (num_splits_out) *num_splits_out = pl.persistent ? -1 : pl.S;
   return pl.bytes;
 }
 

@@ -89,6 +89,11 @@ const char *helm_last_error(void);
  * cross-GPU merge.  With num_splits == 1 and only `out` requested, no
  * workspace is touched.
  *
+ * Paths.  The split path runs a grid of (splits, kv heads, sequences) CTAs
+ * and then the LSE merge; the persistent path runs one launch of two CTAs per
+ * SM that stream-K over every (sequence, kv head, page) unit and merge inside
+ * the kernel, and is the one that carries the fused cross-GPU exchange.
+ *
  * Workspace.  The single-launch (persistent) path keeps per-CTA records and
  * per-(sequence, kv head) arrival counters there.  The counters are tagged
  * with a token the library issues per call, so no call needs them zeroed: a
@@ -141,7 +146,11 @@ typedef struct {
   int32_t B, Hq, Hkv, D, P;
   int32_t q_dtype, kv_dtype, out_dtype; /* helm_dtype */
   float scale;            /* softmax scale; reference default 1/sqrt(D) */
-  int32_t num_splits;     /* >= 1; 0 picks a split count for this GPU */
+  int32_t num_splits;     /* >= 1: that many splits; 0: automatic (the split
+                             path with about one resident wave of CTAs, or the
+                             persistent kernel when `exchange` spans several
+                             GPUs); -1: the persistent single-launch kernel
+                             (bf16/fp16, P=64, D=128 calls; others as 0) */
   float *workspace;       /* split records, may be null if not needed */
   int64_t workspace_bytes;
   void *out;              /* [B, Hq, D] out_dtype, or null */
@@ -152,7 +161,8 @@ typedef struct {
 
 /* Bytes of workspace helm_paged_attn_decode needs for these params, after
  * resolving num_splits == 0.  Writes the split count it will use to
- * *num_splits_out when non-null. */
+ * *num_splits_out when non-null: >= 1 for the split path, -1 for the
+ * persistent kernel (pass it back as num_splits to keep that plan). */
 int64_t helm_paged_attn_workspace_bytes(const helm_paged_attn_params *p,
                                         int32_t *num_splits_out);
 

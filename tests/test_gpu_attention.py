@@ -95,7 +95,7 @@ def test_config1_matches_reference(cuda):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("gq", [1, 4, 5, 8, 16])
-@pytest.mark.parametrize("splits", [1, 3, 0])
+@pytest.mark.parametrize("splits", [1, 3, 0, -1])
 def test_random_pool_tensor_core_path(dtype, gq, splits, cuda):
     """B=3 sequences of ragged lengths over a shuffled pool (P=64, D=128): the TMA/tensor-core path."""
     torch.manual_seed(1000 + gq)
@@ -329,11 +329,13 @@ def test_persistent_kernel_matches_split_kernel(lens, gq, cuda):
         useds.append([P] * (npg - 1) + [n - P * (npg - 1)] if npg else [])
         i += npg
     q = torch.randn(len(lens), Hkv * gq, D, device=cuda).to(torch.bfloat16)
-    a1 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=0, out_dtype=torch.float32)
-    a2 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=0, out_dtype=torch.float32)
+    a1 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=-1, out_dtype=torch.float32)
+    a2 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=-1, out_dtype=torch.float32)
     s1 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=1, out_dtype=torch.float32)
+    s0 = run_pages(q, kp, vp, tables, useds, npages, P=P, num_splits=0, out_dtype=torch.float32)
     assert torch.equal(a1, a2)
     assert float((a1 - s1).abs().max()) < 1e-4
+    assert float((s0 - s1).abs().max()) < 1e-4
     width = max(1, max(npages))
     ref = OA.paged_attention_torch(q.cpu(), kp.cpu(), vp.cpu(),
                                    torch.tensor([t + [0] * (width - len(t)) for t in tables]),
@@ -345,8 +347,8 @@ def test_persistent_kernel_matches_split_kernel(lens, gq, cuda):
 
 
 def test_persistent_out_record_merges_across_calls(cuda):
-    """out_record of the persistent launch, merged over two halves of a sequence, equals the
-    one-call output (the multi-GPU merge contract)."""
+    """out_record of the persistent launch (num_splits=-1) and of the automatic plan, merged over
+    two halves of a sequence, equals the one-call output (the multi-GPU merge contract)."""
     from helm_b200 import ops
     torch.manual_seed(21)
     Hkv, D, P, gq, B = 8, 128, 64, 8, 3
@@ -359,13 +361,14 @@ def test_persistent_out_record_merges_across_calls(cuda):
     full = ops.paged_decode_attention(q, kp, vp, pt, pu, torch.full((B,), 90, dtype=torch.int32, device=cuda),
                                       num_kv_heads=Hkv, page_size=P, page_stride=Hkv * P * D, head_stride=P * D,
                                       num_pool_pages=300, out_dtype=torch.float32)
-    recs = []
-    for lo, hi in ((0, 37), (37, 90)):
-        rec = torch.empty(B * Hkv * gq, D + 2, device=cuda)
-        ops.paged_decode_attention(q, kp, vp, pt[:, lo:hi].contiguous(), pu[:, lo:hi].contiguous(),
-                                   torch.full((B,), hi - lo, dtype=torch.int32, device=cuda), num_kv_heads=Hkv,
-                                   page_size=P, page_stride=Hkv * P * D, head_stride=P * D, num_pool_pages=300,
-                                   out_record=rec)
-        recs.append(rec)
-    merged = ops.lse_merge(torch.stack(recs).contiguous(), out=torch.empty(B * Hkv * gq, D, device=cuda))
-    assert float((merged.reshape(B, -1, D) - full).abs().max()) < 1e-5
+    for splits in (-1, 0):
+        recs = []
+        for lo, hi in ((0, 37), (37, 90)):
+            rec = torch.empty(B * Hkv * gq, D + 2, device=cuda)
+            ops.paged_decode_attention(q, kp, vp, pt[:, lo:hi].contiguous(), pu[:, lo:hi].contiguous(),
+                                       torch.full((B,), hi - lo, dtype=torch.int32, device=cuda), num_kv_heads=Hkv,
+                                       page_size=P, page_stride=Hkv * P * D, head_stride=P * D, num_pool_pages=300,
+                                       out_record=rec, num_splits=splits)
+            recs.append(rec)
+        merged = ops.lse_merge(torch.stack(recs).contiguous(), out=torch.empty(B * Hkv * gq, D, device=cuda))
+        assert float((merged.reshape(B, -1, D) - full).abs().max()) < 1e-5, splits
