@@ -66,7 +66,7 @@ def parse():
     ap.add_argument("--no-sub-records", action="store_true",
                     help="config5 at N=1: skip the config-2 and config-1 sub-records of the line")
     ap.add_argument("--e2e-steps", type=int, default=None)
-    ap.add_argument("--exchange", default="fused", choices=["fused", "p2p", "nccl"],
+    ap.add_argument("--exchange", default="fused", choices=["fused", "split", "p2p", "nccl"],
                     help="cross-GPU record exchange for N > 1")
     # Smaller stacks for ncu captures only; the reported workload is config 5 unless these are set.
     ap.add_argument("--layers", type=int, default=None)
@@ -307,6 +307,7 @@ class Stack:
             from helm_b200.runtime.sharded import KVShardGroup
             self.shard = KVShardGroup(rows, self.D, dev, exchange=exchange)
         self.fused = self.shard is not None and self.shard.fused
+        self.records_only = self.shard is not None and self.shard.records_only
         self.k_base, self.v_base = self.store.base_ptrs()
         self.page_stride = self.store.page_elems
         self.head_stride = self.store.head_stride
@@ -325,7 +326,7 @@ class Stack:
                 num_kv_heads=self.Hkv, page_size=self.P, page_stride=self.page_stride,
                 head_stride=self.head_stride, num_pool_pages=self.n_pool, max_pages=bt.width,
                 out=self.out[l] if (self.world == 1 or self.fused) else None,
-                out_record=self.rec[l] if (self.world > 1 and not self.fused) else None,
+                out_record=self.rec[l] if (self.world > 1 and not self.fused and not self.records_only) else None,
                 error_flag=self.error_flag)
             if self.fused:
                 p.exchange = self.shard.xparams_ptr
@@ -346,7 +347,7 @@ class Stack:
         for p in self.attn_params:
             p.workspace = self.ws.data_ptr()
             p.workspace_bytes = self.ws.numel() * 4
-        per_layer = (1 if self.tail else 0) + 1 + (1 if self.splits > 1 else 0) + \
+        per_layer = (1 if self.tail else 0) + 1 + (1 if (self.splits > 1 and not self.records_only) else 0) + \
             (1 if (self.world > 1 and not self.fused) else 0)
         self.launches_per_step = self.L * per_layer
 
@@ -373,7 +374,16 @@ class Stack:
                 N.check("helm_kv_append", self.lib.helm_kv_append(ctypes.byref(self.append_params[l]), sp))
             N.check("helm_paged_attn_decode", self.lib.helm_paged_attn_decode(ctypes.byref(self.attn_params[l]), sp))
             if self.world > 1 and not self.fused:
-                self.shard.gather_merge(self.rec[l], out=self.out[l].view(self.B * self.Hq, self.D))
+                self.exchange(l, self.out[l].view(self.B * self.Hq, self.D))
+
+    def exchange(self, l, out):
+        """The separate exchange of layer l's attention result (p2p / split / nccl modes): the merged
+        record, or in records-only mode the split records left in the workspace."""
+        if self.records_only:
+            rows, S = self.B * self.Hq, self.splits
+            parts = self.ws[:S * rows * (self.D + 2)].view(S, rows, self.D + 2)
+            return self.shard.gather_merge(parts, out=out)
+        return self.shard.gather_merge(self.rec[l], out=out)
 
 
 def run_helm(args, rank, local, world):
@@ -483,7 +493,9 @@ def run_helm(args, rank, local, world):
                                             "ncu dram__bytes_read/write.sum of a 268.7 MB launch, reads scaled "
                                             "by the units streamed (profiles/attn_tc_persistent_config5.txt)"),
                          "peak_kind": peak_kind,
-                         "kernel": (f"attn_tc_kernel ({st.splits} splits) + lse_merge_wide_kernel (one "
+                         "kernel": (f"attn_tc_kernel ({st.splits} splits, records only) + gather_merge_kernel "
+                                    "(merge + exchange)" if st.records_only else
+                                    f"attn_tc_kernel ({st.splits} splits) + lse_merge_wide_kernel (one "
                                     "helm_paged_attn_decode call)" if st.splits > 0 else
                                     "attn_tc_persistent_kernel (one helm_paged_attn_decode call = one launch)"),
                          "bytes_per_launch": bytes_launch, "avg_launch_ms": attn_avg_ms},
@@ -532,10 +544,10 @@ def check_stack(st, stream, world, dev, appended):
     p.out_record = None
     if world > 1 and not st.fused:
         p.out = None
-        p.out_record = st.rec[l].data_ptr()
+        p.out_record = None if st.records_only else st.rec[l].data_ptr()
     N.check("helm_paged_attn_decode", st.lib.helm_paged_attn_decode(ctypes.byref(p), stream.cuda_stream))
     if world > 1 and not st.fused:
-        st.shard.gather_merge(st.rec[l], out=out32.view(st.B * st.Hq, st.D))
+        st.exchange(l, out32.view(st.B * st.Hq, st.D))
     torch.cuda.synchronize(dev)
     identical = True
     if world > 1:
@@ -594,7 +606,7 @@ def component_breakdown(st, stream, world, dev, reps=3):
             st.attend(l, stream)
             e[2].record(stream)
             if world > 1 and not st.fused:
-                st.shard.gather_merge(st.rec[l], out=st.out[l].view(st.B * st.Hq, st.D))
+                st.exchange(l, st.out[l].view(st.B * st.Hq, st.D))
             e[3].record(stream)
         torch.cuda.synchronize(dev)
         if rep == 0:

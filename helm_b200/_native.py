@@ -14,7 +14,7 @@ import pathlib
 LIB_PATH = pathlib.Path(os.environ.get(
     "HELM_B200_LIB", pathlib.Path(__file__).resolve().parent / "lib" / "libhelm_b200.so"))
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # helm_dtype
 F32, F16, BF16, I8 = 0, 1, 2, 3
@@ -109,6 +109,7 @@ class GatherMergeParams(ctypes.Structure):
         ("recv_local", _p), ("flags_local", _p), ("counters", _p),
         ("out", _p), ("out_dtype", _i32), ("out_record", _p), ("error_flag", _p),
         ("wait_ns", ctypes.c_uint64),
+        ("num_partials", _i32), ("partial_stride", _i64),
     ]
 
 

@@ -1,4 +1,7 @@
 // Cross-GPU exchange of attention records + log-sum-exp merge (KV sequence sharding).
+// The input is this rank's merged record per row, or the split records of the attention's split
+// path, which each CTA then merges for its rows before the exchange (one launch in place of
+// helm_lse_merge + the exchange).
 //
 // Every rank holds a contiguous range of each sequence's pages and produces a
 // merged record [rows][D+2] = (o, m, l) per (sequence, query head).  This
@@ -24,7 +27,8 @@ namespace helm {
 namespace {
 
 constexpr int kRowsPerBlock = 8;
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;                // one warp per row of a block
+constexpr int kMaxD = 256;                   // head dim limit when merging split records here
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
 
 struct GatherArgs {
@@ -41,6 +45,8 @@ struct GatherArgs {
   float *out_record;
   int32_t *error_flag;
   uint64_t wait_ns;
+  int S;                              // > 1: `record` holds S split records, pstride floats apart
+  int64_t pstride;
 };
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
@@ -73,10 +79,48 @@ __global__ void __launch_bounds__(kThreads) gather_merge_kernel(GatherArgs a) {
     s_ok = 1;
   }
   __syncthreads();
+  // 0) with split records: merge this block's rows first (warp w merges row row0 + w over the S
+  //    splits in split order, lane l the dims l, l + 32, ...) into shared memory
+  __shared__ __align__(16) float rec_s[kRowsPerBlock * (kMaxD + 2)];
+  const float *src = a.record + (int64_t)row0 * rl;
+  if (a.S > 1) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < nrows) {
+      const float *base = a.record + (int64_t)(row0 + warp) * rl;
+      float M = -INFINITY;
+      for (int sp = lane; sp < a.S; sp += 32) M = fmaxf(M, base[sp * a.pstride + a.D]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float L = 0.f, O[kMaxD / 32];
+#pragma unroll
+      for (int k = 0; k < kMaxD / 32; ++k) O[k] = 0.f;
+      for (int sp = 0; sp < a.S; ++sp) {
+        const float *pp = base + sp * a.pstride;
+        const float w = rescale_weight(pp[a.D], M);
+        L = fmaf(pp[a.D + 1], w, L);
+#pragma unroll
+        for (int k = 0; k < kMaxD / 32; ++k) {
+          const int d = lane + 32 * k;
+          if (d < a.D) O[k] = fmaf(pp[d], w, O[k]);
+        }
+      }
+      float *r = rec_s + warp * rl;
+#pragma unroll
+      for (int k = 0; k < kMaxD / 32; ++k) {
+        const int d = lane + 32 * k;
+        if (d < a.D) r[d] = M == -INFINITY ? 0.f : O[k];
+      }
+      if (lane == 0) {
+        r[a.D] = M;
+        r[a.D + 1] = M == -INFINITY ? 0.f : L;
+      }
+    }
+    __syncthreads();
+    src = rec_s;
+  }
   // 1) push this rank's rows into every rank's receive slot (sent parity, source = this rank);
   //    16-byte stores when the block is 16-byte aligned (rows*(D+2) floats per block)
   const int n = nrows * rl;
-  const float *src = a.record + (int64_t)row0 * rl;
   const uint32_t slot = s_sent & 1u;
   const bool vec = ((n & 3) == 0) && ((((int64_t)row0 * rl) & 3) == 0) && ((((int64_t)a.rows * rl) & 3) == 0);
   for (int dst = 0; dst < G; ++dst) {
@@ -184,6 +228,13 @@ extern "C" int helm_gather_merge(const helm_gather_merge_params *p, void *stream
     if (!p->peer_recv[r] || !p->peer_flags[r]) return fail(HELM_ERR_INVALID_ARGUMENT, "gather_merge: null peer");
   if (p->out && p->out_dtype != HELM_F32 && p->out_dtype != HELM_F16 && p->out_dtype != HELM_BF16)
     return fail(HELM_ERR_UNSUPPORTED, "gather_merge: dtype %d", p->out_dtype);
+  if (p->num_partials < 0) return fail(HELM_ERR_INVALID_ARGUMENT, "gather_merge: num_partials %d", p->num_partials);
+  if (p->num_partials > 1) {
+    if (p->D > kMaxD) return fail(HELM_ERR_UNSUPPORTED, "gather_merge: split records need D <= %d", kMaxD);
+    if (p->partial_stride < (int64_t)p->rows * (p->D + 2))
+      return fail(HELM_ERR_INVALID_ARGUMENT, "gather_merge: partial_stride %lld < rows*(D+2)",
+                  (long long)p->partial_stride);
+  }
   GatherArgs a{};
   a.rank = p->rank;
   a.world = p->world;
@@ -204,6 +255,8 @@ extern "C" int helm_gather_merge(const helm_gather_merge_params *p, void *stream
   a.out_record = p->out_record;
   a.error_flag = p->error_flag;
   a.wait_ns = p->wait_ns ? p->wait_ns : kWaitNs;
+  a.S = p->num_partials;
+  a.pstride = p->partial_stride;
   gather_merge_kernel<<<a.nblocks, kThreads, 0, as_stream(stream)>>>(a);
   return check_launch("gather_merge_kernel");
 }

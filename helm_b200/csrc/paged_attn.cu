@@ -1882,7 +1882,8 @@ Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
   // Workspace layout: the CTA records then the tagged arrival counters (persistent path), or the
   // split records (split path).
   const bool sharded = p->exchange && p->exchange->world > 1;
-  const bool want = p->num_splits == -1 || (p->num_splits == 0 && sharded);
+  const bool records_only = !p->out && !p->out_record;
+  const bool want = !records_only && (p->num_splits == -1 || (p->num_splits == 0 && sharded));
   if (want && eligible && p->B <= tc::kMaxSeqs && pending_ok && units_max < (1ll << 31) &&
       !env_flag("HELM_B200_NO_PERSISTENT")) {
     pl.persistent = true;
@@ -1897,7 +1898,7 @@ Plan make_plan(const helm_paged_attn_params *p, bool eligible) {
     return pl;
   }
   pl.S = resolve_splits(p);
-  pl.bytes = pl.S > 1 ? (int64_t)pl.S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
+  pl.bytes = (pl.S > 1 || records_only) ? (int64_t)pl.S * rows * (p->D + 2) * (int64_t)sizeof(float) : 0;
   return pl;
 }
 
@@ -1915,7 +1916,9 @@ int validate(const helm_paged_attn_params *p) {
   if (p->B > 0 && p->Hq > 0) {
     if (!p->q || !p->k_base || !p->v_base || !p->page_table || !p->page_used || !p->num_pages)
       return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: null input pointer");
-    if (!p->out && !p->out_record) return fail(HELM_ERR_INVALID_ARGUMENT, "paged_attn: no output requested");
+    // no out and no out_record: records-only mode (the split records, left in the workspace)
+    if (!p->out && !p->out_record && p->exchange && p->exchange->world > 1)
+      return fail(HELM_ERR_UNSUPPORTED, "paged_attn: records-only mode has no fused exchange");
   }
   if (p->page_stride < 0 || p->head_stride < 0 || p->page_table_stride < 0 || p->max_pages < 0 ||
       p->num_pool_pages < 0)
@@ -2105,7 +2108,8 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
   a.num_splits = S;
   a.error_flag = p->error_flag;
   float *const records = p->workspace;
-  if (S > 1) {
+  const bool records_only = !p->out && !p->out_record;  // the split records are the output
+  if (S > 1 || records_only) {
     a.rec = records;
   } else {
     a.out = p->out;
@@ -2168,7 +2172,7 @@ extern "C" int helm_paged_attn_decode(const helm_paged_attn_params *p, void *str
       default: rc = launch_generic<__nv_bfloat16>(a, st); break;
     }
   }
-  if (rc != HELM_OK || S == 1) return rc;
+  if (rc != HELM_OK || S == 1 || records_only) return rc;
   return launch_lse_merge(records, S, (int64_t)rows * (p->D + 2), rows, p->D, p->out, p->out_dtype, p->out_record, st);
 }
 

@@ -105,7 +105,8 @@ def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.
                            out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                            out_record: Optional[torch.Tensor] = None,
                            error_flag: Optional[torch.Tensor] = None,
-                           workspace: Optional[torch.Tensor] = None, exchange=None) -> Optional[torch.Tensor]:
+                           workspace: Optional[torch.Tensor] = None, exchange=None,
+                           records_only: bool = False) -> Optional[torch.Tensor]:
     """Single-query attention of q [B, Hq, D] over paged K/V (see helm_paged_attn_decode).
 
     ``page_table``/``page_used`` are int32 [B, max_pages] and ``num_pages``
@@ -113,6 +114,9 @@ def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.
     ``out_dtype``, default q.dtype, unless given), or None when only
     ``out_record`` is requested.  ``exchange``: a ctypes pointer to a ShardExchange (KV sequence
     sharding with the cross-GPU exchange fused into the kernel).
+    ``records_only``: write no output; return the split records [S, B*Hq, D+2]
+    (fp32, a view of the workspace) for a later merge (KVShardGroup.gather_merge merges and
+    exchanges them in one launch).  Consume them before the workspace is reused.
     """
     dev = _need_cuda("paged_decode_attention", q, k_base, v_base, page_table, page_used, num_pages)
     if not q.is_contiguous() or q.dim() != 3:
@@ -124,7 +128,9 @@ def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.
             raise ValueError(f"paged_decode_attention: {name} must have unit inner stride")
     if page_table.dim() == 2 and page_used.stride(0) != page_table.stride(0):
         raise ValueError("paged_decode_attention: page_used must share page_table's row stride")
-    if out is None and out_record is None:
+    if records_only:
+        out = out_record = None
+    elif out is None and out_record is None:
         out = torch.empty(q.shape, dtype=out_dtype or q.dtype, device=dev)
     p = make_attn_params(q, k_base, v_base, page_table, page_used, num_pages, num_kv_heads=num_kv_heads,
                          page_size=page_size, page_stride=page_stride, head_stride=head_stride,
@@ -138,11 +144,15 @@ def paged_decode_attention(q: torch.Tensor, k_base: torch.Tensor, v_base: torch.
     if need < 0:
         N.check("helm_paged_attn_workspace_bytes", N.ERR_INVALID_ARGUMENT)
     p.num_splits = S.value
+    ws = None
     if need > 0:
         ws = workspace if workspace is not None and workspace.numel() * 4 >= need else WORKSPACE.get(dev, need)
         p.workspace = ws.data_ptr()
         p.workspace_bytes = ws.numel() * ws.element_size()
     N.check("helm_paged_attn_decode", lib.helm_paged_attn_decode(ctypes.byref(p), _stream(dev)))
+    if records_only:
+        B, Hq, D = q.shape
+        return ws.view(-1)[:S.value * B * Hq * (D + 2)].view(S.value, B * Hq, D + 2)
     return out
 
 

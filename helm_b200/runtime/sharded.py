@@ -16,6 +16,10 @@ Three exchanges are provided:
   attention, and no extra launch runs;
 * "p2p": helm_gather_merge, the same exchange as a separate kernel after the
   attention (used when the attention cannot run the persistent kernel);
+* "split": the attention's split path in records-only mode (its split records
+  stay in the workspace), then helm_gather_merge merging those records and
+  exchanging them in one launch: the lower fixed cost of the split path, two
+  launches per layer;
 * "nccl": torch.distributed.all_gather_into_tensor + helm_lse_merge.
 """
 from __future__ import annotations
@@ -58,7 +62,7 @@ class KVShardGroup:
         if exchange == "nccl" or self.world == 1:
             self.gathered = torch.empty((self.world, rows, head_dim + 2), dtype=torch.float32, device=self.device)
             return
-        if exchange not in ("p2p", "fused"):
+        if exchange not in ("p2p", "fused", "split"):
             raise ValueError(f"unknown exchange {exchange!r}")
         lib = N.lib()
         # state of the separate exchange kernel (helm_gather_merge) ...
@@ -122,20 +126,34 @@ class KVShardGroup:
         """True when the attention call itself should do the exchange."""
         return self.exchange == "fused" and self.params is not None and self.world > 1
 
+    @property
+    def records_only(self) -> bool:
+        """True when the attention call should leave its split records for gather_merge to merge."""
+        return self.exchange == "split" and self.params is not None and self.world > 1
+
     def gather_merge(self, record: torch.Tensor, out: Optional[torch.Tensor] = None,
                      out_record: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
-        """Exchanges this rank's record [rows, D+2] (fp32) and writes the merged result to out
-        [rows, D] and/or out_record [rows, D+2] on every rank."""
-        if record.shape != (self.rows, self.D + 2) or record.dtype != torch.float32 or not record.is_contiguous():
-            raise ValueError("gather_merge: record must be contiguous fp32 [rows, D+2]")
+        """Exchanges this rank's record [rows, D+2] (fp32), or its S split records [S, rows, D+2]
+        (merged first, in the same launch), and writes the merged result to out [rows, D] and/or
+        out_record [rows, D+2] on every rank."""
+        parts = record.dim() == 3
+        if (record.shape[-2:] != (self.rows, self.D + 2) or record.dim() not in (2, 3)
+                or record.dtype != torch.float32 or not record.is_contiguous()):
+            raise ValueError("gather_merge: record must be contiguous fp32 [rows, D+2] or [S, rows, D+2]")
         if self.world == 1:
-            return ops.lse_merge(record.unsqueeze(0), out=out, out_record=out_record)
+            return ops.lse_merge(record if parts else record.unsqueeze(0), out=out, out_record=out_record)
         if self.params is None:
             import torch.distributed as dist
+            if parts:
+                merged = torch.empty((self.rows, self.D + 2), dtype=torch.float32, device=self.device)
+                ops.lse_merge(record, out_record=merged)
+                record = merged
             dist.all_gather_into_tensor(self.gathered, record, group=self.group)
             return ops.lse_merge(self.gathered, out=out, out_record=out_record)
         p = self.params
         p.record = record.data_ptr()
+        p.num_partials = record.shape[0] if parts else 0
+        p.partial_stride = self.rows * (self.D + 2) if parts else 0
         p.out = None if out is None else out.data_ptr()
         p.out_dtype = ops.dtype_code(out.dtype) if out is not None else N.F32
         p.out_record = None if out_record is None else out_record.data_ptr()

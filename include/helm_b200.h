@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define HELM_ABI_VERSION 3
+#define HELM_ABI_VERSION 4
 #define HELM_MAX_RANKS 8
 
 /* ---- status codes ------------------------------------------------------- */
@@ -87,7 +87,10 @@ const char *helm_last_error(void);
  * semantics) into out [B, Hq, D] of out_dtype; when `out_record` is non-null
  * the merged but unnormalised record [B*Hq][D+2] is also written, for a later
  * cross-GPU merge.  With num_splits == 1 and only `out` requested, no
- * workspace is touched.
+ * workspace is touched.  With neither `out` nor `out_record` (records-only
+ * mode, split path only, no fused exchange) the call writes its split records
+ * to the workspace and stops there; helm_lse_merge or helm_gather_merge
+ * (num_partials) merges them.
  *
  * Paths.  The split path runs a grid of (splits, kv heads, sequences) CTAs
  * and then the LSE merge; the persistent path runs one launch of two CTAs per
@@ -437,6 +440,12 @@ typedef struct {
   float *out_record;                    /* [rows, D+2] or null */
   int32_t *error_flag;
   uint64_t wait_ns;                     /* bound of each wait for peers; 0 = 2 s */
+  int32_t num_partials;                 /* 0 or 1: `record` is the merged record; > 1:
+                                           `record` holds num_partials split records
+                                           (helm_paged_attn_decode's workspace in records-
+                                           only mode), partial_stride floats apart, merged
+                                           here before the exchange (D <= 256) */
+  int64_t partial_stride;
 } helm_gather_merge_params;
 
 int64_t helm_gather_merge_state_bytes(int32_t world, int32_t rows, int32_t D, int64_t *recv_bytes_out,

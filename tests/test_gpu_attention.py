@@ -372,3 +372,52 @@ def test_persistent_out_record_merges_across_calls(cuda):
             recs.append(rec)
         merged = ops.lse_merge(torch.stack(recs).contiguous(), out=torch.empty(B * Hkv * gq, D, device=cuda))
         assert float((merged.reshape(B, -1, D) - full).abs().max()) < 1e-5, splits
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_records_only_and_gather_merge_of_split_records(dtype, cuda):
+    """Records-only mode leaves the split records in the workspace; helm_lse_merge of them, and
+    helm_gather_merge given them as partials (world 1: the merge + push + wait + merge path on
+    one GPU), equal the normal call."""
+    import ctypes
+    from helm_b200 import _native as N
+    from helm_b200 import ops
+    torch.manual_seed(31)
+    Hkv, D, P, gq, B = 4, 128, 64, 8, 3
+    Hq = Hkv * gq
+    kp = torch.randn(120, Hkv, P, D, device=cuda).to(dtype)
+    vp = torch.randn(120, Hkv, P, D, device=cuda).to(dtype)
+    q = torch.randn(B, Hq, D, device=cuda).to(dtype)
+    pt = torch.randperm(120, device=cuda).to(torch.int32)[:B * 40].reshape(B, 40).contiguous()
+    pu = torch.full((B, 40), P, dtype=torch.int32, device=cuda)
+    pu[:, 39] = 11
+    npg = torch.tensor([40, 7, 23], dtype=torch.int32, device=cuda)
+    common = dict(num_kv_heads=Hkv, page_size=P, page_stride=Hkv * P * D, head_stride=P * D, num_pool_pages=120)
+    full = ops.paged_decode_attention(q, kp, vp, pt, pu, npg, out_dtype=torch.float32, **common)
+    ws = torch.empty(1 << 21, device=cuda)
+    parts = ops.paged_decode_attention(q, kp, vp, pt, pu, npg, records_only=True, workspace=ws, **common)
+    rows = B * Hq
+    assert parts.shape[1:] == (rows, D + 2) and parts.shape[0] >= 1
+    merged = ops.lse_merge(parts.contiguous(), out=torch.empty(rows, D, device=cuda))
+    assert float((merged.reshape(B, Hq, D) - full).abs().max()) < 1e-5
+    lib = N.lib()
+    rb, fb, cb = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    assert lib.helm_gather_merge_state_bytes(1, rows, D, ctypes.byref(rb), ctypes.byref(fb), ctypes.byref(cb)) > 0
+    st = torch.zeros(rb.value + fb.value, dtype=torch.uint8, device=cuda)
+    cnt = torch.zeros(max(cb.value, 4), dtype=torch.uint8, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for call in range(2):
+        out = torch.full((rows, D), 7.0, device=cuda)
+        p = N.GatherMergeParams()
+        p.rank, p.world, p.rows, p.D = 0, 1, rows, D
+        p.record = parts.data_ptr()
+        p.num_partials, p.partial_stride = parts.shape[0], rows * (D + 2)
+        p.peer_recv[0], p.peer_flags[0] = st.data_ptr(), st.data_ptr() + rb.value
+        p.recv_local, p.flags_local = st.data_ptr(), st.data_ptr() + rb.value
+        p.counters = cnt.data_ptr()
+        p.out, p.out_dtype, p.error_flag = out.data_ptr(), N.F32, err.data_ptr()
+        p.wait_ns = 100_000_000
+        N.check("helm_gather_merge", lib.helm_gather_merge(ctypes.byref(p), torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert float((out.reshape(B, Hq, D) - full).abs().max()) < 1e-5, call

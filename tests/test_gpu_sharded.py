@@ -69,6 +69,12 @@ def _worker(rank, world, port, exchange, result_q):
                 out = ops.paged_decode_attention(q, kp, vp, lpt.to(dev), lpu.to(dev), lnp.to(dev),
                                                  out_dtype=torch.float32, exchange=group.xparams_ptr,
                                                  error_flag=group.error_flag, **common)
+            elif exchange == "split":
+                ws = torch.empty(1 << 20, device=dev)
+                parts = ops.paged_decode_attention(q, kp, vp, lpt.to(dev), lpu.to(dev), lnp.to(dev),
+                                                   records_only=True, workspace=ws, **common)
+                out = torch.empty(rows, D, device=dev, dtype=torch.float32)
+                group.gather_merge(parts, out=out)
             else:
                 rec = torch.empty(rows, D + 2, device=dev)
                 ops.paged_decode_attention(q, kp, vp, lpt.to(dev), lpu.to(dev), lnp.to(dev), out_record=rec,
@@ -91,7 +97,7 @@ def _worker(rank, world, port, exchange, result_q):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("exchange", ["fused", "p2p", "nccl"])
+@pytest.mark.parametrize("exchange", ["fused", "split", "p2p", "nccl"])
 def test_sharded_exchange_matches_single_gpu(exchange, world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
