@@ -947,12 +947,13 @@ def kernel_cases(dev):
         es = torch.empty((), dtype=dtype).element_size()
         return 2 * B * Hkv * ctx * D * es + 2 * B * Hq * D * es, setup
 
-    b, s = attn_case(4, 64, 8, 128, 64, 16384, bf, 0, 1)
+    b, s = attn_case(4, 64, 8, 128, 64, 16384, bf, -1, 1)
     cases.append(("attn_persistent", "attn_tc_persistent_kernel", "hbm", b, s,
-                  "bf16, B 4, 64q/8kv, d128, 16384 tokens (256 pages) per sequence: one config-5 layer at N=8"))
-    b, s = attn_case(4, 64, 8, 128, 64, 16384, bf, 8, 1)
-    cases.append(("attn_split", "attn_tc_kernel + lse_merge_kernel", "hbm", b, s,
-                  "the same call on the split path, 8 splits per sequence"))
+                  "bf16, B 4, 64q/8kv, d128, 16384 tokens (256 pages) per sequence: one config-5 layer at N=8; "
+                  "num_splits=-1"))
+    b, s = attn_case(4, 64, 8, 128, 64, 16384, bf, 0, 1)
+    cases.append(("attn_split", "attn_tc_kernel + lse_merge_wide_kernel", "hbm", b, s,
+                  "the same call on the automatic plan (split path, 9 splits per sequence)"))
     b, s = attn_case(4, 32, 8, 128, 64, 16384, torch.float32, 0, 2)
     cases.append(("attn_warp_fp32", "attn_warp_kernel + lse_merge_kernel", "hbm", b, s,
                   "fp32 pages (config-1 heads), B 4, 32q/8kv, d128, 16384 tokens per sequence"))
