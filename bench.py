@@ -89,10 +89,10 @@ def parse():
 # byte, and the record/output writes of a batch-4, 64-head call.
 ATTN_READ_PER_ALG_BYTE = 269.749504 / 268.664832
 ATTN_WRITE_BYTES = 5.910784e6
-# The same for the split path (attention + merge launches of one call), from
-# profiles/attn_tc_kernel_config5.md; None until captured.
-ATTN_SPLIT_READ_PER_ALG_BYTE = None
-ATTN_SPLIT_WRITE_BYTES = None
+# The same for the split path (attention + merge launches of one call, 9 splits), from
+# profiles/attn_tc_kernel_config5.md.
+ATTN_SPLIT_READ_PER_ALG_BYTE = 269.597696 / 268.566528
+ATTN_SPLIT_WRITE_BYTES = 1.132e6 + 1.212e6     # records written by the attention + read back by the merge
 
 
 def peaks():
