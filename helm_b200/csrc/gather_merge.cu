@@ -74,6 +74,10 @@ __global__ void __launch_bounds__(kThreads) gather_merge_kernel(GatherArgs a) {
   const int nrows = min(kRowsPerBlock, a.rows - row0);
   const int rl = a.D + 2;
   const int G = a.world;
+  // Launched with programmatic dependent launch: the CTAs may be resident before the attention
+  // that writes `record` has finished; everything below runs after it has.
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) {
     s_sent = a.sent[rb];
     s_ok = 1;
@@ -94,6 +98,7 @@ __global__ void __launch_bounds__(kThreads) gather_merge_kernel(GatherArgs a) {
       float L = 0.f, O[kMaxD / 32];
 #pragma unroll
       for (int k = 0; k < kMaxD / 32; ++k) O[k] = 0.f;
+#pragma unroll 4
       for (int sp = 0; sp < a.S; ++sp) {
         const float *pp = base + sp * a.pstride;
         const float w = rescale_weight(pp[a.D], M);
@@ -257,7 +262,8 @@ extern "C" int helm_gather_merge(const helm_gather_merge_params *p, void *stream
   a.wait_ns = p->wait_ns ? p->wait_ns : kWaitNs;
   a.S = p->num_partials;
   a.pstride = p->partial_stride;
-  gather_merge_kernel<<<a.nblocks, kThreads, 0, as_stream(stream)>>>(a);
+  const cudaError_t e = launch_pdl(gather_merge_kernel, dim3(a.nblocks), dim3(kThreads), 0, as_stream(stream), a);
+  if (e != cudaSuccess) return fail(HELM_ERR_CUDA, "gather_merge: launch: %s", cudaGetErrorString(e));
   return check_launch("gather_merge_kernel");
 }
 
