@@ -5,20 +5,23 @@ Default workload (the metric's long-context decode): a Qwen3-
 attention stack -- 64 layers, 64 query / 8 KV heads, head_dim 128, bf16, batch 4, 131072 cached
 tokens per sequence in 64-token pages, KV sharded by sequence over the N GPUs (one process per
 GPU).  One step = one decode step of the stack: for every layer, append the new token's K/V (on
-the rank holding the sequence tail, device-directed) and run the persistent paged-attention
-kernel over the rank's shard; for N > 1 the kernel itself exchanges the per-head (m, l, o)
-records with the other ranks over NVLink and merges them.  Synthetic data (seeded normal K/V
+the rank holding the sequence tail, device-directed) and run the paged attention over the rank's
+shard -- at N = 1 the automatic plan (the split kernel with about one resident wave of CTAs, then
+the LSE merge); for N > 1 the persistent kernel, which itself exchanges the per-head (m, l, o)
+records with the other ranks over NVLink and merges them (`--exchange split` runs the split
+kernel and a separate merge-and-exchange launch instead).  Synthetic data (seeded normal K/V
 through KVCacheManager.append_prefill); the KV working set (137 GB / N) is far larger than L2, so
 no flush is needed.  The step is captured in a CUDA graph; `e2e` reruns it through the runtime's
 _decode_batched with pinned-host inputs and outputs.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl helm|reference]
-                  [--workload config5|config1|config2|config3|config4]
+                  [--workload config5|config1|config2|config3|config4|prefill|kernels]
 
 Other workloads (single JSON line each): config1 -- the reference's mixed-residency fp32 case
 through perform_streaming_attention; config2 -- the INT8 GEMV shapes; config3 -- a Qwen3-8B-shaped
 decode step through KVOffloadManager (CUDA graph); config4 -- a Qwen3-14B-shaped INT8 decode step
-with half of the KV in pinned host memory.
+with half of the KV in pinned host memory; prefill -- the config-2 weights at M = 4096 through the
+tcgen05 INT8 GEMM; kernels -- every kernel family once, with its achieved GB/s or TFLOP/s.
 
 Rank 0 prints one JSON line.  `--impl reference` times the reference's own CPU algorithm on the
 host cores instead (oracle/cpu_baseline.py; the compiled reference GEMV for config2).
