@@ -524,8 +524,10 @@ int launch_m(const void *x, int xdt, const int8_t *w, const void *scale, int sdt
     return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
   } else {
     // One row tile per CTA over a long K: eight consumer warps, 1024-k stages (half the stage
-    // round trips of a 512-k ring for the same bytes in flight).
-    if (tiles <= 3 * sms && K >= 8192)
+    // round trips of a 512-k ring for the same bytes in flight).  Measured: +27 % on
+    // (4096, 12288); at K = 4096 it pays only for a single row of x (6144 x 4096: 7.7 -> 6.5 us
+    // at M = 1, no change at M = 4 or 8).
+    if (tiles <= 3 * sms && (K >= 8192 || (M == 1 && K >= 4096)))
       return launch_cfg<XT, 1, MT, 8>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
     if (tiles <= 3 * sms) return launch_cfg<XT, 1, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
     if (tiles <= 2 * 2 * sms) return launch_cfg<XT, 2, MT>(x, xdt, w, scale, sdt, bias, y, M, N, K, st, 0, wpk);
