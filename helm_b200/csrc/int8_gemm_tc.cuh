@@ -9,26 +9,29 @@
 //
 // The weight is the A operand and lives in tensor memory; x is the B operand in shared memory:
 //   D[n, m] (128 channels x 256 tokens, fp32, tensor memory) += W[n, k] . x[m, k]
-// CTA tile 128 output channels x 256 tokens; k in steps of 64.  Each converted weight element feeds
+// CTA tile 128 output channels x 256 tokens; k in steps of 128 (one packed block column, eight
+// MMAs of K = 16 per step, which halves the per-step barrier round trips of 64-k steps).  Each
+// converted weight element feeds
 // 256 tokens, and the converted weights go from registers to tensor memory (tcgen05.st) instead of
 // through shared memory, which leaves shared memory to the x tiles and the int8 blocks.
-//   x   (256 tokens x 64 k, 32 KB, 4 deep)   shared memory, filled by TMA (128-byte swizzle), released
-//                                            by the MMAs (tcgen05.commit);
-//   W   (packed int8 block column: 128 channels x 128 k, 16 KB, 3 deep)  shared memory, filled by bulk
+//   x   (256 tokens x 128 k as two 64-k boxes, 64 KB, 3 deep)  shared memory, filled by TMA (128-byte
+//                                            swizzle), released by the MMAs (tcgen05.commit);
+//   W   (packed int8 block column: 128 channels x 128 k, 16 KB, 2 deep)  shared memory, filled by bulk
 //                                            copies, released by the converters;
-//   A   (converted 16-bit weights: 128 lanes x 32 columns per k step, 4 deep)  tensor memory, written
+//   A   (converted 16-bit weights: 128 lanes x 64 columns per k step, 2 deep)  tensor memory, written
 //                                            by the converters, released by the MMAs.
 // Warp roles (576 threads):
 //   warp 0      producer: TMA for x, bulk copies for the packed weight blocks;
 //   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 with A in tensor memory (M=128
 //               channels, N=256 tokens, K=16; B = x, K-major 128-byte-swizzled descriptor; D in
-//               tensor memory) four times per k step, then tcgen05.commit to the x and A empty
+//               tensor memory) eight times per k step, then tcgen05.commit to the x and A empty
 //               barriers;
 //   warps 2-17  converters, then the epilogue.  Warp w may address the tensor-memory lanes
-//               32*(w%4)..+31, so thread (w, l) owns channel row 32*(w%4) + l.  The warps form four
-//               groups of four (one warp per lane quadrant); group g converts the k steps j with
-//               j % 4 == g into A stage g, so a conversion has four k steps of MMA time to finish.
-//               A row's 64 int8 values of a step (four 16-byte chunks of its packed block row)
+//               32*(w%4)..+31, so thread (w, l) owns channel row 32*(w%4) + l.  The warps form two
+//               groups of eight (two per lane quadrant, one per half of the 128 k); group g converts
+//               the k steps j with j % 2 == g from W stage g into A stage g, so a conversion has
+//               two k steps of MMA time to finish and no barrier is waited on two phases ahead.
+//               A row's 64 int8 values of a half step (four 16-byte chunks of its packed block row)
 //               become 32 words of exact 16-bit pairs, stored with tcgen05.st into the stage's
 //               columns (column c holds k = 2c, 2c+1).  After the last k step the same threads read
 //               their channel's accumulators (tcgen05.ld, 32 tokens at a time, 64 tokens a warp),
@@ -43,16 +46,19 @@
 namespace helm {
 namespace {
 
-constexpr int GCH = 128, GTK = 256, GK = 64;     // CTA tile: channels x tokens; k step
-constexpr int kXStages = 4, kWStages = 3, kAStages = 4;
-constexpr int kXStageBytes = GTK * GK * 2;       // 32 KB: 256 token rows x 128 B
+constexpr int GCH = 128, GTK = 256, GK = 128;    // CTA tile: channels x tokens; k step (one block column)
+// kWStages == kAStages == the number of converter groups: group g converts the k steps j with
+// j % 2 == g from W stage g into A stage g, so no barrier is ever waited on two phases ahead.
+constexpr int kXStages = 3, kWStages = 2, kAStages = 2;
+constexpr int kXBoxBytes = GTK * 64 * 2;         // 32 KB: one 64-k TMA box of 256 token rows x 128 B
+constexpr int kXStageBytes = 2 * kXBoxBytes;     // 64 KB: the k step's two boxes
 constexpr int kWStageBytes = GCH * 128;          // 16 KB: 8 packed blocks (16 rows x 128 k)
 constexpr int kGSmem = kXStages * kXStageBytes + kWStages * kWStageBytes + 1024;
 constexpr int kConvWarps = 16;                  // four groups of four (one per tensor-memory lane quadrant)
-constexpr int kGroupWarps = 4;
+constexpr int kGroupWarps = 8;                  // two per lane quadrant, one per half of the 128 k
 constexpr int kGThreads = (2 + kConvWarps) * 32;
 constexpr int kTmemCols = 512;
-constexpr int kAccCol = 0, kACol0 = 256, kAStageCols = GK / 2;   // 32 columns of 16-bit pairs per k step
+constexpr int kAccCol = 0, kACol0 = 256, kAStageCols = GK / 2;   // 64 columns of 16-bit pairs per k step
 
 __device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr) {
   // K-major, 128-byte swizzle: leading byte offset 1 (16 B, unused for this layout), stride byte
@@ -166,7 +172,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     }
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&w_full[s], 1);
-      mbar_init(&w_empty[s], 2 * kGroupWarps);   // the two k steps of a column, four warps each
+      mbar_init(&w_empty[s], kGroupWarps);       // the eight warps of the group converting it
     }
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(&a_full[s], kGroupWarps);
@@ -199,32 +205,34 @@ __global__ void __launch_bounds__(kGThreads, 1)
     if (lane == 0) {
       int x_issued = 0, w_issued = 0;
       for (int j = 0; j < NK && !*reinterpret_cast<volatile int *>(&failed); ++j) {
-        if ((j & 1) == 0) {                       // the packed block column of k steps j, j + 1
-          const int c = j >> 1, ws = c % kWStages;
-          if (c >= kWStages && !mbar_wait(&w_empty[ws], (uint32_t)((c / kWStages - 1) & 1))) {
-            give_up();
-            break;
-          }
-          mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(tiles * 2048));
-          for (int t = 0; t < tiles; ++t)
-            bulk_g2s(w_ring + ws * kWStageBytes + t * 2048, wpk + ((int64_t)(n0 / 16 + t) * KB + c) * 2048, 2048,
-                     &w_full[ws]);
-          w_issued = c + 1;
+        const int ws = j % kWStages;             // the packed block column of k step j
+        if (j >= kWStages && !mbar_wait(&w_empty[ws], (uint32_t)((j / kWStages - 1) & 1))) {
+          give_up();
+          break;
         }
+        mbar_arrive_expect_tx(&w_full[ws], (uint32_t)(tiles * 2048));
+        for (int t = 0; t < tiles; ++t)
+          bulk_g2s(w_ring + ws * kWStageBytes + t * 2048, wpk + ((int64_t)(n0 / 16 + t) * KB + j) * 2048, 2048,
+                   &w_full[ws]);
+        w_issued = j + 1;
         const int xs = j % kXStages;
         if (j >= kXStages && !mbar_wait(&x_empty[xs], (uint32_t)((j / kXStages - 1) & 1))) {
           give_up();
           break;
         }
-        mbar_arrive_expect_tx(&x_full[xs], (uint32_t)kXStageBytes);
+        // the second 64-k box only where it starts inside K (a box wholly past the edge is not
+        // loaded; the MMAs of the last step stop at K)
+        const bool two = j * GK + 64 < K;
+        mbar_arrive_expect_tx(&x_full[xs], (uint32_t)(two ? kXStageBytes : kXBoxBytes));
         tma_load_2d(x_ring + xs * kXStageBytes, &tmX, &x_full[xs], j * GK, m0);
+        if (two) tma_load_2d(x_ring + xs * kXStageBytes + kXBoxBytes, &tmX, &x_full[xs], j * GK + 64, m0);
         x_issued = j + 1;
       }
       // the copies still in flight land before this CTA can finish
       for (int j = max(0, x_issued - kXStages); j < x_issued; ++j)
         if (!mbar_wait(&x_full[j % kXStages], (uint32_t)((j / kXStages) & 1))) give_up();
       for (int c = max(0, w_issued - kWStages); c < w_issued; ++c)
-        if (!mbar_wait(&w_full[c % kWStages], (uint32_t)((c / kWStages) & 1))) give_up();
+        if (!mbar_wait(&w_full[c % kWStages], (uint32_t)((c / kWStages) & 1))) give_up();  // c: k step
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -240,9 +248,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t b0 = smem_u32(x_ring + xs * kXStageBytes);
         const uint32_t a0 = tmem + (uint32_t)(kACol0 + as * kAStageCols);
+        const int nkk = min(GK / 16, (K - j * GK) / 16);   // K is a multiple of 16
 #pragma unroll
-        for (int kk = 0; kk < GK / 16; ++kk)
-          umma_f16_ts(tmem + kAccCol, a0 + kk * 8, umma_smem_desc(b0 + kk * 32), idesc, (j | kk) != 0);
+        for (int kk = 0; kk < GK / 16; ++kk)       // k 16*kk: box kk/4, 32-byte column (kk%4) of its rows
+          if (kk < nkk)
+            umma_f16_ts(tmem + kAccCol, a0 + kk * 8, umma_smem_desc(b0 + (kk >> 2) * kXBoxBytes + (kk & 3) * 32),
+                        idesc, (j | kk) != 0);
         umma_commit(&x_empty[xs]);
         umma_commit(&a_empty[as]);
       }
@@ -253,13 +264,14 @@ __global__ void __launch_bounds__(kGThreads, 1)
     // Group g (warps 2+4g .. 5+4g, one per lane quadrant) converts k steps g, g+4, g+8, ... into
     // A stage g, so each group has four k steps of MMA time for one conversion.
     const int quad = warp & 3;                 // the tensor-memory lanes this warp may address
-    const int grp = (warp - 2) >> 2;           // k steps j with j % 4 == grp; A stage grp
+    const int grp = (warp - 2) >> 3;           // k steps j with j % 2 == grp; W and A stage grp
+    const int half = ((warp - 2) >> 2) & 1;    // which 64 k of the step
     const int r = quad * 32 + lane;            // channel row of the tile
     const uint32_t lane_addr = (uint32_t)(quad * 32) << 16;
-    const uint32_t a_addr = tmem + lane_addr + (uint32_t)(kACol0 + grp * kAStageCols);
+    const uint32_t a_addr = tmem + lane_addr + (uint32_t)(kACol0 + grp * kAStageCols + half * 32);
     for (int j = grp; j < NK; j += kAStages) {
-      const int c = j >> 1, ws = c % kWStages, js = j & 1;
-      if (!mbar_wait(&w_full[ws], (uint32_t)((c / kWStages) & 1)) ||
+      const int ws = j % kWStages;
+      if (!mbar_wait(&w_full[ws], (uint32_t)((j / kWStages) & 1)) ||
           (j >= kAStages && !mbar_wait(&a_empty[grp], (uint32_t)((j / kAStages - 1) & 1)))) {
         give_up();
         break;
@@ -268,8 +280,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const uint8_t *row = w_ring + ws * kWStageBytes + (r >> 4) * 2048 + (r & 15) * 128;
       uint4 v[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)             // logical 16-value chunks 4*js .. 4*js + 3 of the row
-        v[i] = *reinterpret_cast<const uint4 *>(row + (((4 * js + i) ^ (r & 7)) << 4));
+      for (int i = 0; i < 4; ++i)             // logical 16-value chunk 4*half + i of the row (its swizzled slot)
+        v[i] = *reinterpret_cast<const uint4 *>(row + (((4 * half + i) ^ (r & 7)) << 4));
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint4 q0, q1, q2, q3;
@@ -297,8 +309,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
       const float bi = (bias && n < N) ? Elem<XT>::to_f(bias[n]) : 0.f;
       const bool store = n < N && !*reinterpret_cast<volatile int *>(&failed);
       constexpr int kCols = GTK / (kConvWarps / 4);   // token columns per warp
+      const int slot = grp * 2 + half;                // the quadrant's four warps split the 256 tokens
 #pragma unroll 1
-      for (int c0 = grp * kCols; c0 < grp * kCols + kCols; c0 += 32) {
+      for (int c0 = slot * kCols; c0 < slot * kCols + kCols; c0 += 32) {
         float acc[32];
         tmem_ld32(tmem + lane_addr + (uint32_t)(kAccCol + c0), acc);
         if (!store) continue;
