@@ -95,7 +95,9 @@ ATTN_WRITE_BYTES = 5.910784e6
 # The same for the split path (attention + merge launches of one call, 9 splits), from
 # profiles/attn_tc_kernel_config5.md.
 ATTN_SPLIT_READ_PER_ALG_BYTE = 269.597696 / 268.566528
-ATTN_SPLIT_WRITE_BYTES = 1.132e6 + 1.212e6     # records written by the attention + read back by the merge
+# records written by the attention and read back by the merge, per split and record row (D + 2
+# floats): 1.132 MB written + 1.212 MB read for 9 splits x 256 rows in that capture
+ATTN_SPLIT_RECORD_BYTES = (1.132e6 + 1.212e6) / (9 * 256 * 130)
 
 
 def peaks():
@@ -486,8 +488,9 @@ def run_helm(args, rank, local, world):
             "hbm_gbs": step_bytes_all / (ms_step * 1e-3) / 1e9 / world,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak,
-                         "traffic": (ATTN_SPLIT_READ_PER_ALG_BYTE * bytes_launch + ATTN_SPLIT_WRITE_BYTES
-                                     if (world == 1 and st.splits > 0 and ATTN_SPLIT_READ_PER_ALG_BYTE) else
+                         "traffic": (ATTN_SPLIT_READ_PER_ALG_BYTE * bytes_launch + ATTN_SPLIT_RECORD_BYTES *
+                                     st.splits * st.B * st.Hq * (st.D + 2)
+                                     if (world == 1 and st.splits > 0) else
                                      ATTN_READ_PER_ALG_BYTE * bytes_launch + ATTN_WRITE_BYTES
                                      if (world == 1 and st.splits < 0) else None),
                          "traffic_source": ("ncu dram__bytes_read/write.sum of the attention + merge launches of a "
