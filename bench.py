@@ -959,7 +959,7 @@ def kernel_cases(dev):
                   "num_splits=-1"))
     b, s = attn_case(4, 64, 8, 128, 64, 16384, bf, 0, 1)
     cases.append(("attn_split", "attn_tc_kernel + lse_merge_wide_kernel", "hbm", b, s,
-                  "the same call on the automatic plan (split path, 9 splits per sequence)"))
+                  "the same call on the automatic plan (split path, 8 splits per sequence)"))
     b, s = attn_case(4, 32, 8, 128, 64, 16384, torch.float32, 0, 2)
     cases.append(("attn_warp_fp32", "attn_warp_kernel + lse_merge_kernel", "hbm", b, s,
                   "fp32 pages (config-1 heads), B 4, 32q/8kv, d128, 16384 tokens per sequence"))
