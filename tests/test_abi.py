@@ -152,3 +152,35 @@ def test_packed_layout_sizes_and_unpack_on_cpu():
     assert torch.equal(pk.unpack(), torch.from_numpy(w))
     assert torch.equal(ops.int8_pack_weight(torch.from_numpy(w)).data, torch.from_numpy(packed))
     assert torch.equal(pk.rows(16, 37).unpack(), torch.from_numpy(w[16:]))
+
+
+def _plan(B, Hq, Hkv, pages, splits):
+    """(resolved split count, workspace bytes) of helm_paged_attn_workspace_bytes for a bf16 P=64
+    D=128 call; host-side planning only (the pointers are never dereferenced)."""
+    p = N.PagedAttnParams()
+    fake = 1 << 20                                    # 16-byte-aligned stand-in addresses
+    p.q, p.k_base, p.v_base, p.out = fake, fake, fake, fake
+    p.page_table, p.page_used, p.num_pages = fake, fake, fake
+    p.page_stride, p.head_stride = 2 * Hkv * 64 * 128, 64 * 128
+    p.num_pool_pages, p.page_table_stride, p.max_pages = B * pages, pages, pages
+    p.B, p.Hq, p.Hkv, p.D, p.P = B, Hq, Hkv, 128, 64
+    p.q_dtype = p.kv_dtype = p.out_dtype = N.BF16
+    p.num_splits = splits
+    S = ctypes.c_int32(0)
+    need = N.lib().helm_paged_attn_workspace_bytes(ctypes.byref(p), ctypes.byref(S))
+    return S.value, need
+
+
+def test_attention_plan_on_the_host():
+    """The automatic plan: k splits per (sequence, kv head) pair, k the largest power of two with
+    k * pairs <= 2 * SMs, doubled when every split keeps >= 64 pages; -1 asks for the persistent
+    kernel, whose CTA count is a power-of-two multiple of the pairs.  Without a GPU the library
+    plans for 148 SMs."""
+    rec = lambda S, rows: S * rows * (128 + 2) * 4
+    assert _plan(4, 64, 8, 2048, 0) == (16, rec(16, 256))     # config 5: 32 pairs, 2048 pages
+    assert _plan(4, 64, 8, 256, 0) == (8, rec(8, 256))        # the N = 8 shard of it
+    assert _plan(1, 32, 8, 256, 0) == (32, rec(32, 32))       # batch 1 (config 3's layer)
+    assert _plan(4, 64, 8, 2048, 5) == (5, rec(5, 256))       # explicit split count
+    S, need = _plan(4, 64, 8, 256, -1)                         # persistent: 8 CTAs per pair = 256
+    slots, gq = 256 + 32, 8
+    assert S == -1 and need == slots * gq * 128 * 4 + slots * gq * 2 * 4 + 32 * 8
