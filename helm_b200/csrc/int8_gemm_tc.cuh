@@ -271,33 +271,42 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const uint32_t a_addr = tmem + lane_addr + (uint32_t)(kACol0 + grp * kAStageCols + half * 32);
     for (int j = grp; j < NK; j += kAStages) {
       const int ws = j % kWStages;
-      if (!mbar_wait(&w_full[ws], (uint32_t)((j / kWStages) & 1)) ||
-          (j >= kAStages && !mbar_wait(&a_empty[grp], (uint32_t)((j / kAStages - 1) & 1)))) {
+      // Read and convert the int8 block column as soon as it lands, release the W stage, and only
+      // then wait for the MMAs to free A stage grp: the conversion overlaps the running MMAs, and
+      // only the tensor-memory stores sit between an A stage's release and its refill.
+      if (!mbar_wait(&w_full[ws], (uint32_t)((j / kWStages) & 1))) {
         give_up();
         break;
       }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint8_t *row = w_ring + ws * kWStageBytes + (r >> 4) * 2048 + (r & 15) * 128;
       uint4 v[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)             // logical 16-value chunk 4*half + i of the row (its swizzled slot)
         v[i] = *reinterpret_cast<const uint4 *>(row + (((4 * half + i) ^ (r & 7)) << 4));
+      uint32_t w[2][16];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint4 q0, q1, q2, q3;
         cvt16<XT>(v[2 * h], q0, q1);
         cvt16<XT>(v[2 * h + 1], q2, q3);
-        const uint32_t w[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
+        const uint32_t t[16] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w,
                                 q2.x, q2.y, q2.z, q2.w, q3.x, q3.y, q3.z, q3.w};
-        tmem_st16(a_addr + (uint32_t)(h * 16), w);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w[h][e] = t[e];
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&w_empty[ws]);   // the warp's reads of the stage are done
+      if (j >= kAStages && !mbar_wait(&a_empty[grp], (uint32_t)((j / kAStages - 1) & 1))) {
+        give_up();
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      tmem_st16(a_addr, w[0]);
+      tmem_st16(a_addr + 16u, w[1]);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[grp]);
-        mbar_arrive(&w_empty[ws]);
-      }
+      if (lane == 0) mbar_arrive(&a_full[grp]);
     }
     // ---------------- epilogue ----------------
     if (!mbar_wait(&acc_bar, 0u)) {
